@@ -1,0 +1,409 @@
+"""Benchmark of qwen3x's packed-weight matrix path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (the metric's "Q8_0 GEMV HBM GB/s"):
+y = W x with W 12288x4096 Q8_0 (w ~ N(0, 0.02), d = max|w|/127), x ~ N(0, 1)
+FP32, y FP32.  One step = one GEMV of x against each of COPIES resident copies
+of W (COPIES x 53.5 MB > the 126 MB L2, so every step streams W from HBM).
+Steps are replayed from a CUDA graph; the timed region is bracketed by a
+barrier and a device synchronize, timed with CUDA events, max over ranks.
+
+value       algorithmic bytes of all ranks / max device time (GB/s), W resident
+e2e         the same metric through q3xk_try_mv_host (x from pinned host memory,
+            y back to pinned host memory, synchronous, inside the timed region)
+roofline    the GEMV kernel against the measured HBM copy bandwidth
+cpu_baseline the reference's own arch/cpu.cpp mv (oracle/_ref), 1 thread as
+            the reference runs on Linux, a bounded sample of the same workload
+--impl reference   the reference CPU implementation with all host threads.
+
+N > 1: every rank runs its own full copy of the workload (rows shard with no
+data-path collective), so scaling is "weak".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, COLS = 12288, 4096
+COPIES = 6
+GRAPH_STEPS = 50
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes(mtype: int, rows: int = ROWS, cols: int = COLS) -> int:
+    """Packed weight bytes + x + y (53,542,912 for Q8_0)."""
+    per_row = cols // 32 * (34 if mtype == 1 else 18)
+    return rows * per_row + 4 * cols + 4 * rows
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / f"{name}.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        import torch
+
+        try:  # nvidia-smi ignores CUDA_VISIBLE_DEVICES: address the GPU by UUID
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.index = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            self.index = str(device_index)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)  # first sample before the timed region starts
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").strip().splitlines():
+            f = [s.strip() for s in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def dist_setup(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def make_matrix(mtype: int, device):
+    from qwen3x_b200 import quant
+    from qwen3x_b200.linear import Linear
+
+    w = quant.gaussian((ROWS, COLS), 1, 0.02)
+    packed = quant.quantize(w, mtype)
+    return [Linear.from_packed(packed, mtype, ROWS, COLS, device=device) for _ in range(COPIES)], packed
+
+
+def time_gemv(mtype: int, steps: int, warmup: int, device, world: int, sample_clocks: bool):
+    """Graph-replayed GEMV steps; returns (seconds_max_over_ranks, launches, clocks)."""
+    import torch
+    import torch.distributed as dist
+
+    from qwen3x_b200 import capi, quant
+    from qwen3x_b200.linear import mv
+
+    mats, _ = make_matrix(mtype, device)
+    x = torch.from_numpy(quant.gaussian(COLS, 2)).to(device)
+    ys = [torch.empty(ROWS, device=device) for _ in range(COPIES)]
+
+    def step():
+        for m, y in zip(mats, ys):
+            mv(m, x, y)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    g_steps = min(GRAPH_STEPS, steps)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    lib = capi.lib()
+    with torch.cuda.stream(s):
+        lib.q3xk_reset_launch_count()
+        with torch.cuda.graph(graph, stream=s):
+            for _ in range(g_steps):
+                step()
+        per_graph = lib.q3xk_launch_count()
+    torch.cuda.current_stream().wait_stream(s)
+    replays, rem = divmod(steps, g_steps)
+    graph.replay()  # warm the graph
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(torch.cuda.current_device()) if sample_clocks else None
+    if sampler:
+        sampler.__enter__()
+    lib.q3xk_reset_launch_count()
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    for _ in range(rem):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    eager_launches = lib.q3xk_launch_count()
+    if sampler:
+        sampler.__exit__(None, None, None)
+    if world > 1:
+        dist.barrier()
+    secs = start.elapsed_time(end) / 1e3
+    if world > 1:
+        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    launches = replays * per_graph + eager_launches
+    del graph
+    return secs, launches, (sampler.summary() if sampler else None)
+
+
+def time_e2e(mtype: int, steps: int, warmup: int, device, world: int):
+    """Steps through q3xk_try_mv_host: H2D x, GEMV, D2H y, synchronous."""
+    import torch
+    import torch.distributed as dist
+
+    from qwen3x_b200 import quant
+    from qwen3x_b200.linear import try_mv
+
+    mats, _ = make_matrix(mtype, device)
+    xh = torch.from_numpy(quant.gaussian(COLS, 2)).pin_memory()
+    yh = torch.empty(ROWS, dtype=torch.float32).pin_memory()
+    ws = torch.empty(COLS + ROWS, dtype=torch.float32, device=device)
+    for _ in range(max(warmup, 3)):
+        for m in mats:
+            try_mv(m, xh, yh, ws)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        for m in mats:
+            try_mv(m, xh, yh, ws)
+    end.record()
+    torch.cuda.synchronize()
+    secs = start.elapsed_time(end) / 1e3
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    return secs, {"h2d_bytes_per_step": COPIES * COLS * 4, "d2h_bytes_per_step": COPIES * ROWS * 4}
+
+
+def cpu_reference_gbs(mtype: int, threads: int, budget_s: float, rows_cap=None):
+    """The reference's arch/cpu.cpp mv (oracle/_ref) on host cores: GB/s over a
+    bounded sample (whole 12288x4096 matvecs until `budget_s` elapses, or a
+    row-sample of one when even one call would take longer)."""
+    import numpy as np
+
+    import oracle
+    from qwen3x_b200 import quant
+
+    ref = oracle.reference()
+    kind = "reference"
+    if ref is None:
+        kind = "port"
+    w = quant.gaussian((ROWS, COLS), 1, 0.02)
+    packed = quant.quantize(w, mtype)
+    x = quant.gaussian(COLS, 2)
+    rows = ROWS if rows_cap is None else min(ROWS, rows_cap)
+    sample = packed[:rows]
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        oracle.mv(sample, mtype, rows, COLS, x, threads=threads,
+                  impl="reference" if kind == "reference" else "port")
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    gbs = calls * algorithmic_bytes(mtype, rows) / el / 1e9
+    return gbs, kind, f"{calls} x Q{'8' if mtype == 1 else '4'}_0 matvec {rows}x{COLS} in {el:.1f} s"
+
+
+def run_reference(args):
+    """--impl reference: the reference CPU path with all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    import oracle
+
+    kind = "reference" if oracle.reference() is not None else "port"
+    from qwen3x_b200 import quant
+
+    w = quant.gaussian((ROWS, COLS), 1, 0.02)
+    packed = quant.quantize_q8_0(w)
+    x = quant.gaussian(COLS, 2)
+    for _ in range(args.warmup):
+        oracle.mv(packed, 1, ROWS, COLS, x, threads=threads, impl=kind if kind == "reference" else "port")
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _c in range(COPIES):
+            oracle.mv(packed, 1, ROWS, COLS, x, threads=threads, impl=kind if kind == "reference" else "port")
+    el = time.perf_counter() - t0
+    value = args.steps * COPIES * algorithmic_bytes(1) / el / 1e9
+    line = {
+        "impl": "reference", "metric": "Q8_0 GEMV HBM GB/s", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} steps x {COPIES} Q8_0 matvecs {ROWS}x{COLS}, "
+                                   f"rows split over {threads} threads"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config():
+    return {"workload": "cfg1: Q8_0 GEMV y=Wx, W 12288x4096 (w~N(0,0.02)), x~N(0,1) FP32",
+            "rows": ROWS, "cols": COLS, "weight_copies": COPIES,
+            "l2": f"inputs larger than L2: {COPIES} resident weight copies x 53.5 MB rotated per step",
+            "step": f"{COPIES} GEMV calls (one per weight copy), CUDA-graph replay",
+            "parallelism": "weak: every rank runs the full workload on its own GPU"}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+
+    from qwen3x_b200 import capi
+
+    capi.lib()  # fails loudly without the kernels
+    rank, world, local = dist_setup(args.gpus)
+    device = torch.device("cuda", torch.cuda.current_device())
+
+    secs, launches, clocks = time_gemv(1, args.steps, args.warmup, device, world, rank == 0)
+    bytes_q8 = algorithmic_bytes(1)
+    total = world * args.steps * COPIES * bytes_q8
+    value = total / secs / 1e9
+    per_launch_s = secs / (args.steps * COPIES)
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_q8 / per_launch_s / 1e9
+
+    q4_secs, _, _ = time_gemv(2, max(args.steps // 2, 10), args.warmup, device, world, False)
+    q4_bytes = algorithmic_bytes(2)
+    q4_per_launch = q4_secs / (max(args.steps // 2, 10) * COPIES)
+    q4_achieved = q4_bytes / q4_per_launch / 1e9
+
+    e2e_steps = max(args.steps // 10, 20)
+    e2e_secs, e2e_io = time_e2e(1, e2e_steps, args.warmup, device, world)
+    e2e_value = world * e2e_steps * COPIES * bytes_q8 / e2e_secs / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, kind, sample = cpu_reference_gbs(1, threads=1, budget_s=10.0)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": "Q8_0 GEMV HBM GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(secs / args.steps * 1e3, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profile_traffic("gemv_q8_cfg1"),
+                         "bytes_per_launch": bytes_q8,
+                         "kernel": "q3xk::gemv_kernel<Q8_0,R=4>"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", **e2e_io,
+                    "path": "q3xk_try_mv_host (pinned host x/y, synchronous)"},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "extra": {
+                "q4_0_gemv": {"value": round(world * q4_bytes / q4_per_launch / 1e9, 2),
+                              "unit": "GB/s", "achieved_per_gpu": round(q4_achieved, 1),
+                              "frac": round(q4_achieved / peak, 4),
+                              "bytes_per_launch": q4_bytes},
+            },
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

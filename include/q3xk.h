@@ -1,0 +1,140 @@
+/*
+ * q3xk.h -- C ABI of the B200 (sm_100a) packed-weight matrix kernels.
+ *
+ * This is the thin launcher layer under the qwen3x backend interface
+ * (internal.h:11-34 of qwen3x): plain pointers and sizes, no C++ or torch
+ * types, so ctypes, cgo or a C++ backend can bind it directly.
+ *
+ * Conventions
+ *   - All data pointers are DEVICE pointers unless a comment says otherwise.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *   - Every entry point returns a q3xk_status and never aborts; argument
+ *     errors are detected on the host before any launch.
+ *   - Activations, outputs and logits are FP32, as in the reference
+ *     (README.md:83-86 of qwen3x).
+ *
+ * Device matrix layout ("row records").  The reference keeps model.bin's
+ * packed blocks (34-byte Q8_0, 18-byte Q4_0; q8.h:10-15, q4.h:29-42) as they
+ * are, which leaves them 2-byte aligned.  Here each row is one 16-byte-aligned
+ * record, built once at upload by q3xk_repack():
+ *   Q8_0: cols bytes of (q XOR 0x80), element k at byte k, then the row's
+ *         cols/32 FP16 scales, padded to a multiple of 8 scales.
+ *   Q4_0: cols/2 bytes: the 16 nibble bytes of each block unchanged (element
+ *         i<16 = low nibble of byte i, i>=16 = high nibble of byte i-16), then
+ *         the scales as above.
+ *   BF16: cols*2 bytes, padded to 16 bytes.
+ * Expert pools (MoE) are `experts` such matrices back to back.
+ */
+#ifndef Q3XK_H
+#define Q3XK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q3XK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define Q3XK_API __attribute__((visibility("default")))
+#else
+#define Q3XK_API
+#endif
+
+typedef enum q3xk_status {
+    Q3XK_OK = 0,
+    Q3XK_EINVAL = 1,       /* bad shape, type, pointer or size */
+    Q3XK_EUNSUPPORTED = 2, /* valid request this build does not implement */
+    Q3XK_ECUDA = 3,        /* a CUDA runtime call or launch failed */
+    Q3XK_EALIGN = 4,       /* a pointer or stride breaks the layout's alignment */
+    Q3XK_ETIMEOUT = 5,     /* a bounded device-side wait gave up */
+    Q3XK_EWORKSPACE = 6    /* caller-provided workspace too small */
+} q3xk_status;
+
+/* Matches q3x_model::MatrixType (model_config.h:16-20). */
+typedef enum q3xk_matrix_type {
+    Q3XK_BF16 = 0,
+    Q3XK_Q8_0 = 1,
+    Q3XK_Q4_0 = 2
+} q3xk_matrix_type;
+
+/* One device matrix (or expert pool) in row-record layout. */
+typedef struct q3xk_matrix {
+    void* data;            /* device pointer, 256-byte aligned */
+    int64_t row_stride;    /* bytes between row records, multiple of 16 */
+    int64_t expert_stride; /* bytes between expert matrices (rows*row_stride) */
+    int32_t type;          /* q3xk_matrix_type */
+    int32_t rows;          /* output features per expert */
+    int32_t cols;          /* input features (K); multiple of 32 if quantized */
+    int32_t experts;       /* 1 for a plain matrix */
+} q3xk_matrix;
+
+/* Human-readable name of a status code (static string). */
+Q3XK_API const char* q3xk_status_string(int status);
+Q3XK_API int q3xk_abi_version(void);
+
+/*
+ * Size of a matrix in model.bin's packed format.  Replaces
+ * q3x_cpu::quantized_bytes (arch/cpu.cpp:161-179) with the same rules:
+ * Q8_0/Q4_0 only, rows > 0, cols > 0, cols % 32 == 0, overflow-checked;
+ * returns Q3XK_EINVAL and leaves *bytes untouched otherwise.
+ */
+Q3XK_API int q3xk_quantized_bytes(int type, int rows, int cols, size_t* bytes);
+
+/*
+ * Fill row_stride/expert_stride/type/rows/cols/experts of *m (data is left
+ * as is) and the device bytes the row-record layout needs.  Replaces the
+ * pointer binding of Model::load (engine.cu:2007-2026 `take`).
+ */
+Q3XK_API int q3xk_matrix_layout(int type, int rows, int cols, int experts,
+                       q3xk_matrix* m, size_t* device_bytes);
+
+/*
+ * Build the row-record layout in m->data from `packed`, a DEVICE copy of the
+ * matrix exactly as stored in model.bin (all experts, back to back).
+ * Replaces the whole-file cudaMemcpy of Model::load (engine.cu:2074-2079),
+ * after which the reference kernels read the 34/18-byte blocks in place.
+ */
+Q3XK_API int q3xk_repack(const q3xk_matrix* m, const void* packed, void* stream);
+
+/*
+ * Decode GEMV: y[rows] = W x (accumulate = 0) or y[rows] += W x
+ * (accumulate != 0).  x: cols FP32, y: rows FP32, both 16-byte aligned; x
+ * and y must not overlap.  CUDA cores only (HBM-bound).
+ * Replaces engine.cu:1531-1561 mv()/mv_add() (kernels mv_q8_kernel,
+ * mv_add_q8_kernel, mv_q4_kernel, mv_add_q4_kernel, mv_kernel at
+ * engine.cu:519-612) and, for the CPU engine, q3x_cpu::try_mv
+ * (arch/cpu.cpp:192-226) as called from engine.cpp:207-212.
+ */
+Q3XK_API int q3xk_gemv(const q3xk_matrix* w, const float* x, float* y, int accumulate,
+              void* stream);
+
+/*
+ * GEMV of one expert of a pool: y = W[expert] x.  `expert` is a host int.
+ * Replaces engine.cpp:214-224 expert_mv.
+ */
+Q3XK_API int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, float* y,
+                     int accumulate, void* stream);
+
+/*
+ * Synchronous GEMV on HOST vectors, the contract of q3x_cpu::try_mv
+ * (arch/cpu.cpp:192-226): y_host is complete when the call returns.  The
+ * matrix stays resident on the device; x_host (cols floats) goes up and
+ * y_host (rows floats) comes back on `stream` (pinned host memory makes the
+ * copies asynchronous DMA).  `workspace` is a caller-owned DEVICE buffer of
+ * at least (cols + rows) * 4 bytes, 16-byte aligned: nothing is allocated.
+ */
+Q3XK_API int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* y_host,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Number of kernel launches the calls above made since the last reset
+ * (host-side counter used by the benchmark's gpu_launches report). */
+Q3XK_API uint64_t q3xk_launch_count(void);
+Q3XK_API void q3xk_reset_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,118 @@
+"""ctypes binding of the q3xk C ABI (include/q3xk.h).
+
+Loading fails loudly when libq3xk.so is missing: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libq3xk.so"
+
+# q3xk_status
+OK, EINVAL, EUNSUPPORTED, ECUDA, EALIGN, ETIMEOUT, EWORKSPACE = range(7)
+# q3xk_matrix_type == q3x_model::MatrixType (model_config.h:16-20)
+BF16, Q8_0, Q4_0 = 0, 1, 2
+TYPE_NAMES = {BF16: "BF16", Q8_0: "Q8_0", Q4_0: "Q4_0"}
+
+
+class Matrix(ctypes.Structure):
+    """struct q3xk_matrix."""
+
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("row_stride", ctypes.c_int64),
+        ("expert_stride", ctypes.c_int64),
+        ("type", ctypes.c_int32),
+        ("rows", ctypes.c_int32),
+        ("cols", ctypes.c_int32),
+        ("experts", ctypes.c_int32),
+    ]
+
+
+class Q3xkError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {status_string(status)} ({status})")
+
+
+_lib = None
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "q3xk_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "q3xk_abi_version": (ctypes.c_int, []),
+    "q3xk_quantized_bytes": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.POINTER(ctypes.c_size_t)]),
+    "q3xk_matrix_layout": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.POINTER(Matrix), ctypes.POINTER(ctypes.c_size_t)]),
+    "q3xk_repack": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xk_gemv": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
+                                 ctypes.c_int, ctypes.c_void_p]),
+    "q3xk_expert_gemv": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "q3xk_try_mv_host": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "q3xk_launch_count": (ctypes.c_uint64, []),
+    "q3xk_reset_launch_count": (None, []),
+}
+
+
+def lib():
+    """The loaded libq3xk.so (raises if it was never built)."""
+    global _lib
+    if _lib is None:
+        path = os.environ.get("Q3XK_LIBRARY", str(LIB_PATH))
+        if not Path(path).exists():
+            raise RuntimeError(
+                f"{path} is missing: build it with `python -m qwen3x_b200.build` "
+                "(the qwen3x_b200 kernels have no CPU fallback)")
+        handle = ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def declared_symbols():
+    return list(_SIGNATURES)
+
+
+def status_string(status: int) -> str:
+    try:
+        return lib().q3xk_status_string(status).decode()
+    except Exception:  # pragma: no cover - only when the library is absent
+        return "status"
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise Q3xkError(status, what)
+
+
+def ptr(t) -> int:
+    """Device (or host) address of a torch tensor / numpy array / int."""
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    if hasattr(t, "ctypes"):
+        return t.ctypes.data
+    raise TypeError(type(t))
+
+
+def stream_ptr(stream=None) -> int:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream

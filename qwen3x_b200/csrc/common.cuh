@@ -1,0 +1,73 @@
+// common.cuh -- shared device helpers for the q3xk kernels (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q3xk.h"
+
+namespace q3xk {
+
+constexpr int kBlock = 32;        // weights per Q8_0/Q4_0 block (q8.h:8, q4.h:8)
+constexpr int kQ8PackedBytes = 34;  // q8.h:15
+constexpr int kQ4PackedBytes = 18;  // q4.h:27
+
+// Host-side launch accounting (q3xk_launch_count).
+void count_launch(int n = 1);
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA; }
+
+inline int last_launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
+}
+
+// Bytes of the quantised part of one row record.
+__host__ __device__ inline int64_t quant_bytes(int type, int cols) {
+    return type == Q3XK_Q8_0 ? (int64_t)cols : type == Q3XK_Q4_0 ? (int64_t)cols / 2
+                                                                 : (int64_t)cols * 2;
+}
+// Scale entries per row, padded to a multiple of 8 (16 bytes).
+__host__ __device__ inline int scale_slots(int cols) { return ((cols / kBlock) + 7) & ~7; }
+
+__host__ __device__ inline int64_t row_record_bytes(int type, int cols) {
+    if (type == Q3XK_BF16) return ((int64_t)cols * 2 + 15) & ~(int64_t)15;
+    return quant_bytes(type, cols) + (int64_t)scale_slots(cols) * 2;
+}
+
+// ---- device helpers -------------------------------------------------------
+
+// Streaming 128-bit load that bypasses L1 allocation: weights are read once.
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint16_t ld_nc_u16(const void* p) {
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float f16_bits_to_float(uint16_t bits) {
+    return __half2float(__ushort_as_half(bits));
+}
+
+// Byte k (0..3) of w as the float 2^23 + byte (exact): PRMT places the byte
+// in the low mantissa bits under the exponent byte 0x4B.
+template <int K>
+__device__ __forceinline__ float byte_as_magic_float(uint32_t w) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | K));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace q3xk
