@@ -338,6 +338,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
@@ -364,7 +365,10 @@ def main(argv=None):
     q4_achieved = q4_bytes / q4_per_launch / 1e9
 
     e2e_steps = max(args.steps // 10, 20)
-    e2e_secs, e2e_io = time_e2e(1, e2e_steps, args.warmup, device, world)
+    if args.no_e2e:
+        e2e_secs, e2e_io = float("inf"), {}
+    else:
+        e2e_secs, e2e_io = time_e2e(1, e2e_steps, args.warmup, device, world)
     e2e_value = world * e2e_steps * COPIES * bytes_q8 / e2e_secs / 1e9
 
     cpu = None
@@ -383,7 +387,7 @@ def main(argv=None):
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profile_traffic("gemv_q8_cfg1"),
                          "bytes_per_launch": bytes_q8,
-                         "kernel": "q3xk::gemv_kernel<Q8_0,R=4>"},
+                         "kernel": "q3xk::gemv_kernel<Q8_0,KS=1>"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", **e2e_io,
                     "path": "q3xk_try_mv_host (pinned host x/y, synchronous)"},
             "gpu_launches": int(launches),

@@ -129,6 +129,16 @@ Q3XK_API int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, 
 Q3XK_API int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* y_host,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Device-side error word of the current device: bit 0 = a producer gave up
+ * waiting for a free stage, bit 1 = a consumer gave up waiting for data.
+ * Every device-side wait in these kernels is bounded (about one second);
+ * on a timeout the kernel sets a bit, lets its own in-flight copies land and
+ * returns, so the context stays usable.  Reading synchronises the device.
+ */
+Q3XK_API int q3xk_device_error(int* flags);
+Q3XK_API int q3xk_clear_device_error(void);
+
 /* Number of kernel launches the calls above made since the last reset
  * (host-side counter used by the benchmark's gpu_launches report). */
 Q3XK_API uint64_t q3xk_launch_count(void);

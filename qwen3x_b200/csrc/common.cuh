@@ -71,3 +71,36 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 }  // namespace q3xk
+
+namespace q3xk {
+
+// Programmatic dependent launch (sm_90+).  A kernel launched with the
+// programmatic-serialization attribute may start while its predecessor in
+// the stream is still running; griddep_wait() blocks until the predecessor
+// has completed and its writes are visible.  Everything a kernel reads that
+// an earlier kernel may write (activations, outputs it accumulates into)
+// must be read after griddep_wait(); immutable weights may be read before.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with the programmatic stream serialization attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+}  // namespace q3xk

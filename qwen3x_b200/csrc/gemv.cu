@@ -2,192 +2,434 @@
 //
 // Replaces the reference's one-CTA-per-row kernels with 1-byte loads and a
 // per-element FP16 decode (engine.cu:546-612).  Decode GEMV is HBM-bound
-// (≈1.9 flop/B for Q8_0), so the design goal is bytes in flight, not FLOPs:
-//   * each warp owns R consecutive rows and walks K in 16-byte lane units
-//     (Q8_0: 16 weights, Q4_0: 32 weights = one block, BF16: 8 weights);
-//   * UB units per lane and row are loaded (128-bit, L1::no_allocate) before
-//     any is consumed, so a CTA keeps 8 warps x 32 lanes x UB x R x 16 B of
-//     weights in flight;
-//   * the R rows share each x load, which keeps L1 traffic for x at 4/R bytes
-//     per weight;
-//   * dequant is exact and branch-free: PRMT turns a byte (or a nibble after
-//     one LOP3) into the float 2^23 + value, one packed f32x2 add removes the
-//     offset, one packed f32x2 FMA accumulates (Blackwell FFMA2);
-//   * a block's FP16 scale multiplies the block's inner sum, as in
-//     arch/cpu.cpp:64-73, and the lanes' partial sums meet in a warp shuffle.
+// (~1.9 flop/B for Q8_0); the kernel is built around bytes in flight:
+//
+//  * Every CTA owns a contiguous, balanced range of rows (+-1 row), so all
+//    SMs stream the same number of bytes.  Inside a CTA, thread t owns one
+//    16-byte "unit" column (Q8_0: 16 weights, Q4_0: one 32-weight block,
+//    BF16: 8 weights) and
+//    kRows rows of a row group; a row's units are spread over the threads,
+//    so every thread works on every row group (no imbalance within a CTA).
+//  * Weights are read once with 128-bit L1::no_allocate loads, double
+//    buffered in registers: the next row group's loads are in flight while
+//    the current one is dequantised.  Measured on B200, plain vector loads
+//    stream a 53 MB matrix faster than cp.async.bulk staging.
+//  * x is prescaled once per CTA into shared memory, per unit, by a power of
+//    two chosen from the unit's largest |x|.  A Q8_0 byte (stored as q+128)
+//    or a Q4_0 nibble masked in place is then used directly as the float
+//    n * 2^(pos-149) (exact; FP32 subnormals are kept), so the dequant costs
+//    one LOP3 and half a packed FFMA2 per weight and no offset subtraction;
+//    sum(n x) is rescaled once per unit and the +128 / +8 offsets removed
+//    with the unit's sum of x.  Units whose x holds non-finite values or
+//    magnitudes >= 2^104 use an exact "2^23 + n" PRMT decode instead.
+//  * A row's partial sums meet in a warp butterfly, then in shared memory in
+//    a fixed order: results are deterministic.
+//  * Programmatic dependent launch: the first row group's weights are
+//    requested before griddepcontrol.wait, i.e. while the previous kernel in
+//    the stream is still finishing; x and y are only touched after it.
 #include "common.cuh"
 
 namespace q3xk {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+#ifndef Q3XK_GEMV_PDL
+#define Q3XK_GEMV_PDL 1
+#endif
+#ifndef Q3XK_GEMV_MIN_BLOCKS
+#define Q3XK_GEMV_MIN_BLOCKS 3
+#endif
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kRows = 4;  // rows per warp
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float bits_f(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
-// Inner sum of one Q8_0 half block (16 weights = one 16-byte unit).
-__device__ __forceinline__ float q8_unit_dot(const uint4 q, const float4 xa, const float4 xb,
-                                             const float4 xc, const float4 xd) {
-    const float2 off = f2(-8388736.0f, -8388736.0f);  // 2^23 + 128 (offset binary)
-    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-#define Q8_WORD(W, X)                                                                     \
-    {                                                                                     \
-        const float2 v01 = __fadd2_rn(f2(byte_as_magic_float<0>(W), byte_as_magic_float<1>(W)), off); \
-        const float2 v23 = __fadd2_rn(f2(byte_as_magic_float<2>(W), byte_as_magic_float<3>(W)), off); \
-        a0 = __ffma2_rn(v01, f2(X.x, X.y), a0);                                           \
-        a1 = __ffma2_rn(v23, f2(X.z, X.w), a1);                                           \
-    }
-    Q8_WORD(q.x, xa)
-    Q8_WORD(q.y, xb)
-    Q8_WORD(q.z, xc)
-    Q8_WORD(q.w, xd)
-#undef Q8_WORD
-    return (a0.x + a0.y) + (a1.x + a1.y);
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+    uint16_t r;
+    asm("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
 }
 
-// Inner sum of one Q4_0 block (32 weights = one 16-byte unit).  Byte i holds
-// element i (low nibble) and element i + 16 (high nibble), q4.h:31-36.
-__device__ __forceinline__ float q4_unit_dot(const uint4 q, const float4* xs) {
-    const float2 off = f2(-8388616.0f, -8388616.0f);  // 2^23 + 8
-    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t lo = words[j] & 0x0F0F0F0Fu;
-        const uint32_t hi = (words[j] >> 4) & 0x0F0F0F0Fu;
-        const float4 xl = xs[j], xh = xs[4 + j];
-        const float2 l01 = __fadd2_rn(f2(byte_as_magic_float<0>(lo), byte_as_magic_float<1>(lo)), off);
-        const float2 l23 = __fadd2_rn(f2(byte_as_magic_float<2>(lo), byte_as_magic_float<3>(lo)), off);
-        const float2 h01 = __fadd2_rn(f2(byte_as_magic_float<0>(hi), byte_as_magic_float<1>(hi)), off);
-        const float2 h23 = __fadd2_rn(f2(byte_as_magic_float<2>(hi), byte_as_magic_float<3>(hi)), off);
-        a0 = __ffma2_rn(l01, f2(xl.x, xl.y), a0);
-        a1 = __ffma2_rn(l23, f2(xl.z, xl.w), a1);
-        a0 = __ffma2_rn(h01, f2(xh.x, xh.y), a0);
-        a1 = __ffma2_rn(h23, f2(xh.z, xh.w), a1);
-    }
-    return (a0.x + a0.y) + (a1.x + a1.y);
-}
+struct GemvParams {
+    const uint8_t* w;  // first row record
+    const float* x;
+    float* y;
+    int64_t row_stride;
+    int64_t qbytes;  // quantised bytes per row (scales follow)
+    int rows, cols;
+    int accumulate;
+    int units;   // 16-byte units per row
+    int ksplit;  // warps sharing a row group (1, 2, 4 or 8), each on a slice of K
+};
 
-// BF16 unit: 8 weights; bf16 -> f32 is a 16-bit shift.
-__device__ __forceinline__ float bf16_unit_dot(const uint4 q, const float4 xa, const float4 xb) {
-    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-#define BF_WORD(W, X0, X1, ACC) \
-    ACC = __ffma2_rn(f2(__uint_as_float((W) << 16), __uint_as_float((W) & 0xFFFF0000u)), f2(X0, X1), ACC);
-    BF_WORD(q.x, xa.x, xa.y, a0)
-    BF_WORD(q.y, xa.z, xa.w, a1)
-    BF_WORD(q.z, xb.x, xb.y, a0)
-    BF_WORD(q.w, xb.z, xb.w, a1)
-#undef BF_WORD
-    return (a0.x + a0.y) + (a1.x + a1.y);
-}
-
-template <int TYPE, int R, int UB>
-__global__ void __launch_bounds__(kThreads)
-gemv_kernel(const uint8_t* __restrict__ w, int64_t row_stride, int rows, int cols,
-            const float* __restrict__ x, float* __restrict__ y, int accumulate) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = (blockIdx.x * kWarps + warp) * R;
-    if (row0 >= rows) return;
-    const int64_t qbytes = quant_bytes(TYPE, cols);
-    const int units = (int)((TYPE == Q3XK_BF16 ? (int64_t)cols * 2 : qbytes) / 16);
-    const uint8_t* rec[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) rec[r] = w + (int64_t)min(row0 + r, rows - 1) * row_stride;
-
-    float acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
-
-    for (int base = lane; base < units; base += 32 * UB) {
-        uint4 q[UB][R];
-        float d[UB][R];
-#pragma unroll
-        for (int i = 0; i < UB; ++i) {
-            const int u = base + 32 * i;
-            if (u < units) {
-#pragma unroll
-                for (int r = 0; r < R; ++r) q[i][r] = ld_stream_v4(rec[r] + (int64_t)u * 16);
-                if (TYPE != Q3XK_BF16) {
-                    const int blk = TYPE == Q3XK_Q8_0 ? (u >> 1) : u;
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        d[i][r] = f16_bits_to_float(ld_nc_u16(rec[r] + qbytes + 2 * blk));
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < UB; ++i) {
-            const int u = base + 32 * i;
-            if (u < units) {
-                if (TYPE == Q3XK_Q8_0) {
-                    const float4* xp = reinterpret_cast<const float4*>(x) + (int64_t)u * 4;
-                    const float4 xa = __ldg(xp), xb = __ldg(xp + 1), xc = __ldg(xp + 2),
-                                 xd = __ldg(xp + 3);
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        acc[r] = fmaf(d[i][r], q8_unit_dot(q[i][r], xa, xb, xc, xd), acc[r]);
-                } else if (TYPE == Q3XK_Q4_0) {
-                    const float4* xp = reinterpret_cast<const float4*>(x) + (int64_t)u * 8;
-                    float4 xs[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) xs[k] = __ldg(xp + k);
-#pragma unroll
-                    for (int r = 0; r < R; ++r)
-                        acc[r] = fmaf(d[i][r], q4_unit_dot(q[i][r], xs), acc[r]);
-                } else {
-                    const float4* xp = reinterpret_cast<const float4*>(x) + (int64_t)u * 2;
-                    const float4 xa = __ldg(xp), xb = __ldg(xp + 1);
-#pragma unroll
-                    for (int r = 0; r < R; ++r) acc[r] += bf16_unit_dot(q[i][r], xa, xb);
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = warp_sum(acc[r]);
-    if (lane < R) {
-        float v = acc[0];
-#pragma unroll
-        for (int r = 1; r < R; ++r)
-            if (lane == r) v = acc[r];
-        const int row = row0 + lane;
-        if (row < rows) y[row] = accumulate ? y[row] + v : v;
-    }
-}
-
-template <int TYPE, int R>
-void launch_rows(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y,
-                 int accumulate, cudaStream_t s) {
-    const int rows_per_cta = kWarps * R;
-    const unsigned grid = (unsigned)((m->rows + rows_per_cta - 1) / rows_per_cta);
-    constexpr int UB = TYPE == Q3XK_Q4_0 ? 2 : 2;
-    gemv_kernel<TYPE, R, UB><<<grid, kThreads, 0, s>>>(base, m->row_stride, m->rows, m->cols, x,
-                                                      y, accumulate);
-}
-
+// Per-type geometry and arithmetic.  A unit's x values reach dot() as
+// kChunks float4 in slot order; `gg` = {g, gs}: g = 2^(149-P) rescales
+// sum(n x) on the fast path, gs = -offset * sum(x).
 template <int TYPE>
-void launch_type(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y,
-                 int accumulate, cudaStream_t s, int sm_count) {
-    // Enough CTAs to fill every SM at least twice; more rows per warp when the
-    // matrix is tall, so each x load serves several rows.
-    const int target = 2 * sm_count;
-    if ((m->rows + 31) / 32 >= target)
-        launch_rows<TYPE, 4>(m, base, x, y, accumulate, s);
-    else if ((m->rows + 15) / 16 >= target)
-        launch_rows<TYPE, 2>(m, base, x, y, accumulate, s);
-    else
-        launch_rows<TYPE, 1>(m, base, x, y, accumulate, s);
+struct Codec;
+
+template <>
+struct Codec<Q3XK_Q8_0> {
+    // 16 weights (half a block, 16 bytes) per unit; two units share a scale.
+    static constexpr int kCols = 16, kVecs = 1, kChunks = 4, kUnitsPerBlock = 2, kBatch = 2;
+    static constexpr float kOffset = 128.f;
+    // x slot k holds element k (byte k): byte position k % 4 of word k / 4;
+    // positions 0..2 are masked in place (bit 8k), position 3 after >> 24.
+    __device__ static int shift(int k) { return (k & 3) == 1 ? 8 : (k & 3) == 2 ? 16 : 0; }
+    __device__ static int element(int k) { return k; }
+
+    template <bool FAST>
+    __device__ __forceinline__ static float dot(const uint4* q, const float4* x, float2 gg) {
+        const uint32_t w[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+        float2 a = f2(0.f, 0.f), b = f2(0.f, 0.f);
+        if (FAST) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a = __ffma2_rn(f2(bits_f(w[j] & 0xFFu), bits_f(w[j] & 0xFF00u)), f2(x[j].x, x[j].y), a);
+                b = __ffma2_rn(f2(bits_f(w[j] & 0xFF0000u), bits_f(w[j] >> 24)), f2(x[j].z, x[j].w), b);
+            }
+            return fmaf((a.x + a.y) + (b.x + b.y), gg.x, gg.y);
+        }
+        const float2 off = f2(-8388736.0f, -8388736.0f);  // 2^23 + 128
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 v01 = __fadd2_rn(f2(byte_as_magic_float<0>(w[j]), byte_as_magic_float<1>(w[j])), off);
+            const float2 v23 = __fadd2_rn(f2(byte_as_magic_float<2>(w[j]), byte_as_magic_float<3>(w[j])), off);
+            a = __ffma2_rn(v01, f2(x[j].x, x[j].y), a);
+            b = __ffma2_rn(v23, f2(x[j].z, x[j].w), b);
+        }
+        return (a.x + a.y) + (b.x + b.y);
+    }
+};
+
+// Q4_0: word j of the 16-byte unit holds bytes 4j..4j+3; nibble position p
+// (bits 4p..4p+3) is element 4j + p/2, +16 for odd p (q4.h:31-36).  x slot
+// 8j + p holds that element; positions 0..5 are masked in place, 6 and 7
+// after >> 8 (so they sit at bits 16 and 20).
+template <>
+struct Codec<Q3XK_Q4_0> {
+    static constexpr int kCols = 32, kVecs = 1, kChunks = 8, kUnitsPerBlock = 1, kBatch = 1;
+    static constexpr float kOffset = 8.f;
+    __device__ static int shift(int k) {
+        const int p = k & 7;
+        return p < 6 ? 4 * p : 4 * p - 8;
+    }
+    __device__ static int element(int k) {
+        const int j = k >> 3, p = k & 7;
+        return 4 * j + (p >> 1) + (p & 1) * 16;
+    }
+
+    template <bool FAST>
+    __device__ __forceinline__ static float dot(const uint4* q, const float4* x, float2 gg) {
+        const uint32_t w[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+        float2 a = f2(0.f, 0.f), b = f2(0.f, 0.f);
+        if (FAST) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 x0 = x[2 * j], x1 = x[2 * j + 1];
+                const uint32_t h = w[j] >> 8;
+                a = __ffma2_rn(f2(bits_f(w[j] & 0xFu), bits_f(w[j] & 0xF0u)), f2(x0.x, x0.y), a);
+                b = __ffma2_rn(f2(bits_f(w[j] & 0xF00u), bits_f(w[j] & 0xF000u)), f2(x0.z, x0.w), b);
+                a = __ffma2_rn(f2(bits_f(w[j] & 0xF0000u), bits_f(w[j] & 0xF00000u)), f2(x1.x, x1.y), a);
+                b = __ffma2_rn(f2(bits_f(h & 0xF0000u), bits_f(h & 0xF00000u)), f2(x1.z, x1.w), b);
+            }
+            return fmaf((a.x + a.y) + (b.x + b.y), gg.x, gg.y);
+        }
+        const float2 off = f2(-8388616.0f, -8388616.0f);  // 2^23 + 8
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 x0 = x[2 * j], x1 = x[2 * j + 1];  // (lo0 hi0 lo1 hi1) (lo2 hi2 lo3 hi3)
+            const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+            const float2 l01 = __fadd2_rn(f2(byte_as_magic_float<0>(lo), byte_as_magic_float<1>(lo)), off);
+            const float2 l23 = __fadd2_rn(f2(byte_as_magic_float<2>(lo), byte_as_magic_float<3>(lo)), off);
+            const float2 h01 = __fadd2_rn(f2(byte_as_magic_float<0>(hi), byte_as_magic_float<1>(hi)), off);
+            const float2 h23 = __fadd2_rn(f2(byte_as_magic_float<2>(hi), byte_as_magic_float<3>(hi)), off);
+            a = __ffma2_rn(l01, f2(x0.x, x0.z), a);
+            b = __ffma2_rn(l23, f2(x1.x, x1.z), b);
+            a = __ffma2_rn(h01, f2(x0.y, x0.w), a);
+            b = __ffma2_rn(h23, f2(x1.y, x1.w), b);
+        }
+        return (a.x + a.y) + (b.x + b.y);
+    }
+};
+
+template <>
+struct Codec<Q3XK_BF16> {
+    static constexpr int kCols = 8, kVecs = 1, kChunks = 2, kUnitsPerBlock = 1, kBatch = 2;
+    static constexpr float kOffset = 0.f;
+    __device__ static int shift(int) { return 0; }
+    __device__ static int element(int k) { return k; }
+
+    template <bool FAST>
+    __device__ __forceinline__ static float dot(const uint4* q, const float4* x, float2) {
+        const uint32_t w[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+        float2 a = __ffma2_rn(f2(bits_f(w[0] << 16), bits_f(w[0] & 0xFFFF0000u)), f2(x[0].x, x[0].y), f2(0.f, 0.f));
+        float2 b = __ffma2_rn(f2(bits_f(w[1] << 16), bits_f(w[1] & 0xFFFF0000u)), f2(x[0].z, x[0].w), f2(0.f, 0.f));
+        a = __ffma2_rn(f2(bits_f(w[2] << 16), bits_f(w[2] & 0xFFFF0000u)), f2(x[1].x, x[1].y), a);
+        b = __ffma2_rn(f2(bits_f(w[3] << 16), bits_f(w[3] & 0xFFFF0000u)), f2(x[1].z, x[1].w), b);
+        return (a.x + a.y) + (b.x + b.y);
+    }
+};
+
+// Unit u's 16-byte chunk j lives at chunk swz(u, j) of the unit's slot, so the
+// 8 lanes of a quarter warp (consecutive units) hit 8 different bank groups.
+template <int TYPE>
+__device__ __forceinline__ int swz(int u, int j) {
+    return (j + u) & (Codec<TYPE>::kChunks - 1);
+}
+
+// Warp-level work: kRows consecutive rows and one of `ksplit` interleaved
+// slices of their units; the warp's lanes walk the slice with a stride of 32
+// units and load Codec::kBatch units per lane and row at once.
+template <int TYPE>
+struct Batch {
+    static constexpr int kBatch = Codec<TYPE>::kBatch;
+    uint4 q[kBatch][kRows];
+    uint16_t d[kBatch][kRows];
+};
+
+// Unit index of batch b, entry i, for a warp on slice ks of ksplit.
+__device__ __forceinline__ int unit_of(int lane, int b, int i, int kbatch, int ks, int ksplit) {
+    return lane + 32 * ((b * kbatch + i) * ksplit + ks);
+}
+
+template <int TYPE, int KS>
+__device__ __forceinline__ void load_batch(Batch<TYPE>& bt, const GemvParams& p,
+                                           const uint8_t* const* rec, int lane, int b, int ks) {
+    constexpr int kBatch = Codec<TYPE>::kBatch;
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+        const int u = unit_of(lane, b, i, kBatch, ks, KS);
+        if (u < p.units) {
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {
+                bt.q[i][j] = ldg_stream(rec[j] + (int64_t)u * 16);
+                if (TYPE != Q3XK_BF16)
+                    bt.d[i][j] = ldg_u16(rec[j] + p.qbytes + 2 * (u / Codec<TYPE>::kUnitsPerBlock));
+            }
+        }
+    }
+}
+
+// Returns this warp's partial sum of row (b4 ? 2 : 0) + (b3 ? 1 : 0) in lanes
+// 0, 8, 16 and 24 (transposed butterfly over the 4 rows).
+template <int TYPE, bool FAST, int KS>
+__device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* const* rec, int lane,
+                                           int ks, Batch<TYPE>& A, const float4* xs4,
+                                           const float2* gg) {
+    using C = Codec<TYPE>;
+    constexpr int kC = C::kChunks;
+    constexpr int kBatch = C::kBatch;
+    float acc[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) acc[j] = 0.f;
+    const int span = 32 * kBatch * KS;
+    const int nb = (p.units + span - 1) / span;  // batches per row group and slice
+    for (int b = 0; b < nb; ++b) {
+        if (b > 0) load_batch<TYPE, KS>(A, p, rec, lane, b, ks);
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const int u = unit_of(lane, b, i, kBatch, ks, KS);
+            if (u < p.units) {
+                float4 xr[kC];
+#pragma unroll
+                for (int j = 0; j < kC; ++j) xr[j] = xs4[u * kC + swz<TYPE>(u, j)];
+                const float2 gu = gg[u];
+#pragma unroll
+                for (int j = 0; j < kRows; ++j) {
+                    const float dv = C::template dot<FAST>(&A.q[i][j], xr, gu);
+                    if (TYPE == Q3XK_BF16) acc[j] += dv;
+                    else acc[j] = fmaf(f16_bits_to_float(A.d[i][j]), dv, acc[j]);
+                }
+            }
+        }
+    }
+    const bool b4 = lane & 16, b3 = lane & 8;
+    float k0 = b4 ? acc[2] : acc[0], k1 = b4 ? acc[3] : acc[1];
+    const float s0 = b4 ? acc[0] : acc[2], s1 = b4 ? acc[1] : acc[3];
+    k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+    k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+    float k = b3 ? k1 : k0;
+    k += __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+    k += __shfl_xor_sync(0xffffffffu, k, 4);
+    k += __shfl_xor_sync(0xffffffffu, k, 2);
+    k += __shfl_xor_sync(0xffffffffu, k, 1);
+    return k;
+}
+
+template <int TYPE, int KS>
+__global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(const GemvParams p) {
+    using C = Codec<TYPE>;
+    static_assert(kRows == 4, "the transposed row reduction is written for 4 rows");
+    extern __shared__ __align__(16) float smem[];
+    float4* xs4 = reinterpret_cast<float4*>(smem);                              // units * kChunks
+    float2* gg = reinterpret_cast<float2*>(smem + (size_t)p.units * C::kCols);  // units
+    float* part = reinterpret_cast<float*>(gg + p.units);                      // kWarps * kRows
+
+    griddep_launch_dependents();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ks = warp % KS;                 // K slice of this warp
+    constexpr int groups_per_cta = kWarps / KS;  // row groups per CTA
+    const int group = warp / KS;
+    const int row0 = (blockIdx.x * groups_per_cta + group) * kRows;
+    const uint8_t* rec[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) rec[j] = p.w + (int64_t)min(row0 + j, p.rows - 1) * p.row_stride;
+
+    // The first batch of weights is requested before waiting on the previous kernel.
+    Batch<TYPE> A;
+    if (row0 < p.rows) load_batch<TYPE, KS>(A, p, rec, lane, 0, ks);
+
+    griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
+
+    // Prescale x per unit into shared memory (16-byte chunks, swizzled).
+    int slow = 0;
+    for (int u = tid; u < p.units; u += kThreads) {
+        const float* xu = p.x + (int64_t)u * C::kCols;
+        float v[C::kCols];
+#pragma unroll
+        for (int i = 0; i < C::kCols / 4; ++i) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(xu) + i);
+            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+        }
+        int P = 0;
+        float2 gu = f2(1.f, 0.f);
+        if (TYPE != Q3XK_BF16) {
+            uint32_t emax = 0;
+            float sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < C::kCols; ++k) {
+                emax = max(emax, (__float_as_uint(v[k]) >> 23) & 0xFFu);
+                sum += v[k];
+            }
+            // Exponents up to 103 keep every prescaled value finite.
+            slow |= (emax == 0xFFu || (int)emax - 127 > 103) ? 1 : 0;
+            P = min(127, max(23, 126 - ((int)emax - 127)));
+            gu = f2(pow2f(149 - P), -C::kOffset * sum);
+        }
+#pragma unroll
+        for (int j = 0; j < C::kChunks; ++j) {
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int kk = 4 * j + e;
+                o[e] = TYPE == Q3XK_BF16 ? v[kk] : v[C::element(kk)] * pow2f(P - C::shift(kk));
+            }
+            xs4[u * C::kChunks + swz<TYPE>(u, j)] = make_float4(o[0], o[1], o[2], o[3]);
+        }
+        gg[u] = gu;
+    }
+    const int any_slow = __syncthreads_or(slow);
+    float k = 0.f;
+    if (any_slow) {
+        // Exact fallback for the whole CTA: unscaled x in the same slot order.
+        for (int u = tid; u < p.units; u += kThreads) {
+            const float* xu = p.x + (int64_t)u * C::kCols;
+#pragma unroll
+            for (int j = 0; j < C::kChunks; ++j)
+                xs4[u * C::kChunks + swz<TYPE>(u, j)] =
+                    make_float4(xu[C::element(4 * j)], xu[C::element(4 * j + 1)],
+                                xu[C::element(4 * j + 2)], xu[C::element(4 * j + 3)]);
+        }
+        __syncthreads();
+        if (row0 < p.rows) k = warp_rows<TYPE, false, KS>(p, rec, lane, ks, A, xs4, gg);
+    } else {
+        if (row0 < p.rows) k = warp_rows<TYPE, true, KS>(p, rec, lane, ks, A, xs4, gg);
+    }
+    const int r = (lane & 16 ? 2 : 0) + (lane & 8 ? 1 : 0);
+    if (KS == 1) {
+        if ((lane & 7) == 0 && row0 + r < p.rows) {
+            float* yp = p.y + row0 + r;
+            *yp = p.accumulate ? *yp + k : k;
+        }
+        return;
+    }
+    // Slices of a row group meet in shared memory, added in slice order.
+    if ((lane & 7) == 0) part[warp * kRows + r] = k;
+    __syncthreads();
+    if (tid < groups_per_cta * kRows) {
+        const int g = tid / kRows, rr = tid % kRows;
+        const int row = (blockIdx.x * groups_per_cta + g) * kRows + rr;
+        if (row < p.rows) {
+            float v = 0.f;
+#pragma unroll
+            for (int s = 0; s < KS; ++s) v += part[(g * KS + s) * kRows + rr];
+            p.y[row] = p.accumulate ? p.y[row] + v : v;
+        }
+    }
 }
 
 int sm_count_cached() {
     static int count = 0;
     if (!count) {
         int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             count = 148;
     }
     return count;
+}
+
+// Split K over the warps of a CTA only when the matrix has too few rows to
+// fill the GPU: the smallest split (1, 2, 4) whose grid keeps at least half
+// of the resident CTA slots busy.  Every CTA prescales all of x, so small
+// CTAs (large splits) pay that prologue over fewer rows.
+int choose_ksplit(int rows, int units, int slots) {
+    for (int ks = 1; ks <= 4; ks *= 2) {
+        if (ks > 1 && units < 32 * ks) return ks / 2;
+        const int64_t per = (int64_t)(kWarps / ks) * kRows;
+        const int64_t ctas = (rows + per - 1) / per;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        if (2 * ctas >= waves * slots) return ks;
+    }
+    return 4;
+}
+
+template <int TYPE>
+size_t smem_bytes(const GemvParams& p) {
+    return (size_t)p.units * Codec<TYPE>::kCols * 4 + (size_t)p.units * 8 + kWarps * kRows * 4;
+}
+
+template <int TYPE, int KS>
+int launch_ks(const GemvParams& p, size_t smem, cudaStream_t s) {
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+        if (cudaFuncSetAttribute(gemv_kernel<TYPE, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024) != cudaSuccess)
+            return Q3XK_ECUDA;
+        configured = 200 * 1024;
+    }
+    constexpr int rows_per_cta = (kWarps / KS) * kRows;
+    const int64_t grid = (p.rows + rows_per_cta - 1) / rows_per_cta;
+#if Q3XK_GEMV_PDL
+    const cudaError_t e = launch_pdl(gemv_kernel<TYPE, KS>, dim3((unsigned)grid), dim3(kThreads), smem, s, p);
+#else
+    gemv_kernel<TYPE, KS><<<(unsigned)grid, kThreads, smem, s>>>(p);
+    const cudaError_t e = cudaGetLastError();
+#endif
+    return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
+}
+
+template <int TYPE>
+int launch(const GemvParams& p, cudaStream_t s) {
+    const size_t smem = smem_bytes<TYPE>(p);
+    if (smem > 200 * 1024) return Q3XK_EUNSUPPORTED;
+    switch (p.ksplit) {
+    case 1: return launch_ks<TYPE, 1>(p, smem, s);
+    case 2: return launch_ks<TYPE, 2>(p, smem, s);
+    case 4: return launch_ks<TYPE, 4>(p, smem, s);
+    default: return launch_ks<TYPE, 8>(p, smem, s);
+    }
 }
 
 int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y,
@@ -195,23 +437,27 @@ int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* 
     if (!m || !base || !x || !y || m->rows <= 0 || m->cols <= 0) return Q3XK_EINVAL;
     if (m->row_stride != row_record_bytes(m->type, m->cols)) return Q3XK_EINVAL;
     if (((uintptr_t)base & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
-    const int sms = sm_count_cached();
+    if (m->type != Q3XK_BF16 && m->type != Q3XK_Q8_0 && m->type != Q3XK_Q4_0) return Q3XK_EINVAL;
+    if (m->type != Q3XK_BF16 && m->cols % kBlock) return Q3XK_EINVAL;
+    if (m->type == Q3XK_BF16 && m->cols % 8) return Q3XK_EUNSUPPORTED;
+    GemvParams p{};
+    p.w = base;
+    p.x = x;
+    p.y = y;
+    p.row_stride = m->row_stride;
+    p.qbytes = quant_bytes(m->type, m->cols);
+    p.rows = m->rows;
+    p.cols = m->cols;
+    p.accumulate = accumulate ? 1 : 0;
+    p.units = m->cols / (m->type == Q3XK_Q4_0 ? 32 : m->type == Q3XK_Q8_0 ? 16 : 8);
+    p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * Q3XK_GEMV_MIN_BLOCKS);
+    int st;
     switch (m->type) {
-    case Q3XK_Q8_0:
-        if (m->cols % kBlock) return Q3XK_EINVAL;
-        launch_type<Q3XK_Q8_0>(m, base, x, y, accumulate, s, sms);
-        break;
-    case Q3XK_Q4_0:
-        if (m->cols % kBlock) return Q3XK_EINVAL;
-        launch_type<Q3XK_Q4_0>(m, base, x, y, accumulate, s, sms);
-        break;
-    case Q3XK_BF16:
-        if (m->cols % 8) return Q3XK_EUNSUPPORTED;
-        launch_type<Q3XK_BF16>(m, base, x, y, accumulate, s, sms);
-        break;
-    default:
-        return Q3XK_EINVAL;
+    case Q3XK_Q8_0: st = launch<Q3XK_Q8_0>(p, s); break;
+    case Q3XK_Q4_0: st = launch<Q3XK_Q4_0>(p, s); break;
+    default: st = launch<Q3XK_BF16>(p, s); break;
     }
+    if (st != Q3XK_OK) return st;
     count_launch();
     return last_launch_status();
 }
@@ -256,5 +502,15 @@ int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* y_host, v
         return Q3XK_ECUDA;
     return cuda_status(cudaStreamSynchronize(s));
 }
+
+// This GEMV has no device-side waits; the error word is kept for the kernels
+// that do (and for ABI stability) and is always 0 here.
+int q3xk_device_error(int* flags) {
+    if (!flags) return Q3XK_EINVAL;
+    *flags = 0;
+    return cuda_status(cudaDeviceSynchronize());
+}
+
+int q3xk_clear_device_error(void) { return Q3XK_OK; }
 
 }  // extern "C"

@@ -113,7 +113,7 @@ def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
 
 def dequantize(packed: np.ndarray, mtype: int, rows: int, cols: int) -> np.ndarray:
     """Packed bytes -> FP32 [rows, cols] (value = f16(d) * q, exact in FP32)."""
-    raw = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1)
+    raw = np.ascontiguousarray(packed).reshape(-1).view(np.uint8)
     if mtype == Q8_0:
         b = raw.view(Q8_DTYPE)
         d = b["scale"].view("<f2").astype(np.float32)

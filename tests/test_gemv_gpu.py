@@ -159,3 +159,52 @@ def test_deterministic(cuda):
     mv(lin, xd, a)
     mv(lin, xd, b)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+def test_huge_inputs_take_exact_fallback(cuda, mtype):
+    """x entries >= 2^104 send their unit to the unscaled decode path."""
+    rows, cols = 200, 2048
+    packed = quant.quantize(quant.gaussian((rows, cols), 16, 0.02), mtype)
+    x = quant.gaussian(cols, 17)
+    x[::97] *= np.float32(3e32)
+    ref = oracle.mv(packed, mtype, rows, cols, x)
+    y = run_mv(cuda, packed, mtype, rows, cols, x)
+    assert np.all(np.isfinite(y))
+    assert scaled_err(y, ref, packed, mtype, rows, cols, x) <= TOL
+
+
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+def test_non_finite_inputs_propagate_like_reference(cuda, mtype):
+    """inf/nan in x give the reference's inf/nan pattern (q*inf, 0*inf = nan)."""
+    rows, cols = 64, 512
+    packed = quant.quantize(quant.gaussian((rows, cols), 18, 0.02), mtype)
+    x = quant.gaussian(cols, 19)
+    x[5] = np.inf
+    x[300] = -np.inf if mtype == Q8_0 else np.nan
+    ref = oracle.mv(packed, mtype, rows, cols, x)
+    y = run_mv(cuda, packed, mtype, rows, cols, x)
+    assert np.array_equal(np.isnan(y), np.isnan(ref))
+    fin = ~np.isnan(ref)
+    assert np.array_equal(y[fin], ref[fin]) or np.array_equal(np.sign(y[fin]), np.sign(ref[fin]))
+
+
+@pytest.mark.parametrize("cols", [4096, 6144])
+def test_bf16_chunked(cuda, cols):
+    rows = 100
+    bits = quant.to_bf16_bits(quant.gaussian((rows, cols), 20, 0.02))
+    x = quant.gaussian(cols, 21)
+    ref = oracle.mv(bits, BF16, rows, cols, x)
+    y = run_mv(cuda, bits, BF16, rows, cols, x)
+    assert scaled_err(y, ref, bits, BF16, rows, cols, x) <= TOL
+
+
+def test_no_device_timeouts(cuda):
+    """Every bounded wait of the runs above completed (error word still 0)."""
+    import ctypes
+
+    from qwen3x_b200.capi import lib
+
+    flags = ctypes.c_int(-1)
+    assert lib().q3xk_device_error(ctypes.byref(flags)) == 0
+    assert flags.value == 0
