@@ -57,6 +57,16 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
 def profile_traffic(name: str):
     """Per-launch DRAM bytes of the kernel from the committed ncu summary."""
     p = ROOT / "profiles" / f"{name}.json"
@@ -255,6 +265,39 @@ def time_e2e(mtype: int, steps: int, warmup: int, device, world: int):
     return secs, {"h2d_bytes_per_step": COPIES * COLS * 4, "d2h_bytes_per_step": COPIES * ROWS * 4}
 
 
+def time_gemm(mtype: int, T: int, reps: int, device, world: int):
+    """Prefill dequant-GEMM Y[T, 12288] = X[T, 4096] W^T (BASELINE config 2);
+    returns (seconds per call, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from qwen3x_b200 import quant
+    from qwen3x_b200.linear import Linear, batch_mv, gemm_workspace_bytes
+
+    packed = quant.quantize(quant.gaussian((ROWS, COLS), 1, 0.02), mtype)
+    lin = Linear.from_packed(packed, mtype, ROWS, COLS, device=device)
+    X = torch.from_numpy(quant.gaussian((T, COLS), 3)).to(device)
+    Y = torch.empty(T, ROWS, device=device)
+    ws = torch.empty(gemm_workspace_bytes(T, COLS), dtype=torch.uint8, device=device)
+    for _ in range(3):
+        batch_mv(lin, X, Y, workspace=ws)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        batch_mv(lin, X, Y, workspace=ws)
+    end.record()
+    torch.cuda.synchronize()
+    secs = start.elapsed_time(end) / 1e3 / reps
+    if world > 1:
+        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    return secs
+
+
 def cpu_reference_gbs(mtype: int, threads: int, budget_s: float, rows_cap=None):
     """The reference's arch/cpu.cpp mv (oracle/_ref) on host cores: GB/s over a
     bounded sample (whole 12288x4096 matvecs until `budget_s` elapses, or a
@@ -339,6 +382,8 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling)")
+    ap.add_argument("--only", choices=["gemv", "gemm"], default=None,
+                    help="run one kernel family only (for profiling; no JSON line)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
@@ -350,6 +395,13 @@ def main(argv=None):
     capi.lib()  # fails loudly without the kernels
     rank, world, local = dist_setup(args.gpus)
     device = torch.device("cuda", torch.cuda.current_device())
+    if args.only == "gemm":
+        for mtype in (1, 2):
+            secs = time_gemm(mtype, 4096, max(args.steps, 1), device, world)
+            if rank == 0:
+                print(f"gemm type={mtype} T=4096: {secs * 1e6:.1f} us "
+                      f"{2 * 4096 * ROWS * COLS / secs / 1e12:.1f} TFLOP/s", flush=True)
+        return 0
 
     secs, launches, clocks = time_gemv(1, args.steps, args.warmup, device, world, rank == 0)
     bytes_q8 = algorithmic_bytes(1)
@@ -370,6 +422,18 @@ def main(argv=None):
     else:
         e2e_secs, e2e_io = time_e2e(1, e2e_steps, args.warmup, device, world)
     e2e_value = world * e2e_steps * COPIES * bytes_q8 / e2e_secs / 1e9
+
+    gemm = {}
+    if args.only is None:
+        peak_tf = measured_tflops()
+        for mtype, name in ((1, "q8_0"), (2, "q4_0")):
+            for T in (1, 8, 64, 512, 4096):
+                secs = time_gemm(mtype, T, 10 if T >= 512 else 50, device, world)
+                tf = world * 2 * T * ROWS * COLS / secs / 1e12
+                gemm[f"{name}_T{T}"] = {"us": round(secs * 1e6, 1), "tflops": round(tf, 1),
+                                        "frac_of_bf16_peak": round(tf / world / peak_tf[0], 4)}
+        gemm["peak_tflops"] = peak_tf[0]
+        gemm["peak_kind"] = peak_tf[1]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -398,6 +462,8 @@ def main(argv=None):
                               "unit": "GB/s", "achieved_per_gpu": round(q4_achieved, 1),
                               "frac": round(q4_achieved / peak, 4),
                               "bytes_per_launch": q4_bytes},
+                "gemm_cfg2": dict(gemm, workload="cfg2: Y[T,12288] = X[T,4096] W^T, dequant-GEMM on "
+                                                  "tcgen05 (FP16 x FP16 -> FP32), T sweep"),
             },
         }
         print(json.dumps(line), flush=True)

@@ -119,6 +119,22 @@ Q3XK_API int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, 
                      int accumulate, void* stream);
 
 /*
+ * Prefill dequant-GEMM on tcgen05: Y[T, rows] = X[T, cols] W^T (accumulate =
+ * 0) or Y += X W^T, all row-major FP32 (Y[t][r] at t * rows + r).  Q8_0/Q4_0
+ * only; cols % 32 == 0.  X is rounded to FP16 with a per-token power-of-two
+ * scale, W to FP16 (d*q), FP32 accumulation; error within 2e-3 of
+ * sum_k |w x| (measured ~1e-4).  `workspace` is a caller-owned DEVICE buffer
+ * of q3xk_gemm_workspace_bytes(T, cols) bytes, 256-byte aligned.
+ * Replaces engine.cu:1568-1597 batch_mv (batch_mv_q8_kernel, engine.cu:751-
+ * 839) and adds the Q4_0 prefill the reference asserts on (engine.cu:1580).
+ */
+Q3XK_API int q3xk_gemm_workspace_bytes(int T, int cols, size_t* bytes);
+Q3XK_API int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate,
+                       void* workspace, size_t workspace_bytes, void* stream);
+/* Device error word of the GEMM kernels (bit 0: a bounded wait gave up). */
+Q3XK_API int q3xk_gemm_device_error(int* flags);
+
+/*
  * Synchronous GEMV on HOST vectors, the contract of q3x_cpu::try_mv
  * (arch/cpu.cpp:192-226): y_host is complete when the call returns.  The
  * matrix stays resident on the device; x_host (cols floats) goes up and

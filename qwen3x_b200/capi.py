@@ -55,6 +55,12 @@ _SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "q3xk_try_mv_host": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "q3xk_gemm_workspace_bytes": (ctypes.c_int, [ctypes.c_int, ctypes.c_int,
+                                                 ctypes.POINTER(ctypes.c_size_t)]),
+    "q3xk_gemm": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
+                                 ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                 ctypes.c_void_p]),
+    "q3xk_gemm_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "q3xk_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "q3xk_clear_device_error": (ctypes.c_int, []),
     "q3xk_launch_count": (ctypes.c_uint64, []),

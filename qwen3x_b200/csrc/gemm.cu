@@ -1,0 +1,547 @@
+// gemm.cu -- prefill dequant-GEMM  Y[T, N] (+)= X[T, K] * W[N, K]^T  on tcgen05.
+//
+// Replaces the reference's CUDA-core batch_mv_q8_kernel (engine.cu:751-839)
+// and adds the Q4_0 prefill the reference lacks (engine.cu:1580-1581 asserts).
+//
+//  * X (FP32) is first converted to FP16 with a per-token power-of-two scale
+//    (x * 2^s_t has its largest magnitude in [2^14, 2^15)), so FP16 cannot
+//    overflow whatever the activations' range; the epilogue multiplies by
+//    2^-s_t exactly.
+//  * One tcgen05.mma tile is 128 weight rows (M, operand A) x 128 tokens (N,
+//    operand B) x 16 K, FP16 x FP16 -> FP32 accumulated in tensor memory.
+//    Operands are K-major in the 128-byte-swizzled layout: B (X16) arrives by
+//    TMA, A is dequantised from the row-record layout by kDqWarps warps straight into
+//    that layout (value = fp16(d * q), one rounding of the exact product).
+//  * Warp roles: 0 TMA producer, 1 MMA issuer (one thread) and TMEM owner,
+//    2..1+kDqWarps dequantisers, then 4 epilogue warps (TMEM -> registers -> Y).
+//    A 4-stage shared-memory ring and two TMEM accumulators let the dequant,
+//    the MMAs and the epilogue of consecutive tiles overlap.  Persistent CTAs
+//    walk the tiles; every mbarrier wait is bounded.
+#include <cuda.h>
+
+#include "tc.cuh"
+
+namespace q3xk {
+namespace {
+
+#ifndef Q3XK_GEMM_DQ_WARPS
+#define Q3XK_GEMM_DQ_WARPS 8
+#endif
+#ifndef Q3XK_GEMM_STAGES
+#define Q3XK_GEMM_STAGES 3
+#endif
+#ifndef Q3XK_GEMM_RAW_STAGES
+#define Q3XK_GEMM_RAW_STAGES 2
+#endif
+
+constexpr int BM = 128;  // weight rows per tile (MMA M)
+constexpr int BK = 64;   // K per stage: 64 FP16 = one 128-byte swizzle row
+constexpr int kStages = Q3XK_GEMM_STAGES;
+constexpr int kAcc = 2;  // TMEM accumulator buffers
+constexpr int kDqWarps = Q3XK_GEMM_DQ_WARPS;   // dequantiser warps
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kEpiWarp0 = 2 + kDqWarps;        // first of 4 epilogue warps
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;
+static_assert(kDqThreads <= 256 && 256 % kDqThreads == 0, "dequant work split");
+constexpr int kTileBytesW = BM * BK * 2;   // 16 KB
+// Raw weights are staged by TMA RAWK columns (4 MMA K-steps) at a time:
+// quants (Q8_0: 256 B per row, Q4_0: 128 B) and the 8 FP16 scales of the
+// 256 columns (16 B per row).
+constexpr int RAWK = 256;
+constexpr int kRawStages = Q3XK_GEMM_RAW_STAGES;
+constexpr int kRawQuantBytes = BM * RAWK;  // sized for Q8_0 (Q4_0 uses half)
+constexpr int kRawScaleBytes = BM * 16;
+constexpr int kRawBytes = kRawQuantBytes + kRawScaleBytes;
+
+__device__ int g_gemm_error;
+
+struct GemmParams {
+    const uint8_t* w;  // row records
+    int64_t row_stride;
+    int64_t qbytes;
+    int N, K, T;
+    const float* tok_scale;  // [T] 2^-s_t
+    float* y;
+    int accumulate;
+    int tiles_w, tiles_t, ksteps;
+};
+
+// Per token-tile-width geometry: BN tokens per tile = MMA N (64, 128, 256).
+template <int BN>
+struct TileN {
+    static constexpr int kTileBytesX = BN * BK * 2;
+    static constexpr uint32_t kTmemCols = kAcc * BN < 32 ? 32 : kAcc * BN;  // power of 2 >= 32
+    static constexpr uint32_t kIdesc = f16_idesc(BM, BN, 0);
+};
+
+// ---- X -> FP16 with a per-token power-of-two scale -----------------------------
+
+__global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ x16,
+                                                       float* __restrict__ tok_scale, int K) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int t = blockIdx.x;
+    const float* row = x + (int64_t)t * K;
+    uint32_t emax = 0;
+    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + k);
+        emax = max(emax, max(max((__float_as_uint(v.x) >> 23) & 0xFFu, (__float_as_uint(v.y) >> 23) & 0xFFu),
+                             max((__float_as_uint(v.z) >> 23) & 0xFFu, (__float_as_uint(v.w) >> 23) & 0xFFu)));
+    }
+    __shared__ uint32_t red[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = emax;
+    __syncthreads();
+    emax = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) emax = max(emax, red[i]);
+    // Largest |x| < 2^(E+1): scale by 2^(14-E) so it lands in [2^14, 2^15).
+    const int E = emax == 0xFFu ? 0 : (int)emax - 127;  // inf/nan stay inf/nan
+    const int s = min(100, max(-100, 14 - E));
+    const float up = __uint_as_float((uint32_t)(s + 127) << 23);
+    if (threadIdx.x == 0) tok_scale[t] = __uint_as_float((uint32_t)(127 - s) << 23);
+    __half2* out = reinterpret_cast<__half2*>(x16 + (int64_t)t * K);
+    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(row + k);
+        out[k / 2] = __floats2half2_rn(v.x * up, v.y * up);
+        out[k / 2 + 1] = __floats2half2_rn(v.z * up, v.w * up);
+    }
+}
+
+// ---- dequantisation into the SW128 K-major layout ------------------------------
+
+// Byte offset of 16-byte chunk c (8 FP16 along K) of row m in a 128-byte-row
+// SWIZZLE_128B tile: chunks are XOR-swizzled with the row index mod 8.
+__device__ __forceinline__ uint32_t sw128_off(int m, int c) {
+    return (uint32_t)(m * 128 + ((c ^ (m & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// 4 bytes of offset-binary Q8 (q + 128) -> 4 FP16 d*q (two half2).
+__device__ __forceinline__ void q8_word(uint32_t w, __half2 d2, uint32_t& o01, uint32_t& o23) {
+    const __half2 bias = u2h(0x64806480u);  // 1024 + 128 in both halves
+    const __half2 h01 = __hsub2(u2h(__byte_perm(w, 0x64646464u, 0x4140)), bias);  // exact q
+    const __half2 h23 = __hsub2(u2h(__byte_perm(w, 0x64646464u, 0x4342)), bias);
+    o01 = h2u(__hmul2(h01, d2));
+    o23 = h2u(__hmul2(h23, d2));
+}
+
+// Two Q4 bytes (b0 in byte 0, b1 in byte 2 of `x`) -> low and high nibbles as
+// exact FP16 (n - 8), multiplied by d.
+__device__ __forceinline__ void q4_pair(uint32_t x, __half2 d2, uint32_t& lo, uint32_t& hi) {
+    const __half2 lo_h = __hsub2(u2h((x & 0x000F000Fu) | 0x64006400u), u2h(0x64086408u));  // 1024+n - 1032
+    // (x & 0xF0) | 0x6400 = 1024 + 16 n; /16 - 72 = n - 8 (exact, one rounding)
+    const __half2 hi_h = __hfma2(u2h((x & 0x00F000F0u) | 0x64006400u), u2h(0x2C002C00u) /* 1/16 */,
+                                 u2h(0xD480D480u) /* -72 */);
+    lo = h2u(__hmul2(lo_h, d2));
+    hi = h2u(__hmul2(hi_h, d2));
+}
+
+template <int TYPE>
+struct Dequant;
+
+// Q8_0: a stage row segment is 64 bytes (4 raw chunks of 16 weights); thread
+// d handles raw chunks d, d+128, d+256, d+384 of the 128x4 chunk grid.
+template <>
+struct Dequant<Q3XK_Q8_0> {
+    static constexpr int kPerThread = 512 / kDqThreads;  // 128 rows x 4 raw chunks
+    static constexpr int kRawRow = RAWK;  // quant bytes per staged row
+    // raw: [128 rows][256 B] quants, then [128 rows][8] FP16 scales.
+    // kk: which 64-column K-step of the 256-column raw stage.
+    __device__ static void run(const uint8_t* raw, uint8_t* dst, int d, int kk) {
+        const uint16_t* scales = reinterpret_cast<const uint16_t*>(raw + kRawQuantBytes);
+#pragma unroll
+        for (int i = 0; i < kPerThread; ++i) {
+            const int idx = d + kDqThreads * i;
+            const int m = idx >> 2, c = idx & 3;  // row in tile, 16-byte raw chunk
+            const int col = kk * BK + 16 * c;     // column within the raw stage
+            const uint4 q = *reinterpret_cast<const uint4*>(raw + m * kRawRow + col);
+            const __half2 d2 = __half2half2(__ushort_as_half(scales[m * 8 + (col >> 5)]));
+            uint4 o0, o1;
+            q8_word(q.x, d2, o0.x, o0.y);
+            q8_word(q.y, d2, o0.z, o0.w);
+            q8_word(q.z, d2, o1.x, o1.y);
+            q8_word(q.w, d2, o1.z, o1.w);
+            *reinterpret_cast<uint4*>(dst + sw128_off(m, 2 * c)) = o0;
+            *reinterpret_cast<uint4*>(dst + sw128_off(m, 2 * c + 1)) = o1;
+        }
+    }
+};
+
+// Q4_0: a stage row segment is 2 blocks = 32 bytes (2 raw chunks of 32
+// weights); element i < 16 of a block is the low nibble of byte i, i >= 16
+// the high nibble of byte i - 16 (q4.h:31-36).
+template <>
+struct Dequant<Q3XK_Q4_0> {
+    static constexpr int kPerThread = 256 / kDqThreads;  // 128 rows x 2 blocks
+    static constexpr int kRawRow = RAWK / 2;
+    __device__ static void run(const uint8_t* raw, uint8_t* dst, int d, int kk) {
+        const uint16_t* scales = reinterpret_cast<const uint16_t*>(raw + kRawQuantBytes);
+#pragma unroll
+        for (int i = 0; i < kPerThread; ++i) {
+            const int idx = d + kDqThreads * i;
+            const int m = idx >> 1, b = idx & 1;  // row in tile, block within the K-step
+            const int blk = kk * 2 + b;           // block within the raw stage
+            const uint4 q = *reinterpret_cast<const uint4*>(raw + m * kRawRow + 16 * blk);
+            const __half2 d2 = __half2half2(__ushort_as_half(scales[m * 8 + blk]));
+            uint32_t l[8], h[8];
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // bytes (4j, 4j+1) and (4j+2, 4j+3) -> elements in order
+                q4_pair(__byte_perm(w[j], 0u, 0x5150), d2, l[2 * j], h[2 * j]);
+                q4_pair(__byte_perm(w[j], 0u, 0x5352), d2, l[2 * j + 1], h[2 * j + 1]);
+            }
+            const int c0 = 4 * b;  // 16-byte FP16 chunk of element 32b within the K-step
+            *reinterpret_cast<uint4*>(dst + sw128_off(m, c0)) = make_uint4(l[0], l[1], l[2], l[3]);
+            *reinterpret_cast<uint4*>(dst + sw128_off(m, c0 + 1)) = make_uint4(l[4], l[5], l[6], l[7]);
+            *reinterpret_cast<uint4*>(dst + sw128_off(m, c0 + 2)) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(dst + sw128_off(m, c0 + 3)) = make_uint4(h[4], h[5], h[6], h[7]);
+        }
+    }
+};
+
+__device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, int* cta_err) {
+    if (mbar_wait_bounded(bar, parity)) return true;
+    atomicOr(&g_gemm_error, 1);
+    atomicExch(cta_err, 1);
+    return false;
+}
+
+template <int TYPE, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap,
+            const __grid_constant__ CUtensorMap smap, const GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    constexpr int kTileBytesX = TileN<BN>::kTileBytesX;
+    constexpr uint32_t kTmemCols = TileN<BN>::kTmemCols;
+    constexpr uint32_t kIdesc = TileN<BN>::kIdesc;
+    uint8_t* sx = smem;                                // kStages x BN x 128 B
+    uint8_t* sw = smem + kStages * kTileBytesX;        // kStages x 16 KB
+    uint8_t* sraw = sw + kStages * kTileBytesW;        // kRawStages x (32 + 2) KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sraw + kRawStages * kRawBytes);
+    uint64_t* full = bars;   // X bytes landed and every dequant warp arrived
+    uint64_t* empty = bars + 2 * kStages;
+    uint64_t* acc_full = bars + 3 * kStages;
+    uint64_t* acc_empty = acc_full + kAcc;
+    uint64_t* raw_full = acc_empty + kAcc;
+    uint64_t* raw_empty = raw_full + kRawStages;
+    uint32_t* tmem_base_p = reinterpret_cast<uint32_t*>(raw_empty + kRawStages);
+    int* cta_err = reinterpret_cast<int*>(tmem_base_p + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1 + kDqWarps);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < kAcc; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        for (int r = 0; r < kRawStages; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], kDqWarps);
+        }
+        *cta_err = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_base_p, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_base_p;
+    griddep_launch_dependents();
+
+    const int tiles = p.tiles_w * p.tiles_t;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: X16 tiles and raw weight stages ----------------
+        griddep_wait();  // X16 is written by the conversion kernel
+        if (lane == 0) {
+            const int qdiv = TYPE == Q3XK_Q4_0 ? 2 : 1;  // quant bytes per column
+            const uint32_t raw_tx = (uint32_t)(BM * (RAWK / qdiv) + kRawScaleBytes);
+            int it = 0, rit = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x) {
+                const int wt = tile / p.tiles_t, tt = tile % p.tiles_t;
+                bool ok = true;
+                for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+                    if (ks % (RAWK / BK) == 0) {
+                        const int r = rit % kRawStages;
+                        if (rit >= kRawStages && !wait_or_flag(&raw_empty[r], ((rit / kRawStages) - 1) & 1, cta_err)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* dst = sraw + r * kRawBytes;
+                        mbar_arrive_expect_tx(&raw_full[r], raw_tx);
+                        tma_load_2d(dst, &qmap, ks * BK / qdiv, wt * BM, &raw_full[r]);
+                        tma_load_2d(dst + kRawQuantBytes, &smap, ks * BK / 32, wt * BM, &raw_full[r]);
+                        ++rit;
+                    }
+                    const int s = it % kStages;
+                    if (it >= kStages && !wait_or_flag(&empty[s], ((it / kStages) - 1) & 1, cta_err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], kTileBytesX);
+                    tma_load_2d(sx + s * kTileBytesX, &xmap, ks * BK, tt * BN, &full[s]);
+                }
+                if (!ok) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int it = 0, lt = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x, ++lt) {
+                const int b = lt % kAcc;
+                if (lt >= kAcc && !wait_or_flag(&acc_empty[b], ((lt / kAcc) - 1) & 1, cta_err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + b * BN;
+                bool ok = true;
+                for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1;
+                    if (!wait_or_flag(&full[s], ph, cta_err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sw + s * kTileBytesW), b0 = smem_u32(sx + s * kTileBytesX);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_f16(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc,
+                                 (ks | kk) ? 1u : 0u);
+                    umma_commit(&empty[s]);  // stage s free once these MMAs finish
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[b]);
+            }
+        }
+    } else if (warp < kEpiWarp0) {
+        // ---------------- dequantisers ----------------
+        const int d = threadIdx.x - 64;
+        int it = 0, rit = 0;
+        for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x) {
+            bool ok = true;
+            for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+                const int kk = ks % (RAWK / BK);
+                const int r = rit % kRawStages;
+                if (kk == 0) {
+                    int good = 1;
+                    if (lane == 0) good = wait_or_flag(&raw_full[r], (rit / kRawStages) & 1, cta_err);
+                    good = __shfl_sync(0xffffffffu, good, 0);
+                    if (!good) {
+                        ok = false;
+                        break;
+                    }
+                }
+                const int s = it % kStages;
+                if (it >= kStages) {
+                    int good = 1;
+                    if (lane == 0) good = wait_or_flag(&empty[s], ((it / kStages) - 1) & 1, cta_err);
+                    good = __shfl_sync(0xffffffffu, good, 0);
+                    if (!good) {
+                        ok = false;
+                        break;
+                    }
+                }
+                Dequant<TYPE>::run(sraw + r * kRawBytes, sw + s * kTileBytesW, d, kk);
+                fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+                if (kk == RAWK / BK - 1 || ks == p.ksteps - 1) {
+                    if (lane == 0) mbar_arrive(&raw_empty[r]);
+                    ++rit;
+                }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ---------------- epilogue (TMEM -> Y) ----------------
+        griddep_wait();  // Y may be read (accumulate) and must not be written early
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x, ++lt) {
+            const int wt = tile / p.tiles_t, tt = tile % p.tiles_t;
+            const int b = lt % kAcc;
+            int good = 1;
+            if (lane == 0) good = wait_or_flag(&acc_full[b], (lt / kAcc) & 1, cta_err);
+            good = __shfl_sync(0xffffffffu, good, 0);
+            if (!good) break;
+            tc_fence_after();
+            const int n = wt * BM + 32 * q + lane;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + b * BN + c0, r);
+                const int t0 = tt * BN + c0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + j;
+                    if (t < p.T && n < p.N) {
+                        const float v = __uint_as_float(r[j]) * __ldg(&p.tok_scale[t]);
+                        float* yp = p.y + (int64_t)t * p.N + n;
+                        *yp = p.accumulate ? *yp + v : v;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+size_t gemm_smem_bytes() {
+    return 1024 /* alignment slack */ + (size_t)kStages * (TileN<256>::kTileBytesX + kTileBytesW) +
+           (size_t)kRawStages * kRawBytes + (size_t)(3 * kStages + 2 * kAcc + 2 * kRawStages) * 8 + 16;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+int sm_count() {
+    static int count = 0;
+    if (!count) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            count = 148;
+    }
+    return count;
+}
+
+}  // namespace
+}  // namespace q3xk
+
+using namespace q3xk;
+
+extern "C" {
+
+int q3xk_gemm_workspace_bytes(int T, int K, size_t* bytes) {
+    if (!bytes || T <= 0 || K <= 0) return Q3XK_EINVAL;
+    *bytes = (((size_t)T * K * 2 + 255) & ~(size_t)255) + (size_t)T * 4;
+    return Q3XK_OK;
+}
+
+int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate, void* workspace,
+              size_t workspace_bytes, void* stream) {
+    if (!w || !w->data || !x || !y || T <= 0 || w->rows <= 0 || w->cols <= 0) return Q3XK_EINVAL;
+    if (w->type != Q3XK_Q8_0 && w->type != Q3XK_Q4_0) return Q3XK_EUNSUPPORTED;
+    if (w->cols % kBlock || w->row_stride != row_record_bytes(w->type, w->cols)) return Q3XK_EINVAL;
+    if (w->cols % 8) return Q3XK_EINVAL;  // TMA row stride of X16 must be a multiple of 16 bytes
+    size_t need = 0;
+    q3xk_gemm_workspace_bytes(T, w->cols, &need);
+    if (!workspace || workspace_bytes < need) return Q3XK_EWORKSPACE;
+    if (((uintptr_t)workspace & 255) || ((uintptr_t)x & 15) || ((uintptr_t)w->data & 15) || ((uintptr_t)y & 3))
+        return Q3XK_EALIGN;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int K = w->cols;
+    __half* x16 = static_cast<__half*>(workspace);
+    float* tok_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (((size_t)T * K * 2 + 255) & ~(size_t)255));
+
+    // Token tile = MMA N: the smallest of 64/128/256 that covers T, else 256.
+    const int bn = T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    EncodeTiled enc = encode_fn();
+    if (!enc) return Q3XK_ECUDA;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {BK, (cuuint32_t)bn};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return Q3XK_ECUDA;
+
+    // Raw weights: the quant bytes of every row record (uint8, [rows][qbytes])
+    // and the scales ([rows][cols/32] FP16), both with the record stride.
+    const int64_t qbytes = quant_bytes(w->type, K);
+    CUtensorMap qmap, smap;
+    {
+        const cuuint64_t qd[2] = {(cuuint64_t)qbytes, (cuuint64_t)w->rows};
+        const cuuint64_t qs[1] = {(cuuint64_t)w->row_stride};
+        const cuuint32_t qb[2] = {(cuuint32_t)(w->type == Q3XK_Q4_0 ? RAWK / 2 : RAWK), BM};
+        if (enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->data, qd, qs, qb, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return Q3XK_ECUDA;
+        const cuuint64_t sd[2] = {(cuuint64_t)(K / kBlock), (cuuint64_t)w->rows};
+        const cuuint32_t sb[2] = {8, BM};
+        if (enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, static_cast<uint8_t*>(w->data) + qbytes, sd, qs, sb, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return Q3XK_ECUDA;
+    }
+
+    const cudaError_t e0 = launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, tok_scale, K);
+    if (e0 != cudaSuccess) return Q3XK_ECUDA;
+    count_launch();
+
+    GemmParams p{};
+    p.w = static_cast<const uint8_t*>(w->data);
+    p.row_stride = w->row_stride;
+    p.qbytes = qbytes;
+    p.N = w->rows;
+    p.K = K;
+    p.T = T;
+    p.tok_scale = tok_scale;
+    p.y = y;
+    p.accumulate = accumulate ? 1 : 0;
+    p.tiles_w = (w->rows + BM - 1) / BM;
+    p.tiles_t = (T + bn - 1) / bn;
+    p.ksteps = (K + BK - 1) / BK;
+    const size_t smem = gemm_smem_bytes();
+    using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+    const int q8 = w->type == Q3XK_Q8_0;
+    const int slot = (q8 ? 0 : 3) + (bn == 64 ? 0 : bn == 128 ? 1 : 2);
+    static const Kern kernels[6] = {gemm_kernel<Q3XK_Q8_0, 64>, gemm_kernel<Q3XK_Q8_0, 128>,
+                                    gemm_kernel<Q3XK_Q8_0, 256>, gemm_kernel<Q3XK_Q4_0, 64>,
+                                    gemm_kernel<Q3XK_Q4_0, 128>, gemm_kernel<Q3XK_Q4_0, 256>};
+    static bool configured[6] = {false, false, false, false, false, false};
+    const Kern kern = kernels[slot];
+    if (!configured[slot]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return Q3XK_ECUDA;
+        configured[slot] = true;
+    }
+    const int tiles = p.tiles_w * p.tiles_t;
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    const cudaError_t e1 = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, qmap, smap, p);
+    if (e1 != cudaSuccess) return Q3XK_ECUDA;
+    count_launch();
+    return last_launch_status();
+}
+
+int q3xk_gemm_device_error(int* flags) {
+    if (!flags) return Q3XK_EINVAL;
+    return cuda_status(cudaMemcpyFromSymbol(flags, g_gemm_error, sizeof(int)));
+}
+
+}  // extern "C"

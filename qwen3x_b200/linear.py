@@ -94,6 +94,26 @@ def expert_mv(linear: Linear, expert: int, x, y, stream=None, accumulate: bool =
                                  int(accumulate), stream_ptr(stream)), "q3xk_expert_gemv")
 
 
+def gemm_workspace_bytes(T: int, cols: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(lib().q3xk_gemm_workspace_bytes(int(T), int(cols), ctypes.byref(out)),
+          "q3xk_gemm_workspace_bytes")
+    return out.value
+
+
+def batch_mv(linear: Linear, X, Y, add: bool = False, workspace=None, stream=None) -> None:
+    """Y[T, rows] (+)= X[T, cols] W^T on tcgen05 (engine.cu:1568 batch_mv)."""
+    import torch
+
+    T = int(X.shape[0])
+    need = gemm_workspace_bytes(T, linear.cols)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
+    nbytes = workspace.numel() * workspace.element_size()
+    check(lib().q3xk_gemm(ctypes.byref(linear.m), ptr(X), T, ptr(Y), int(add), ptr(workspace),
+                          nbytes, stream_ptr(stream)), "q3xk_gemm")
+
+
 def try_mv(linear: Linear, x_host, y_host, workspace, stream=None) -> None:
     """Synchronous y_host = W x_host on host vectors (arch/cpu.cpp:192 try_mv
     contract); `workspace` is a device buffer of >= (cols + rows) floats."""
@@ -102,5 +122,5 @@ def try_mv(linear: Linear, x_host, y_host, workspace, stream=None) -> None:
                                  nbytes, stream_ptr(stream)), "q3xk_try_mv_host")
 
 
-__all__ = ["Linear", "mv", "mv_add", "expert_mv", "try_mv", "quantized_bytes", "BF16", "Q8_0",
-           "Q4_0"]
+__all__ = ["Linear", "mv", "mv_add", "expert_mv", "try_mv", "batch_mv", "gemm_workspace_bytes",
+           "quantized_bytes", "BF16", "Q8_0", "Q4_0"]

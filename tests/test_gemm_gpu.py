@@ -1,0 +1,102 @@
+"""Parity of the tcgen05 dequant-GEMM (q3xk_gemm) with the CPU oracle.
+
+The reference CPU prefill is a per-token mv (engine.cpp:580-583), so the
+oracle of Y[T, N] = X W^T is T independent matvecs.  Bar (north star):
+max |Y - Y_ref| / sum_k |w_nk x_tk| <= 2e-3; FP16 operands with FP32
+accumulation typically land near 1e-4.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from qwen3x_b200 import quant
+from qwen3x_b200.capi import Q4_0, Q8_0
+from qwen3x_b200.linear import Linear, batch_mv
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def run_gemm(cuda, packed, mtype, rows, cols, X, Y0=None):
+    import torch
+
+    lin = Linear.from_packed(packed, mtype, rows, cols, device=cuda)
+    Xd = torch.from_numpy(np.ascontiguousarray(X, np.float32)).to(cuda)
+    if Y0 is None:
+        Yd = torch.full((X.shape[0], rows), float("nan"), device=cuda)
+    else:
+        Yd = torch.from_numpy(np.ascontiguousarray(Y0, np.float32)).to(cuda)
+    batch_mv(lin, Xd, Yd, add=Y0 is not None)
+    torch.cuda.synchronize()
+    return Yd.cpu().numpy()
+
+
+def check(Y, packed, mtype, rows, cols, X, tokens=None, Y0=None):
+    tokens = range(X.shape[0]) if tokens is None else tokens
+    w = np.abs(quant.dequantize(packed, mtype, rows, cols).astype(np.float64))
+    worst = 0.0
+    for t in tokens:
+        ref = oracle.mv(packed, mtype, rows, cols, X[t], threads=8).astype(np.float64)
+        mag = w @ np.abs(X[t].astype(np.float64))
+        if Y0 is not None:
+            ref = ref + Y0[t]
+            mag = mag + np.abs(Y0[t])
+        worst = max(worst, float((np.abs(Y[t] - ref) / np.maximum(mag, 1e-30)).max()))
+    return worst
+
+
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+@pytest.mark.parametrize("T,rows,cols", [(1, 128, 64), (8, 256, 512), (64, 333, 2176),
+                                         (129, 1000, 1024), (300, 128, 4096)])
+def test_gemm_shapes(cuda, mtype, T, rows, cols):
+    packed = quant.quantize(quant.gaussian((rows, cols), rows + cols + T, 0.02), mtype)
+    X = quant.gaussian((T, cols), 7 + T)
+    Y = run_gemm(cuda, packed, mtype, rows, cols, X)
+    assert np.all(np.isfinite(Y))
+    err = check(Y, packed, mtype, rows, cols, X)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+def test_gemm_accumulate(cuda, mtype):
+    T, rows, cols = 40, 256, 1024
+    packed = quant.quantize(quant.gaussian((rows, cols), 3, 0.02), mtype)
+    X = quant.gaussian((T, cols), 4)
+    Y0 = quant.gaussian((T, rows), 5)
+    Y = run_gemm(cuda, packed, mtype, rows, cols, X, Y0)
+    assert check(Y, packed, mtype, rows, cols, X, Y0=Y0) <= TOL
+
+
+def test_gemm_activation_range(cuda):
+    """Per-token scaling keeps FP16 in range for large and tiny activations."""
+    T, rows, cols = 6, 256, 512
+    packed = quant.quantize_q8_0(quant.gaussian((rows, cols), 8, 0.02))
+    X = quant.gaussian((T, cols), 9)
+    X[0] *= 1e6
+    X[1] *= 1e-6
+    X[2, ::3] = 0.0
+    Y = run_gemm(cuda, packed, Q8_0, rows, cols, X)
+    assert check(Y, packed, Q8_0, rows, cols, X) <= TOL
+
+
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+def test_gemm_cfg2_full_size(cuda, mtype):
+    """Benchmark config 2: T=4096, K=4096, N=12288; oracle on 12 sampled tokens."""
+    T, rows, cols = 4096, 12288, 4096
+    packed = quant.quantize(quant.gaussian((rows, cols), 1, 0.02), mtype)
+    X = quant.gaussian((T, cols), 2)
+    Y = run_gemm(cuda, packed, mtype, rows, cols, X)
+    assert np.all(np.isfinite(Y))
+    sample = [0, 1, 127, 128, 129, 1000, 2047, 2048, 3000, 4094, 4095, 511]
+    assert check(Y, packed, mtype, rows, cols, X, tokens=sample) <= TOL
+
+
+def test_gemm_no_device_timeouts(cuda):
+    import ctypes
+
+    from qwen3x_b200.capi import lib
+
+    flags = ctypes.c_int(-1)
+    assert lib().q3xk_gemm_device_error(ctypes.byref(flags)) == 0
+    assert flags.value == 0
