@@ -119,6 +119,43 @@ Q3XK_API int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, 
                      int accumulate, void* stream);
 
 /*
+ * Grouped expert GEMVs over an expert pool (MoE decode), expert ids read on
+ * the device so a whole layer stays inside one CUDA graph:
+ *   rows:     y[s * pool->rows + r] (+)= W[ids[s]][r] . x          (s < slots)
+ *   segments: y[r] (+)= sum_s W[ids[s]][r] . x[s * cols .. (s+1) * cols)
+ * `ids` (int32) and x, y are device pointers; slots <= 16 for segments.
+ * Replace expert_gate_up_q4_kernel (rows) and expert_down_weighted_q4_kernel
+ * (segments, weights folded into x; engine.cu:1186-1250) and the CPU loop of
+ * engine.cpp:412-420.
+ */
+Q3XK_API int q3xk_expert_gemv_rows(const q3xk_matrix* pool, const int* ids, int slots, const float* x,
+                                   float* y, int accumulate, void* stream);
+Q3XK_API int q3xk_expert_gemv_segments(const q3xk_matrix* pool, const int* ids, int slots,
+                                       const float* x, float* y, int accumulate, void* stream);
+
+/*
+ * Router of one token (engine.cpp:377-405; replaces router_top_k_kernel,
+ * engine.cu:1153-1184): softmax over logits[0..experts), greedy top_k
+ * (strict '>', the lowest id wins a tie), weights renormalised over the
+ * selected slots.  With with_shared != 0, logits[experts] is the shared-expert
+ * gate and slot top_k gets id `experts` and weight sigmoid(logit)
+ * (engine.cpp:427-429).  One warp; experts <= 512, top_k <= 8.
+ */
+Q3XK_API int q3xk_router_topk(const float* logits, int experts, int top_k, int with_shared, int* ids,
+                              float* weights, void* stream);
+
+/* out[s][i] = w[s] * silu(g) * u with [g | u] = gate_up[s] (w may be NULL);
+ * engine.cpp:415-416, :424-425. */
+Q3XK_API int q3xk_swiglu(const float* gate_up, const float* weights, int slots, int width, float* out,
+                         void* stream);
+
+/* First index of the maximum of values[0..n) into *out_index (device int);
+ * replaces the host scan of state_argmax (engine.cu:2339-2350). */
+Q3XK_API int q3xk_argmax_workspace_bytes(size_t* bytes);
+Q3XK_API int q3xk_argmax(const float* values, int n, int* out_index, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/*
  * Prefill dequant-GEMM on tcgen05: Y[T, rows] = X[T, cols] W^T (accumulate =
  * 0) or Y += X W^T, all row-major FP32 (Y[t][r] at t * rows + r).  Q8_0/Q4_0
  * only; cols % 32 == 0.  X is rounded to FP16 with a per-token power-of-two

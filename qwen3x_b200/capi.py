@@ -55,6 +55,19 @@ _SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "q3xk_try_mv_host": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "q3xk_expert_gemv_rows": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                             ctypes.c_void_p]),
+    "q3xk_expert_gemv_segments": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
+                                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                 ctypes.c_void_p]),
+    "q3xk_router_topk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xk_swiglu": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xk_argmax_workspace_bytes": (ctypes.c_int, [ctypes.POINTER(ctypes.c_size_t)]),
+    "q3xk_argmax": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                   ctypes.c_size_t, ctypes.c_void_p]),
     "q3xk_gemm_workspace_bytes": (ctypes.c_int, [ctypes.c_int, ctypes.c_int,
                                                  ctypes.POINTER(ctypes.c_size_t)]),
     "q3xk_gemm": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,

@@ -68,9 +68,19 @@ struct GemvParams {
     int64_t qbytes;  // quantised bytes per row (scales follow)
     int rows, cols;
     int accumulate;
-    int units;   // 16-byte units per row
+    int units;   // 16-byte units per (virtual) row
     int ksplit;  // warps sharing a row group (1, 2, 4 or 8), each on a slice of K
+    // Expert gathers (MoE): `ids` (device) picks experts of a pool whose
+    // matrices are `expert_stride` bytes apart.
+    const int* ids;
+    int64_t expert_stride;
+    int rows_per_expert;  // row gather: virtual row r = expert ids[r / rpe], row r % rpe
+    int units_per_seg;    // segment gather: unit u reads expert ids[u / ups]
 };
+
+// Row addressing modes of the GEMV kernel.
+enum GemvMode { kPlain = 0, kRowGather = 1, kSegGather = 2 };
+constexpr int kMaxSegments = 16;
 
 // Per-type geometry and arithmetic.  A unit's x values reach dot() as
 // kChunks float4 in slot order; `gg` = {g, gs}: g = 2^(149-P) rescales
@@ -203,19 +213,26 @@ __device__ __forceinline__ int unit_of(int lane, int b, int i, int kbatch, int k
     return lane + 32 * ((b * kbatch + i) * ksplit + ks);
 }
 
-template <int TYPE, int KS>
+template <int TYPE, int KS, int MODE>
 __device__ __forceinline__ void load_batch(Batch<TYPE>& bt, const GemvParams& p,
-                                           const uint8_t* const* rec, int lane, int b, int ks) {
+                                           const uint8_t* const* rec, int lane, int b, int ks,
+                                           const int64_t* seg_off) {
     constexpr int kBatch = Codec<TYPE>::kBatch;
 #pragma unroll
     for (int i = 0; i < kBatch; ++i) {
-        const int u = unit_of(lane, b, i, kBatch, ks, KS);
+        int u = unit_of(lane, b, i, kBatch, ks, KS);
         if (u < p.units) {
+            int64_t off = 0;
+            if (MODE == kSegGather) {  // unit u of segment u / ups, at that expert's row
+                const int seg = u / p.units_per_seg;
+                off = seg_off[seg];
+                u -= seg * p.units_per_seg;
+            }
 #pragma unroll
             for (int j = 0; j < kRows; ++j) {
-                bt.q[i][j] = ldg_stream(rec[j] + (int64_t)u * 16);
+                bt.q[i][j] = ldg_stream(rec[j] + off + (int64_t)u * 16);
                 if (TYPE != Q3XK_BF16)
-                    bt.d[i][j] = ldg_u16(rec[j] + p.qbytes + 2 * (u / Codec<TYPE>::kUnitsPerBlock));
+                    bt.d[i][j] = ldg_u16(rec[j] + off + p.qbytes + 2 * (u / Codec<TYPE>::kUnitsPerBlock));
             }
         }
     }
@@ -223,10 +240,10 @@ __device__ __forceinline__ void load_batch(Batch<TYPE>& bt, const GemvParams& p,
 
 // Returns this warp's partial sum of row (b4 ? 2 : 0) + (b3 ? 1 : 0) in lanes
 // 0, 8, 16 and 24 (transposed butterfly over the 4 rows).
-template <int TYPE, bool FAST, int KS>
+template <int TYPE, bool FAST, int KS, int MODE>
 __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* const* rec, int lane,
                                            int ks, Batch<TYPE>& A, const float4* xs4,
-                                           const float2* gg) {
+                                           const float2* gg, const int64_t* seg_off) {
     using C = Codec<TYPE>;
     constexpr int kC = C::kChunks;
     constexpr int kBatch = C::kBatch;
@@ -236,7 +253,7 @@ __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* c
     const int span = 32 * kBatch * KS;
     const int nb = (p.units + span - 1) / span;  // batches per row group and slice
     for (int b = 0; b < nb; ++b) {
-        if (b > 0) load_batch<TYPE, KS>(A, p, rec, lane, b, ks);
+        if (b > 0) load_batch<TYPE, KS, MODE>(A, p, rec, lane, b, ks, seg_off);
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
             const int u = unit_of(lane, b, i, kBatch, ks, KS);
@@ -267,7 +284,7 @@ __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* c
     return k;
 }
 
-template <int TYPE, int KS>
+template <int TYPE, int KS, int MODE>
 __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(const GemvParams p) {
     using C = Codec<TYPE>;
     static_assert(kRows == 4, "the transposed row reduction is written for 4 rows");
@@ -282,15 +299,32 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
     constexpr int groups_per_cta = kWarps / KS;  // row groups per CTA
     const int group = warp / KS;
     const int row0 = (blockIdx.x * groups_per_cta + group) * kRows;
+    __shared__ int64_t seg_off[kMaxSegments];
     const uint8_t* rec[kRows];
-#pragma unroll
-    for (int j = 0; j < kRows; ++j) rec[j] = p.w + (int64_t)min(row0 + j, p.rows - 1) * p.row_stride;
-
-    // The first batch of weights is requested before waiting on the previous kernel.
     Batch<TYPE> A;
-    if (row0 < p.rows) load_batch<TYPE, KS>(A, p, rec, lane, 0, ks);
-
-    griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
+    if (MODE == kPlain) {
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) rec[j] = p.w + (int64_t)min(row0 + j, p.rows - 1) * p.row_stride;
+        // The first batch of weights is requested before waiting on the previous kernel.
+        if (row0 < p.rows) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+        griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
+    } else {
+        griddep_wait();  // the expert ids come from the previous kernel
+        if (MODE == kSegGather) {
+            if (tid < p.units / p.units_per_seg) seg_off[tid] = (int64_t)p.ids[tid] * p.expert_stride;
+            __syncthreads();
+        }
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            const int row = min(row0 + j, p.rows - 1);
+            if (MODE == kRowGather)
+                rec[j] = p.w + (int64_t)p.ids[row / p.rows_per_expert] * p.expert_stride +
+                         (int64_t)(row % p.rows_per_expert) * p.row_stride;
+            else
+                rec[j] = p.w + (int64_t)row * p.row_stride;
+        }
+        if (row0 < p.rows) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+    }
 
     // Prescale x per unit into shared memory (16-byte chunks, swizzled).
     int slow = 0;
@@ -342,9 +376,9 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
                                 xu[C::element(4 * j + 2)], xu[C::element(4 * j + 3)]);
         }
         __syncthreads();
-        if (row0 < p.rows) k = warp_rows<TYPE, false, KS>(p, rec, lane, ks, A, xs4, gg);
+        if (row0 < p.rows) k = warp_rows<TYPE, false, KS, MODE>(p, rec, lane, ks, A, xs4, gg, seg_off);
     } else {
-        if (row0 < p.rows) k = warp_rows<TYPE, true, KS>(p, rec, lane, ks, A, xs4, gg);
+        if (row0 < p.rows) k = warp_rows<TYPE, true, KS, MODE>(p, rec, lane, ks, A, xs4, gg, seg_off);
     }
     const int r = (lane & 16 ? 2 : 0) + (lane & 8 ? 1 : 0);
     if (KS == 1) {
@@ -400,11 +434,11 @@ size_t smem_bytes(const GemvParams& p) {
     return (size_t)p.units * Codec<TYPE>::kCols * 4 + (size_t)p.units * 8 + kWarps * kRows * 4;
 }
 
-template <int TYPE, int KS>
+template <int TYPE, int KS, int MODE>
 int launch_ks(const GemvParams& p, size_t smem, cudaStream_t s) {
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
-        if (cudaFuncSetAttribute(gemv_kernel<TYPE, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(gemv_kernel<TYPE, KS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  200 * 1024) != cudaSuccess)
             return Q3XK_ECUDA;
         configured = 200 * 1024;
@@ -412,34 +446,47 @@ int launch_ks(const GemvParams& p, size_t smem, cudaStream_t s) {
     constexpr int rows_per_cta = (kWarps / KS) * kRows;
     const int64_t grid = (p.rows + rows_per_cta - 1) / rows_per_cta;
 #if Q3XK_GEMV_PDL
-    const cudaError_t e = launch_pdl(gemv_kernel<TYPE, KS>, dim3((unsigned)grid), dim3(kThreads), smem, s, p);
+    const cudaError_t e = launch_pdl(gemv_kernel<TYPE, KS, MODE>, dim3((unsigned)grid), dim3(kThreads), smem, s, p);
 #else
-    gemv_kernel<TYPE, KS><<<(unsigned)grid, kThreads, smem, s>>>(p);
+    gemv_kernel<TYPE, KS, MODE><<<(unsigned)grid, kThreads, smem, s>>>(p);
     const cudaError_t e = cudaGetLastError();
 #endif
     return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
 }
 
-template <int TYPE>
+template <int TYPE, int MODE>
 int launch(const GemvParams& p, cudaStream_t s) {
     const size_t smem = smem_bytes<TYPE>(p);
     if (smem > 200 * 1024) return Q3XK_EUNSUPPORTED;
     switch (p.ksplit) {
-    case 1: return launch_ks<TYPE, 1>(p, smem, s);
-    case 2: return launch_ks<TYPE, 2>(p, smem, s);
-    case 4: return launch_ks<TYPE, 4>(p, smem, s);
-    default: return launch_ks<TYPE, 8>(p, smem, s);
+    case 1: return launch_ks<TYPE, 1, MODE>(p, smem, s);
+    case 2: return launch_ks<TYPE, 2, MODE>(p, smem, s);
+    case 4: return launch_ks<TYPE, 4, MODE>(p, smem, s);
+    default: return launch_ks<TYPE, 8, MODE>(p, smem, s);
     }
 }
 
-int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y,
-              int accumulate, cudaStream_t s) {
-    if (!m || !base || !x || !y || m->rows <= 0 || m->cols <= 0) return Q3XK_EINVAL;
+template <int MODE>
+int launch_type(int type, const GemvParams& p, cudaStream_t s) {
+    switch (type) {
+    case Q3XK_Q8_0: return launch<Q3XK_Q8_0, MODE>(p, s);
+    case Q3XK_Q4_0: return launch<Q3XK_Q4_0, MODE>(p, s);
+    default: return launch<Q3XK_BF16, MODE>(p, s);
+    }
+}
+
+int unit_cols(int type) { return type == Q3XK_Q4_0 ? 32 : type == Q3XK_Q8_0 ? 16 : 8; }
+
+int check_matrix(const q3xk_matrix* m) {
+    if (!m || !m->data || m->rows <= 0 || m->cols <= 0) return Q3XK_EINVAL;
     if (m->row_stride != row_record_bytes(m->type, m->cols)) return Q3XK_EINVAL;
-    if (((uintptr_t)base & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
     if (m->type != Q3XK_BF16 && m->type != Q3XK_Q8_0 && m->type != Q3XK_Q4_0) return Q3XK_EINVAL;
     if (m->type != Q3XK_BF16 && m->cols % kBlock) return Q3XK_EINVAL;
     if (m->type == Q3XK_BF16 && m->cols % 8) return Q3XK_EUNSUPPORTED;
+    return Q3XK_OK;
+}
+
+GemvParams base_params(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y, int accumulate) {
     GemvParams p{};
     p.w = base;
     p.x = x;
@@ -449,14 +496,19 @@ int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* 
     p.rows = m->rows;
     p.cols = m->cols;
     p.accumulate = accumulate ? 1 : 0;
-    p.units = m->cols / (m->type == Q3XK_Q4_0 ? 32 : m->type == Q3XK_Q8_0 ? 16 : 8);
+    p.units = m->cols / unit_cols(m->type);
+    p.expert_stride = m->expert_stride;
+    return p;
+}
+
+int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y,
+              int accumulate, cudaStream_t s) {
+    int st = check_matrix(m);
+    if (st != Q3XK_OK || !base || !x || !y) return Q3XK_EINVAL;
+    if (((uintptr_t)base & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
+    GemvParams p = base_params(m, base, x, y, accumulate);
     p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * Q3XK_GEMV_MIN_BLOCKS);
-    int st;
-    switch (m->type) {
-    case Q3XK_Q8_0: st = launch<Q3XK_Q8_0>(p, s); break;
-    case Q3XK_Q4_0: st = launch<Q3XK_Q4_0>(p, s); break;
-    default: st = launch<Q3XK_BF16>(p, s); break;
-    }
+    st = launch_type<kPlain>(m->type, p, s);
     if (st != Q3XK_OK) return st;
     count_launch();
     return last_launch_status();
@@ -481,6 +533,42 @@ int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, float* y,
     if (w->expert_stride != w->row_stride * w->rows) return Q3XK_EINVAL;
     const uint8_t* base = static_cast<const uint8_t*>(w->data) + (int64_t)expert * w->expert_stride;
     return gemv_impl(w, base, x, y, accumulate, static_cast<cudaStream_t>(stream));
+}
+
+int q3xk_expert_gemv_rows(const q3xk_matrix* pool, const int* ids, int slots, const float* x, float* y,
+                          int accumulate, void* stream) {
+    int st = check_matrix(pool);
+    if (st != Q3XK_OK || !ids || !x || !y || slots <= 0) return Q3XK_EINVAL;
+    if (pool->expert_stride != pool->row_stride * pool->rows) return Q3XK_EINVAL;
+    if (((uintptr_t)pool->data & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
+    GemvParams p = base_params(pool, static_cast<const uint8_t*>(pool->data), x, y, accumulate);
+    p.ids = ids;
+    p.rows_per_expert = pool->rows;
+    p.rows = pool->rows * slots;
+    p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * Q3XK_GEMV_MIN_BLOCKS);
+    st = launch_type<kRowGather>(pool->type, p, static_cast<cudaStream_t>(stream));
+    if (st != Q3XK_OK) return st;
+    count_launch();
+    return last_launch_status();
+}
+
+int q3xk_expert_gemv_segments(const q3xk_matrix* pool, const int* ids, int slots, const float* x, float* y,
+                              int accumulate, void* stream) {
+    int st = check_matrix(pool);
+    if (st != Q3XK_OK || !ids || !x || !y || slots <= 0) return Q3XK_EINVAL;
+    if (slots > kMaxSegments) return Q3XK_EUNSUPPORTED;
+    if (pool->expert_stride != pool->row_stride * pool->rows) return Q3XK_EINVAL;
+    if (((uintptr_t)pool->data & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
+    GemvParams p = base_params(pool, static_cast<const uint8_t*>(pool->data), x, y, accumulate);
+    p.ids = ids;
+    p.units_per_seg = p.units;
+    p.units = p.units * slots;
+    p.cols = pool->cols * slots;
+    p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * Q3XK_GEMV_MIN_BLOCKS);
+    st = launch_type<kSegGather>(pool->type, p, static_cast<cudaStream_t>(stream));
+    if (st != Q3XK_OK) return st;
+    count_launch();
+    return last_launch_status();
 }
 
 int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* y_host, void* workspace,

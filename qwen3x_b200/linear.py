@@ -94,6 +94,43 @@ def expert_mv(linear: Linear, expert: int, x, y, stream=None, accumulate: bool =
                                  int(accumulate), stream_ptr(stream)), "q3xk_expert_gemv")
 
 
+def expert_mv_rows(pool: Linear, ids, slots: int, x, y, accumulate=False, stream=None) -> None:
+    """y[s*rows + r] (+)= W[ids[s]][r] . x for s < slots; ids on the device."""
+    check(lib().q3xk_expert_gemv_rows(ctypes.byref(pool.m), ptr(ids), int(slots), ptr(x), ptr(y),
+                                      int(accumulate), stream_ptr(stream)), "q3xk_expert_gemv_rows")
+
+
+def expert_mv_segments(pool: Linear, ids, slots: int, x, y, accumulate=False, stream=None) -> None:
+    """y[r] (+)= sum_s W[ids[s]][r] . x[s*cols:(s+1)*cols]; ids on the device."""
+    check(lib().q3xk_expert_gemv_segments(ctypes.byref(pool.m), ptr(ids), int(slots), ptr(x), ptr(y),
+                                          int(accumulate), stream_ptr(stream)),
+          "q3xk_expert_gemv_segments")
+
+
+def router_top_k(logits, experts: int, top_k: int, ids, weights, with_shared=False,
+                 stream=None) -> None:
+    """engine.cpp:377-405 on the device (+ the shared-expert gate slot)."""
+    check(lib().q3xk_router_topk(ptr(logits), int(experts), int(top_k), int(with_shared), ptr(ids),
+                                 ptr(weights), stream_ptr(stream)), "q3xk_router_topk")
+
+
+def swiglu(gate_up, weights, slots: int, width: int, out, stream=None) -> None:
+    check(lib().q3xk_swiglu(ptr(gate_up), ptr(weights), int(slots), int(width), ptr(out),
+                            stream_ptr(stream)), "q3xk_swiglu")
+
+
+def argmax(values, n: int, out_index, workspace=None, stream=None) -> None:
+    import torch
+
+    if workspace is None:
+        need = ctypes.c_size_t(0)
+        check(lib().q3xk_argmax_workspace_bytes(ctypes.byref(need)), "q3xk_argmax_workspace_bytes")
+        workspace = torch.empty(need.value, dtype=torch.uint8, device=values.device)
+    check(lib().q3xk_argmax(ptr(values), int(n), ptr(out_index), ptr(workspace),
+                            workspace.numel() * workspace.element_size(), stream_ptr(stream)),
+          "q3xk_argmax")
+
+
 def gemm_workspace_bytes(T: int, cols: int) -> int:
     out = ctypes.c_size_t(0)
     check(lib().q3xk_gemm_workspace_bytes(int(T), int(cols), ctypes.byref(out)),
@@ -123,4 +160,5 @@ def try_mv(linear: Linear, x_host, y_host, workspace, stream=None) -> None:
 
 
 __all__ = ["Linear", "mv", "mv_add", "expert_mv", "try_mv", "batch_mv", "gemm_workspace_bytes",
+           "expert_mv_rows", "expert_mv_segments", "router_top_k", "swiglu", "argmax",
            "quantized_bytes", "BF16", "Q8_0", "Q4_0"]
