@@ -1,0 +1,103 @@
+/*
+ * q3x_backend.h -- the qwen3x compute-backend interface, implemented on B200.
+ *
+ * Part 1 (C++) is the reference's opaque backend API with the same names,
+ * signatures and semantics (internal.h:11-34, namespace q3x_backend), so the
+ * reference's runtime.cpp (Session, CLI, HTTP server) links against this
+ * library in place of engine.cpp / arch/cuda/engine.cu.  As in the reference,
+ * invalid arguments are fatal (the reference's Q3X_ASSERT reports and aborts).
+ *
+ * Part 2 (C) is the same operations as a C ABI with status codes instead of
+ * aborts, for FFI callers (Python ctypes in this repository's tests and
+ * benchmark).  Statuses are q3xk_status values (q3xk.h).
+ *
+ * One Model and its States live on the device that is current when
+ * model_create is called; every later call sets that device itself.
+ */
+#ifndef Q3X_BACKEND_H
+#define Q3X_BACKEND_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "q3xk.h"
+
+#ifdef __cplusplus
+namespace q3x_backend {
+
+struct Model;
+struct State;
+
+/* internal.h:16-17; model.bin is mmapped, checked (magic, registered model
+ * ID, header fields, schema size; the reference's error strings) and its
+ * matrices uploaded once in the device row-record layout. */
+Q3XK_API Model* model_create(const char* path, char* err, size_t errlen);
+Q3XK_API void model_destroy(Model* model);
+
+/* internal.h:19-30. */
+Q3XK_API State* state_create(Model* model, int context_size);
+Q3XK_API void state_destroy(State* state);
+Q3XK_API void state_reset(State* state);
+Q3XK_API void state_forward(Model* model, State* state, const int* tokens, int count, bool compute_logits);
+Q3XK_API void state_checkpoint_save(State* state);
+Q3XK_API void state_checkpoint_restore(State* state);
+Q3XK_API int state_argmax(const State* state);
+Q3XK_API void state_copy_logits(const State* state, float* output);
+Q3XK_API uint32_t model_id(const Model* model);
+
+/* internal.h:32-34 (constants of the registered Qwen family). */
+Q3XK_API int vocab_size();
+Q3XK_API int max_context();
+Q3XK_API bool token_is_stop(int token);
+
+}  // namespace q3x_backend
+
+extern "C" {
+#endif
+
+typedef struct q3xb_model q3xb_model;
+typedef struct q3xb_state q3xb_state;
+
+/* Model handles: NULL on failure with the reason in err. */
+Q3XK_API q3xb_model* q3xb_model_create(const char* path, char* err, size_t errlen);
+Q3XK_API void q3xb_model_destroy(q3xb_model* model);
+Q3XK_API uint32_t q3xb_model_id(const q3xb_model* model);
+/* The 16 header fields of the model's configuration followed by experts,
+ * top_k, shared_I, matrix_type, tied (21 ints). */
+Q3XK_API int q3xb_model_config(const q3xb_model* model, int* fields21);
+/* Device bytes the model's weights occupy. */
+Q3XK_API size_t q3xb_model_device_bytes(const q3xb_model* model);
+
+/* State: context_size in 1..262144.  NULL on failure (err filled). */
+Q3XK_API q3xb_state* q3xb_state_create(q3xb_model* model, int context_size, char* err, size_t errlen);
+Q3XK_API void q3xb_state_destroy(q3xb_state* state);
+Q3XK_API int q3xb_state_reset(q3xb_state* state);
+/* tokens: host int32[count]; returns once the work is queued on the
+ * state's stream (logits/argmax calls synchronise). */
+Q3XK_API int q3xb_state_forward(q3xb_model* model, q3xb_state* state, const int* tokens, int count,
+                                int compute_logits);
+Q3XK_API int q3xb_state_checkpoint_save(q3xb_state* state);
+Q3XK_API int q3xb_state_checkpoint_restore(q3xb_state* state);
+Q3XK_API int q3xb_state_argmax(const q3xb_state* state, int* token);
+Q3XK_API int q3xb_state_copy_logits(const q3xb_state* state, float* output);
+Q3XK_API int q3xb_state_position(const q3xb_state* state);
+/* Blocks until the state's queued work is done; returns its CUDA status. */
+Q3XK_API int q3xb_state_synchronize(const q3xb_state* state);
+/* The CUDA stream the state's work runs on (cudaStream_t). */
+Q3XK_API void* q3xb_state_stream(const q3xb_state* state);
+/* 1 = decode steps (count 1 with logits) replay one captured CUDA graph
+ * (default); 0 = launch them one by one. */
+Q3XK_API int q3xb_state_set_graphs(q3xb_state* state, int enabled);
+/* 1 = prompts (count > 1) run every matrix through the CUDA-core GEMV, one
+ * token at a time, with the decode path's FP32 accuracy; 0 (default) = the
+ * tcgen05 dequant-GEMM with FP16 operands. */
+Q3XK_API int q3xb_state_set_exact_prefill(q3xb_state* state, int enabled);
+/* Tokens per forward pass of a prompt, 1..min(context, 2048) (the default is
+ * the maximum; the work buffers are sized for it at state creation). */
+Q3XK_API int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens);
+
+#ifdef __cplusplus
+}  // extern "C"
+#endif
+
+#endif /* Q3X_BACKEND_H */

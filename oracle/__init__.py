@@ -66,6 +66,7 @@ _REF_SIGS = {
     "q3xref_state_checkpoint_save": (None, [_p]),
     "q3xref_state_checkpoint_restore": (None, [_p]),
     "q3xref_model_id": (_u32, [_p]),
+    "q3xref_model_create_custom": (_p, [ctypes.c_char_p, _p, ctypes.c_char_p, _sz]),
 }
 
 _port = None
@@ -116,6 +117,68 @@ def reference():
             return None
         _ref = _bind(ctypes.CDLL(str(path)), _REF_SIGS)
     return _ref
+
+
+class RefEngine:
+    """The reference CPU forward (engine.cpp) on a model.bin, through oracle/_ref.
+
+    `config` (a qwen3x_b200.modelfile.ModelConfig) is needed for model IDs the
+    reference does not register; the tensor walk is then ref_shim.cpp's
+    restatement of Model::load."""
+
+    def __init__(self, path, config=None, context=512):
+        self.lib = reference()
+        if self.lib is None:
+            raise RuntimeError("oracle/_ref was not built")
+        err = ctypes.create_string_buffer(256)
+        if config is None:
+            self.model = self.lib.q3xref_model_create(str(path).encode(), err, 256)
+            self.vocab = 248320
+        else:
+            c = config
+            f = np.array([c.id, c.V, c.H, c.I, c.N, c.AI, c.AH, c.KVH, c.AD, c.RD, c.KH, c.VH, c.KD,
+                          c.VD, c.CK, c.experts, c.top_k, c.shared_I, c.matrix_type, int(c.tied)],
+                         np.int32)
+            self.model = self.lib.q3xref_model_create_custom(str(path).encode(), f.ctypes.data, err, 256)
+            self.vocab = c.V
+        if not self.model:
+            raise RuntimeError(err.value.decode())
+        self.state = self.lib.q3xref_state_create(self.model, context)
+
+    def forward(self, tokens, logits=True):
+        t = np.ascontiguousarray(tokens, np.int32)
+        self.lib.q3xref_state_forward(self.model, self.state, t.ctypes.data, t.size, int(logits))
+
+    def logits(self):
+        out = np.empty(self.vocab, np.float32)
+        self.lib.q3xref_state_copy_logits(self.state, out.ctypes.data)
+        return out
+
+    def argmax(self):
+        return self.lib.q3xref_state_argmax(self.state)
+
+    def reset(self):
+        self.lib.q3xref_state_reset(self.state)
+
+    def checkpoint_save(self):
+        self.lib.q3xref_state_checkpoint_save(self.state)
+
+    def checkpoint_restore(self):
+        self.lib.q3xref_state_checkpoint_restore(self.state)
+
+    def close(self):
+        if self.state:
+            self.lib.q3xref_state_destroy(self.state)
+            self.state = None
+        if self.model:
+            self.lib.q3xref_model_destroy(self.model)
+            self.model = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _a(arr):

@@ -163,3 +163,108 @@ uint32_t q3xref_model_id(void* model) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Custom-shape models for the parity tests.  Model::load only accepts the
+// registered model IDs (model_config.h:104-113); the tests also use small
+// models with the real head sizes.  This binds a model.bin written for a
+// caller-given ModelConfig with the same tensor walk as Model::load
+// (engine.cpp:481-559), then the unmodified reference forward runs on it.
+namespace {
+
+bool load_custom(q3x_backend::Model& m, const char* path, const q3x_model::ModelConfig* cfg,
+                 const char** error) {
+    using namespace q3x_backend;
+    auto fail = [&](const char* message) { *error = message; return false; };
+    m.fd = open(path, O_RDONLY);
+    struct stat info {};
+    if (m.fd < 0) return fail("cannot open model.bin");
+    if (fstat(m.fd, &info) || info.st_size < static_cast<off_t>(q3x_model::HEADER_SIZE))
+        return fail("bad model.bin");
+    m.file_size = static_cast<size_t>(info.st_size);
+    m.file = static_cast<const uint8_t*>(mmap(nullptr, m.file_size, PROT_READ, MAP_PRIVATE, m.fd, 0));
+    if (m.file == MAP_FAILED) { m.file = nullptr; return fail("mmap model.bin failed"); }
+    if (std::memcmp(m.file, "Q3XMODL\0", 8) != 0) return fail("wrong model.bin magic");
+    if (!q3x_model::header_matches(m.file, m.file_size, *cfg)) return fail("Qwen model.bin header mismatch");
+    m.config = cfg;
+    const auto& c = *cfg;
+    size_t cursor = q3x_model::HEADER_SIZE;
+    const int AS = c.AH * c.AD, KVW = c.KVH * c.AD;
+    const int DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO;
+    auto linear = [&](int rows, int cols, q3x_model::MatrixType type) {
+        if (type == q3x_model::MATRIX_BF16)
+            return Linear {take<BF16>(m.file, m.file_size, cursor, static_cast<size_t>(rows) * cols, error),
+                           rows, cols, type};
+        size_t bytes = 0;
+        if (!*error && !q3x_cpu::quantized_bytes(type, rows, cols, &bytes)) *error = "invalid quantized matrix layout";
+        return Linear {take<uint8_t>(m.file, m.file_size, cursor, bytes, error), rows, cols, type};
+    };
+    auto model_linear = [&](int rows, int cols) { return linear(rows, cols, c.matrix_type); };
+    auto expert = [&](int rows, int cols) {
+        const Linear all = model_linear(c.experts * rows, cols);
+        return ExpertLinear {all.w, c.experts, rows, cols, all.type};
+    };
+    m.layer.reset(new (std::nothrow) Layer[c.N]);
+    if (!m.layer) return fail("cannot allocate model layer table");
+    m.embedding = model_linear(c.V, c.H);
+    m.lm_head = c.tied_embeddings ? m.embedding : model_linear(c.V, c.H);
+    m.final_norm = take<BF16>(m.file, m.file_size, cursor, c.H, error);
+    for (int i = 0; i < c.N; ++i) {
+        Layer& l = m.layer[i];
+        l.input_norm = take<BF16>(m.file, m.file_size, cursor, c.H, error);
+        if (i % c.AI != c.AI - 1) {
+            l.delta.qkv = model_linear(DQKV, c.H); l.delta.z = model_linear(DO, c.H);
+            l.delta.a = model_linear(c.VH, c.H); l.delta.b = model_linear(c.VH, c.H);
+            l.delta.conv = take<BF16>(m.file, m.file_size, cursor, static_cast<size_t>(DQKV) * c.CK, error);
+            l.delta.alog = take<FP32>(m.file, m.file_size, cursor, c.VH, error);
+            l.delta.dt = take<BF16>(m.file, m.file_size, cursor, c.VH, error);
+            l.delta.norm = take<FP32>(m.file, m.file_size, cursor, c.VD, error);
+            l.delta.out = model_linear(c.H, DO);
+        } else {
+            l.attention.q = model_linear(2 * AS, c.H); l.attention.k = model_linear(KVW, c.H);
+            l.attention.v = model_linear(KVW, c.H);
+            l.attention.qnorm = take<BF16>(m.file, m.file_size, cursor, c.AD, error);
+            l.attention.knorm = take<BF16>(m.file, m.file_size, cursor, c.AD, error);
+            l.attention.out = model_linear(c.H, AS);
+        }
+        l.post_norm = take<BF16>(m.file, m.file_size, cursor, c.H, error);
+        if (c.experts) {
+            l.moe.router = linear(c.experts, c.H, q3x_model::MATRIX_BF16);
+            l.moe.gate_up = expert(2 * c.I, c.H);
+            l.moe.down = expert(c.H, c.I);
+            l.moe.shared_gate = model_linear(c.shared_I, c.H);
+            l.moe.shared_up = model_linear(c.shared_I, c.H);
+            l.moe.shared_down = model_linear(c.H, c.shared_I);
+            l.moe.shared_scale = linear(1, c.H, q3x_model::MATRIX_BF16);
+        } else {
+            l.gate = model_linear(c.I, c.H);
+            l.up = model_linear(c.I, c.H); l.down = model_linear(c.H, c.I);
+        }
+    }
+    if (*error) return false;
+    if (cursor != m.file_size) return fail("model.bin size does not match schema");
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+// fields: id V H I N AI AH KVH AD RD KH VH KD VD CK experts top_k shared_I matrix_type tied
+void* q3xref_model_create_custom(const char* path, const int* f, char* err, size_t errlen) {
+    auto* cfg = new q3x_model::ModelConfig {
+        static_cast<uint32_t>(f[0]), "custom", f[1], f[2], f[3], f[4], f[5], f[6], f[7], f[8], f[9],
+        f[10], f[11], f[12], f[13], f[14], f[15], f[16], f[17],
+        static_cast<q3x_model::MatrixType>(f[18]), f[19] != 0,
+    };
+    std::unique_ptr<q3x_backend::Model> model(new (std::nothrow) q3x_backend::Model());
+    const char* message = nullptr;
+    if (!model || !load_custom(*model, path, cfg, &message)) {
+        if (err && errlen) std::snprintf(err, errlen, "%s", message ? message : "allocation failed");
+        return nullptr;
+    }
+    if (err && errlen) err[0] = '\0';
+    return model.release();
+}
+
+}  // extern "C"

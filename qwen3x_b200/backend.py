@@ -1,0 +1,134 @@
+"""Python mirror of the qwen3x backend interface (internal.h:11-34) over the C ABI
+of include/q3x_backend.h.
+
+    model = Model("model.bin")            # q3x_backend::model_create
+    state = State(model, context=4096)    # q3x_backend::state_create
+    state.forward(prompt)                 # state_forward(..., compute_logits=True)
+    token = state.argmax()                # state_argmax
+    logits = state.logits()               # state_copy_logits
+
+Errors raise (the reference aborts through Q3X_ASSERT); there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import capi
+
+FIELDS = ("id", "V", "H", "I", "N", "AI", "AH", "KVH", "AD", "RD", "KH", "VH", "KD", "VD", "CK",
+          "context", "experts", "top_k", "shared_I", "matrix_type", "tied")
+
+
+class Model:
+    def __init__(self, path):
+        self.lib = capi.lib()
+        err = ctypes.create_string_buffer(256)
+        self.handle = self.lib.q3xb_model_create(str(path).encode(), err, 256)
+        if not self.handle:
+            raise RuntimeError(f"model_create: {err.value.decode()}")
+        f = (ctypes.c_int * 21)()
+        capi.check(self.lib.q3xb_model_config(self.handle, f), "q3xb_model_config")
+        self.config = dict(zip(FIELDS, list(f)))
+
+    @property
+    def id(self) -> int:
+        return self.lib.q3xb_model_id(self.handle)
+
+    @property
+    def vocab(self) -> int:
+        return self.config["V"]
+
+    @property
+    def device_bytes(self) -> int:
+        return self.lib.q3xb_model_device_bytes(self.handle)
+
+    def close(self):
+        if self.handle:
+            self.lib.q3xb_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class State:
+    def __init__(self, model: Model, context: int):
+        self.model = model
+        self.lib = model.lib
+        err = ctypes.create_string_buffer(256)
+        self.handle = self.lib.q3xb_state_create(model.handle, int(context), err, 256)
+        if not self.handle:
+            raise RuntimeError(f"state_create: {err.value.decode()}")
+
+    def forward(self, tokens, compute_logits: bool = True):
+        t = np.ascontiguousarray(np.atleast_1d(tokens), dtype=np.int32)
+        capi.check(self.lib.q3xb_state_forward(self.model.handle, self.handle, t.ctypes.data, t.size,
+                                               int(compute_logits)), "state_forward")
+
+    def argmax(self) -> int:
+        out = ctypes.c_int(-1)
+        capi.check(self.lib.q3xb_state_argmax(self.handle, ctypes.byref(out)), "state_argmax")
+        return out.value
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.model.vocab, np.float32)
+        capi.check(self.lib.q3xb_state_copy_logits(self.handle, out.ctypes.data), "state_copy_logits")
+        return out
+
+    def reset(self):
+        capi.check(self.lib.q3xb_state_reset(self.handle), "state_reset")
+
+    def checkpoint_save(self):
+        capi.check(self.lib.q3xb_state_checkpoint_save(self.handle), "state_checkpoint_save")
+
+    def checkpoint_restore(self):
+        capi.check(self.lib.q3xb_state_checkpoint_restore(self.handle), "state_checkpoint_restore")
+
+    @property
+    def position(self) -> int:
+        return self.lib.q3xb_state_position(self.handle)
+
+    @property
+    def stream(self) -> int:
+        return self.lib.q3xb_state_stream(self.handle) or 0
+
+    def synchronize(self):
+        capi.check(self.lib.q3xb_state_synchronize(self.handle), "state_synchronize")
+
+    def set_graphs(self, enabled: bool):
+        capi.check(self.lib.q3xb_state_set_graphs(self.handle, int(enabled)), "state_set_graphs")
+
+    def set_exact_prefill(self, enabled: bool):
+        capi.check(self.lib.q3xb_state_set_exact_prefill(self.handle, int(enabled)),
+                   "state_set_exact_prefill")
+
+    def set_prefill_chunk(self, tokens: int):
+        capi.check(self.lib.q3xb_state_set_prefill_chunk(self.handle, int(tokens)),
+                   "state_set_prefill_chunk")
+
+    def generate(self, prompt, steps: int):
+        """Greedy decode: forward(prompt), then `steps` tokens fed back one at
+        a time (runtime.cpp's greedy loop).  Returns the generated tokens."""
+        self.forward(prompt)
+        out = []
+        for _ in range(steps):
+            tok = self.argmax()
+            out.append(tok)
+            self.forward([tok])
+        return out
+
+    def close(self):
+        if self.handle:
+            self.lib.q3xb_state_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

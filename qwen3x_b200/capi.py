@@ -78,6 +78,28 @@ _SIGNATURES = {
     "q3xk_clear_device_error": (ctypes.c_int, []),
     "q3xk_launch_count": (ctypes.c_uint64, []),
     "q3xk_reset_launch_count": (None, []),
+    # q3x_backend.h, C part
+    "q3xb_model_create": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "q3xb_model_destroy": (None, [ctypes.c_void_p]),
+    "q3xb_model_id": (ctypes.c_uint32, [ctypes.c_void_p]),
+    "q3xb_model_config": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xb_model_device_bytes": (ctypes.c_size_t, [ctypes.c_void_p]),
+    "q3xb_state_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p,
+                                            ctypes.c_size_t]),
+    "q3xb_state_destroy": (None, [ctypes.c_void_p]),
+    "q3xb_state_reset": (ctypes.c_int, [ctypes.c_void_p]),
+    "q3xb_state_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_int, ctypes.c_int]),
+    "q3xb_state_checkpoint_save": (ctypes.c_int, [ctypes.c_void_p]),
+    "q3xb_state_checkpoint_restore": (ctypes.c_int, [ctypes.c_void_p]),
+    "q3xb_state_argmax": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "q3xb_state_copy_logits": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xb_state_position": (ctypes.c_int, [ctypes.c_void_p]),
+    "q3xb_state_synchronize": (ctypes.c_int, [ctypes.c_void_p]),
+    "q3xb_state_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "q3xb_state_set_graphs": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "q3xb_state_set_exact_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "q3xb_state_set_prefill_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
 }
 
 
@@ -90,7 +112,7 @@ def lib():
             raise RuntimeError(
                 f"{path} is missing: build it with `python -m qwen3x_b200.build` "
                 "(the qwen3x_b200 kernels have no CPU fallback)")
-        handle = ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+        handle = ctypes.CDLL(path)
         for name, (res, args) in _SIGNATURES.items():
             fn = getattr(handle, name, None)
             if fn is None:

@@ -1,0 +1,857 @@
+// engine.cu -- the qwen3x backend on one B200: model.bin load, state, forward.
+//
+// Implements q3x_backend (internal.h:11-34) and its C mirror (q3x_backend.h).
+// The forward follows the reference CPU engine (engine.cpp:406-458) layer by
+// layer, with every matrix product on the packed-weight path:
+//   T == 1   q3xk_gemv (CUDA cores, HBM-bound; residual adds fused as y += W x)
+//   T >  1   q3xk_gemm (tcgen05 dequant-GEMM) for Q8_0/Q4_0 models
+//   MoE      router GEMV -> device top-k -> grouped expert GEMVs over pools
+//            that hold the shared expert as one more expert (engine.cpp:406-430)
+//   logits   rms of the last token -> lm_head GEMV; argmax on the device.
+// Matrices that read the same input are stored as one matrix (row
+// concatenation), so a DeltaNet layer reads its input once for qkv|z|a|b,
+// attention once for q|k|v, the FFN once for gate|up.
+//
+// Device layout: one arena holds every weight (row-record matrices, FP32
+// norms with the 1 + w' folded in); a State owns the recurrent arena (conv
+// history + DeltaNet memory of every DeltaNet layer, as engine.cpp:126-160),
+// the KV cache, the logits and chunk-sized work buffers.  Positions live in
+// device memory, so a decode step (count 1, logits) is one CUDA graph replay.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <new>
+#include <vector>
+
+#include "layers.cuh"
+#include "q3x_backend.h"
+
+namespace q3xk {
+namespace {
+
+constexpr int kMaxContext = 262144;                 // model_config.h:13
+constexpr size_t kHeaderSize = 8 + 16 * 4;          // model_config.h:10-12
+constexpr int kEndOfText = 248044, kImEnd = 248046;  // engine.cpp:28
+constexpr int kChunk = 2048;                        // prefill tokens per pass
+constexpr int kAttnSplits = 32;                     // key splits of decode attention
+constexpr size_t kAlign = 256;
+
+struct Config {
+    uint32_t id;
+    const char* name;
+    int V, H, I, N, AI, AH, KVH, AD, RD, KH, VH, KD, VD, CK;
+    int experts, top_k, shared_I;
+    int matrix_type;
+    bool tied;
+};
+
+// model_config.h:59-101 (registered IDs) plus the IDs this build adds: a
+// Q8_0 27B-shaped model and three small test models with the real head sizes.
+const Config kConfigs[] = {
+    {800, "Qwen3.5-0.8B", 248320, 1024, 3584, 24, 4, 8, 2, 256, 64, 16, 16, 128, 128, 4, 0, 0, 0, Q3XK_BF16, true},
+    {4000, "Qwen3.5-4B", 248320, 2560, 9216, 32, 4, 16, 4, 256, 64, 16, 32, 128, 128, 4, 0, 0, 0, Q3XK_BF16, true},
+    {9000, "Qwen3.5-9B", 248320, 4096, 12288, 32, 4, 16, 4, 256, 64, 16, 32, 128, 128, 4, 0, 0, 0, Q3XK_Q8_0, false},
+    {36035, "Qwen3.6-35B-A3B", 248320, 2048, 512, 40, 4, 16, 2, 256, 64, 16, 32, 128, 128, 4, 256, 8, 512,
+     Q3XK_Q4_0, false},
+    {38027, "Qwen3.8-27B", 248320, 5120, 17408, 64, 4, 24, 4, 256, 64, 16, 48, 128, 128, 4, 0, 0, 0, Q3XK_Q4_0,
+     false},
+    {27008, "27B-shaped Q8_0", 248320, 5120, 17408, 64, 4, 24, 4, 256, 64, 16, 48, 128, 128, 4, 0, 0, 0, Q3XK_Q8_0,
+     false},
+    {9091, "test dense Q8_0", 4096, 512, 1024, 8, 4, 2, 1, 256, 64, 2, 4, 128, 128, 4, 0, 0, 0, Q3XK_Q8_0, false},
+    {9092, "test dense Q4_0", 4096, 512, 1024, 4, 4, 2, 1, 256, 64, 2, 4, 128, 128, 4, 0, 0, 0, Q3XK_Q4_0, false},
+    {35091, "test MoE Q4_0", 4096, 512, 128, 4, 4, 2, 1, 256, 64, 2, 4, 128, 128, 4, 16, 4, 128, Q3XK_Q4_0, false},
+};
+
+const Config* config_for_id(uint32_t id) {
+    for (const Config& c : kConfigs)
+        if (c.id == id) return &c;
+    return nullptr;
+}
+
+uint32_t header_field(const uint8_t* file, int i) {
+    uint32_t v;
+    std::memcpy(&v, file + 8 + 4 * (size_t)i, 4);
+    return v;
+}
+
+// model_config.h:107-133
+bool header_matches(const uint8_t* file, const Config& c) {
+    const uint32_t expect[16] = {c.id,         (uint32_t)c.V,   (uint32_t)c.H,   (uint32_t)c.I,  (uint32_t)c.N,
+                                 (uint32_t)c.AI, (uint32_t)c.AH,  (uint32_t)c.KVH, (uint32_t)c.AD, (uint32_t)c.RD,
+                                 (uint32_t)c.KH, (uint32_t)c.VH,  (uint32_t)c.KD,  (uint32_t)c.VD, (uint32_t)c.CK,
+                                 (uint32_t)kMaxContext};
+    for (int i = 0; i < 16; ++i)
+        if (header_field(file, i) != expect[i]) return false;
+    return true;
+}
+
+bool is_delta(const Config& c, int layer) { return layer % c.AI != c.AI - 1; }
+
+float bf16_to_float(uint16_t b) {
+    const uint32_t bits = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+struct Layer {
+    bool delta = false;
+    float* in_norm = nullptr;  // 1 + w'
+    float* post_norm = nullptr;
+    q3xk_matrix in_proj{};  // delta: [qkv | z | a | b]; attention: [q+gate | k | v]
+    q3xk_matrix out{};      // delta.out / attention.out
+    float *conv = nullptr, *alog = nullptr, *dt = nullptr, *dnorm = nullptr;  // DeltaNet
+    float *qn1 = nullptr, *kn1 = nullptr;                                     // attention
+    q3xk_matrix gate_up{};  // FFN [gate | up]; MoE pool [experts + 1][2I] (shared last)
+    q3xk_matrix down{};     // FFN down; MoE pool [experts + 1][H]
+    q3xk_matrix router{};   // MoE: BF16 [experts + 1][H] = router rows + shared gate row
+};
+
+}  // namespace
+}  // namespace q3xk
+
+using namespace q3xk;
+
+namespace q3x_backend {
+
+struct Model {
+    const Config* config = nullptr;
+    int device = 0;
+    int fd = -1;
+    size_t file_size = 0;
+    const uint8_t* file = nullptr;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    q3xk_matrix embedding{}, lm_head{};
+    float* final_norm = nullptr;
+    std::vector<q3xk::Layer> layer;
+    int P = 0;       // widest in_proj / gate_up (dense) row count
+    int mix = 0;     // widest mixer output (DO, AS, I)
+    int maxcols = 0; // widest matrix input
+
+    ~Model() {
+        if (arena) {
+            cudaSetDevice(device);
+            cudaFree(arena);
+        }
+        if (file) munmap(const_cast<uint8_t*>(file), file_size);
+        if (fd >= 0) close(fd);
+    }
+    bool load(const char* path, const char** error);
+};
+
+struct State {
+    Model* model = nullptr;
+    const Config* c = nullptr;
+    int device = 0;
+    int capacity = 0, position = 0, checkpoint_position = 0;
+    cudaStream_t stream = nullptr;
+    // recurrent arena: per DeltaNet layer conv history [DQKV][CK-1] then memory [VH][KD][VD]
+    float* recurrent = nullptr;
+    float* checkpoint_recurrent = nullptr;
+    size_t recurrent_floats = 0;
+    std::vector<float*> conv, memory, kcache, vcache;
+    float* kv = nullptr;
+    float *logits = nullptr, *checkpoint_logits = nullptr;
+    int* pos = nullptr;        // device position
+    int* tokens = nullptr;     // device tokens of the current chunk
+    int* argmax_out = nullptr;
+    void* argmax_ws = nullptr;
+    size_t argmax_ws_bytes = 0;
+    float *hidden = nullptr, *normed = nullptr, *proj = nullptr, *mix = nullptr, *part = nullptr;
+    float *rlogits = nullptr, *rweights = nullptr, *gu = nullptr, *hbuf = nullptr;
+    int* rids = nullptr;
+    void* gemm_ws = nullptr;
+    size_t gemm_ws_bytes = 0;
+    int split_len = 0;
+    bool use_graphs = true;
+    bool exact_prefill = false;  // T > 1 through per-token GEMVs instead of the FP16 GEMM
+    int chunk = 0;               // tokens per forward pass (work buffers hold `chunk_capacity`)
+    int chunk_capacity = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    std::vector<void*> allocations;
+
+    ~State() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        if (graph) cudaGraphDestroy(graph);
+        for (void* p : allocations) cudaFree(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+    template <typename T>
+    bool alloc(T** p, size_t count) {
+        void* raw = nullptr;
+        if (cudaMalloc(&raw, count * sizeof(T) > 0 ? count * sizeof(T) : 16) != cudaSuccess) return false;
+        allocations.push_back(raw);
+        *p = static_cast<T*>(raw);
+        return true;
+    }
+};
+
+}  // namespace q3x_backend
+
+using q3x_backend::Model;
+using q3x_backend::State;
+
+namespace q3xk {
+namespace {
+
+// engine.cpp:461-477 `take`: 64-byte aligned tensors in a fixed order.
+struct Cursor {
+    const uint8_t* file;
+    size_t size, pos;
+    const char* error = nullptr;
+    const uint8_t* take(size_t bytes) {
+        if (error) return nullptr;
+        const size_t pad = (64 - pos % 64) % 64;
+        if (pos > size || pad > size - pos) {
+            error = "truncated model.bin";
+            return nullptr;
+        }
+        pos += pad;
+        if (bytes > size - pos) {
+            error = "truncated model.bin";
+            return nullptr;
+        }
+        const uint8_t* r = file + pos;
+        pos += bytes;
+        return r;
+    }
+};
+
+// Builds the device copy of the model.  Pass 0 only sizes the arena; pass 1
+// carves it and uploads (matrices through a device staging buffer and
+// q3xk_repack, small vectors converted to FP32 on the host).
+struct Loader {
+    Model& m;
+    const Config& c;
+    int pass = 0;
+    size_t used = 0;
+    uint8_t* staging = nullptr;
+    size_t staging_bytes = 0;
+    cudaStream_t stream = nullptr;
+    int status = Q3XK_OK;
+    std::vector<float> host;
+
+    uint8_t* carve(size_t bytes) {
+        const size_t at = used;
+        used += align_up(bytes);
+        return pass == 0 ? nullptr : m.arena + at;
+    }
+    // A matrix (or pool) of `rows` x `cols` per expert in row-record layout.
+    q3xk_matrix matrix(int type, int rows, int cols, int experts) {
+        q3xk_matrix w{};
+        size_t bytes = 0;
+        if (q3xk_matrix_layout(type, rows, cols, experts, &w, &bytes) != Q3XK_OK) {
+            status = Q3XK_EINVAL;
+            return w;
+        }
+        w.data = carve(bytes);
+        return w;
+    }
+    // Rows [row0, row0 + rows) of expert `e` of w, as a matrix of its own.
+    static q3xk_matrix view(const q3xk_matrix& w, int e, int row0, int rows) {
+        q3xk_matrix v = w;
+        v.data = static_cast<uint8_t*>(w.data) + (size_t)e * w.expert_stride + (size_t)row0 * w.row_stride;
+        v.rows = rows;
+        v.experts = 1;
+        v.expert_stride = (int64_t)rows * w.row_stride;
+        return v;
+    }
+    // Repack `experts` consecutive packed matrices of the file into dst.
+    void upload(const q3xk_matrix& dst, const uint8_t* src, int experts) {
+        if (pass == 0 || status != Q3XK_OK) return;
+        size_t bytes = 0;
+        if (dst.type == Q3XK_BF16)
+            bytes = (size_t)dst.rows * dst.cols * 2 * experts;
+        else if (q3xk_quantized_bytes(dst.type, dst.rows, dst.cols, &bytes) == Q3XK_OK)
+            bytes *= experts;
+        if (bytes > staging_bytes) {
+            status = Q3XK_EINVAL;
+            return;
+        }
+        q3xk_matrix d = dst;
+        d.experts = experts;
+        if (cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+            status = Q3XK_ECUDA;
+            return;
+        }
+        const int st = q3xk_repack(&d, staging, stream);
+        if (st != Q3XK_OK) status = st;
+    }
+    void need_staging(int type, int rows, int cols) {
+        size_t b = 0;
+        if (type == Q3XK_BF16)
+            b = (size_t)rows * cols * 2;
+        else
+            q3xk_quantized_bytes(type, rows, cols, &b);
+        if (b > staging_bytes) staging_bytes = b;
+    }
+    // FP32 device vector from n values of the file: BF16 (plus `add`) or FP32.
+    float* vec(const uint8_t* src, int n, bool bf16, float add) {
+        float* d = reinterpret_cast<float*>(carve((size_t)n * 4));
+        if (pass == 0 || status != Q3XK_OK || !src) return d;
+        host.resize(n);
+        for (int i = 0; i < n; ++i) {
+            if (bf16) {
+                uint16_t b;
+                std::memcpy(&b, src + 2 * (size_t)i, 2);
+                host[i] = add + bf16_to_float(b);
+            } else {
+                std::memcpy(&host[i], src + 4 * (size_t)i, 4);
+            }
+        }
+        // synchronous: the host vector is reused
+        if (cudaMemcpy(d, host.data(), (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) status = Q3XK_ECUDA;
+        return d;
+    }
+
+    // One walk over the file (engine.cpp:488-557).  Returns the cursor error.
+    const char* walk() {
+        const int type = c.matrix_type;
+        const int AS = c.AH * c.AD, KVW = c.KVH * c.AD, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO;
+        const int E = c.experts;
+        Cursor cur{m.file, m.file_size, kHeaderSize};
+        auto packed = [&](int t, int rows, int cols) -> const uint8_t* {
+            size_t b = 0;
+            if (t == Q3XK_BF16)
+                b = (size_t)rows * cols * 2;
+            else if (q3xk_quantized_bytes(t, rows, cols, &b) != Q3XK_OK && !cur.error)
+                cur.error = "invalid quantized matrix layout";
+            if (pass == 0) need_staging(t, rows, cols);
+            return cur.take(b);
+        };
+        m.embedding = matrix(type, c.V, c.H, 1);
+        upload(m.embedding, packed(type, c.V, c.H), 1);
+        if (c.tied) {
+            m.lm_head = m.embedding;
+        } else {
+            m.lm_head = matrix(type, c.V, c.H, 1);
+            upload(m.lm_head, packed(type, c.V, c.H), 1);
+        }
+        m.final_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
+        m.layer.assign(c.N, Layer{});
+        for (int i = 0; i < c.N; ++i) {
+            Layer& l = m.layer[i];
+            l.delta = is_delta(c, i);
+            l.in_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
+            if (l.delta) {
+                l.in_proj = matrix(type, DQKV + DO + 2 * c.VH, c.H, 1);
+                upload(view(l.in_proj, 0, 0, DQKV), packed(type, DQKV, c.H), 1);
+                upload(view(l.in_proj, 0, DQKV, DO), packed(type, DO, c.H), 1);
+                upload(view(l.in_proj, 0, DQKV + DO, c.VH), packed(type, c.VH, c.H), 1);
+                upload(view(l.in_proj, 0, DQKV + DO + c.VH, c.VH), packed(type, c.VH, c.H), 1);
+                l.conv = vec(cur.take((size_t)DQKV * c.CK * 2), DQKV * c.CK, true, 0.0f);
+                l.alog = vec(cur.take((size_t)c.VH * 4), c.VH, false, 0.0f);
+                l.dt = vec(cur.take((size_t)c.VH * 2), c.VH, true, 0.0f);
+                l.dnorm = vec(cur.take((size_t)c.VD * 4), c.VD, false, 0.0f);
+                l.out = matrix(type, c.H, DO, 1);
+                upload(l.out, packed(type, c.H, DO), 1);
+            } else {
+                l.in_proj = matrix(type, 2 * AS + 2 * KVW, c.H, 1);
+                upload(view(l.in_proj, 0, 0, 2 * AS), packed(type, 2 * AS, c.H), 1);
+                upload(view(l.in_proj, 0, 2 * AS, KVW), packed(type, KVW, c.H), 1);
+                upload(view(l.in_proj, 0, 2 * AS + KVW, KVW), packed(type, KVW, c.H), 1);
+                l.qn1 = vec(cur.take((size_t)c.AD * 2), c.AD, true, 1.0f);
+                l.kn1 = vec(cur.take((size_t)c.AD * 2), c.AD, true, 1.0f);
+                l.out = matrix(type, c.H, AS, 1);
+                upload(l.out, packed(type, c.H, AS), 1);
+            }
+            l.post_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
+            if (E) {
+                l.router = matrix(Q3XK_BF16, E + 1, c.H, 1);
+                upload(view(l.router, 0, 0, E), packed(Q3XK_BF16, E, c.H), 1);
+                l.gate_up = matrix(type, 2 * c.I, c.H, E + 1);
+                upload(view(l.gate_up, 0, 0, 2 * c.I), packed(type, E * 2 * c.I, c.H), E);
+                l.down = matrix(type, c.H, c.I, E + 1);
+                upload(view(l.down, 0, 0, c.H), packed(type, E * c.H, c.I), E);
+                upload(view(l.gate_up, E, 0, c.I), packed(type, c.shared_I, c.H), 1);
+                upload(view(l.gate_up, E, c.I, c.I), packed(type, c.shared_I, c.H), 1);
+                upload(view(l.down, E, 0, c.H), packed(type, c.H, c.shared_I), 1);
+                upload(view(l.router, 0, E, 1), packed(Q3XK_BF16, 1, c.H), 1);
+            } else {
+                l.gate_up = matrix(type, 2 * c.I, c.H, 1);
+                upload(view(l.gate_up, 0, 0, c.I), packed(type, c.I, c.H), 1);
+                upload(view(l.gate_up, 0, c.I, c.I), packed(type, c.I, c.H), 1);
+                l.down = matrix(type, c.H, c.I, 1);
+                upload(l.down, packed(type, c.H, c.I), 1);
+            }
+        }
+        if (!cur.error && cur.pos != m.file_size) cur.error = "model.bin size does not match schema";
+        return cur.error;
+    }
+};
+
+}  // namespace
+}  // namespace q3xk
+
+namespace q3x_backend {
+
+// engine.cpp:480-559: same checks and error strings, then the device upload.
+bool Model::load(const char* path, const char** error) {
+    auto fail = [&](const char* message) {
+        *error = message;
+        return false;
+    };
+    fd = open(path, O_RDONLY);
+    struct stat info {};
+    if (fd < 0) return fail("cannot open model.bin");
+    if (fstat(fd, &info) || info.st_size < (off_t)kHeaderSize) return fail("bad model.bin");
+    file_size = (size_t)info.st_size;
+    void* mapped = mmap(nullptr, file_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (mapped == MAP_FAILED) return fail("mmap model.bin failed");
+    file = static_cast<const uint8_t*>(mapped);
+    if (std::memcmp(file, "Q3XMODL\0", 8) != 0) return fail("wrong model.bin magic");
+    config = config_for_id(header_field(file, 0));
+    if (!config) return fail("unsupported Qwen model ID");
+    if (!header_matches(file, *config)) return fail("Qwen model.bin header mismatch");
+    const Config& c = *config;
+    if (c.experts && c.shared_I != c.I) return fail("unsupported MoE shape (shared_I != I)");
+    if (c.experts && (c.experts > 512 || c.top_k > 8)) return fail("unsupported MoE shape");
+
+    Loader ld{*this, c};
+    ld.pass = 0;
+    if (const char* e = ld.walk()) return fail(e);
+    if (ld.status != Q3XK_OK) return fail("invalid quantized matrix layout");
+    arena_bytes = ld.used;
+    if (cudaGetDevice(&device) != cudaSuccess) return fail("no CUDA device");
+    if (cudaMalloc(reinterpret_cast<void**>(&arena), arena_bytes) != cudaSuccess) {
+        arena = nullptr;
+        return fail("cannot allocate device memory for the model");
+    }
+    if (cudaMalloc(reinterpret_cast<void**>(&ld.staging), ld.staging_bytes) != cudaSuccess)
+        return fail("cannot allocate the upload staging buffer");
+    cudaStreamCreateWithFlags(&ld.stream, cudaStreamNonBlocking);
+    madvise(mapped, file_size, MADV_SEQUENTIAL);
+    ld.pass = 1;
+    ld.used = 0;
+    const char* e = ld.walk();
+    const cudaError_t se = cudaStreamSynchronize(ld.stream);
+    cudaStreamDestroy(ld.stream);
+    cudaFree(ld.staging);
+    if (e) return fail(e);
+    if (ld.status != Q3XK_OK || se != cudaSuccess) return fail("model upload to the device failed");
+
+    const int AS = c.AH * c.AD, KVW = c.KVH * c.AD, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO;
+    P = DQKV + DO + 2 * c.VH;
+    if (2 * AS + 2 * KVW > P) P = 2 * AS + 2 * KVW;
+    if (!c.experts && 2 * c.I > P) P = 2 * c.I;
+    mix = DO > AS ? DO : AS;
+    if (c.I > mix) mix = c.I;
+    maxcols = c.H > mix ? c.H : mix;
+    return true;
+}
+
+}  // namespace q3x_backend
+
+namespace q3xk {
+namespace {
+
+#define Q3XB_TRY(expr)                  \
+    do {                                \
+        const int q3xb_st = (expr);     \
+        if (q3xb_st != Q3XK_OK) return q3xb_st; \
+    } while (0)
+
+int mm(State& s, const q3xk_matrix& w, const float* X, int T, float* Y, int accumulate) {
+    if (T == 1) return q3xk_gemv(&w, X, Y, accumulate, s.stream);
+    if (w.type == Q3XK_BF16 || s.exact_prefill) {  // no BF16 GEMM / FP32-exact mode: one GEMV per token
+        for (int t = 0; t < T; ++t)
+            Q3XB_TRY(q3xk_gemv(&w, X + (size_t)t * w.cols, Y + (size_t)t * w.rows, accumulate, s.stream));
+        return Q3XK_OK;
+    }
+    return q3xk_gemm(&w, X, T, Y, accumulate, s.gemm_ws, s.gemm_ws_bytes, s.stream);
+}
+
+// One pass over T <= kChunk tokens already in s.tokens (engine.cpp:431-458).
+int forward_chunk(Model& m, State& s, int T, bool logits) {
+    const Config& c = *m.config;
+    const cudaStream_t st = s.stream;
+    const int H = c.H, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO, AS = c.AH * c.AD;
+    Q3XB_TRY(launch_embed(m.embedding, s.tokens, T, s.hidden, st));
+    int di = 0, ai = 0;
+    for (int i = 0; i < c.N; ++i) {
+        const Layer& l = m.layer[i];
+        Q3XB_TRY(launch_rms(s.hidden, l.in_norm, H, T, s.normed, st));
+        const int P = l.in_proj.rows;
+        Q3XB_TRY(mm(s, l.in_proj, s.normed, T, s.proj, 0));
+        if (l.delta) {
+            Q3XB_TRY(launch_conv(s.proj, P, T, DQKV, l.conv, c.CK, s.conv[di], st));
+            const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
+            Q3XB_TRY(launch_delta(s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di], s.mix, DO, st));
+            Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
+            ++di;
+        } else {
+            const AttnDims ad{c.AH, c.KVH, c.AD, c.RD};
+            Q3XB_TRY(launch_attention(s.proj, P, T, ad, l.qn1, l.kn1, s.pos, s.kcache[ai], s.vcache[ai], s.capacity,
+                                      s.part, s.split_len, s.mix, AS, st));
+            Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
+            ++ai;
+        }
+        Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
+        if (c.experts) {
+            const int S = c.top_k + 1;  // routed slots + the shared expert
+            for (int t = 0; t < T; ++t) {
+                const float* x = s.normed + (size_t)t * H;
+                Q3XB_TRY(q3xk_gemv(&l.router, x, s.rlogits, 0, st));
+                Q3XB_TRY(q3xk_router_topk(s.rlogits, c.experts, c.top_k, 1, s.rids, s.rweights, st));
+                Q3XB_TRY(q3xk_expert_gemv_rows(&l.gate_up, s.rids, S, x, s.gu, 0, st));
+                Q3XB_TRY(q3xk_swiglu(s.gu, s.rweights, S, c.I, s.hbuf, st));
+                Q3XB_TRY(q3xk_expert_gemv_segments(&l.down, s.rids, S, s.hbuf, s.hidden + (size_t)t * H, 1, st));
+            }
+        } else {
+            Q3XB_TRY(mm(s, l.gate_up, s.normed, T, s.proj, 0));
+            Q3XB_TRY(launch_ffn_swiglu(s.proj, 2 * c.I, T, c.I, s.mix, st));
+            Q3XB_TRY(mm(s, l.down, s.mix, T, s.hidden, 1));
+        }
+    }
+    if (logits) {
+        Q3XB_TRY(launch_rms(s.hidden + (size_t)(T - 1) * H, m.final_norm, H, 1, s.normed, st));
+        Q3XB_TRY(q3xk_gemv(&m.lm_head, s.normed, s.logits, 0, st));
+    }
+    return launch_advance(s.pos, T, st);
+}
+
+int capture_decode_graph(Model& m, State& s) {
+    if (cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return Q3XK_ECUDA;
+    const int st = forward_chunk(m, s, 1, true);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s.stream, &g);
+    if (st != Q3XK_OK || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return st != Q3XK_OK ? st : Q3XK_ECUDA;
+    }
+    if (cudaGraphInstantiate(&s.graph_exec, g, 0) != cudaSuccess) {
+        cudaGraphDestroy(g);
+        s.graph_exec = nullptr;
+        return Q3XK_ECUDA;
+    }
+    s.graph = g;
+    return Q3XK_OK;
+}
+
+void set_error(char* err, size_t errlen, const char* fmt, ...) {
+    if (!err || !errlen) return;
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(err, errlen, fmt, ap);
+    va_end(ap);
+}
+
+State* create_state(Model* model, int context, char* err, size_t errlen) {
+    if (!model || !model->config || context <= 0 || context > kMaxContext) {
+        set_error(err, errlen, "state_create model=%p context=%d", static_cast<void*>(model), context);
+        return nullptr;
+    }
+    if (cudaSetDevice(model->device) != cudaSuccess) {
+        set_error(err, errlen, "cannot select the model's device");
+        return nullptr;
+    }
+    std::unique_ptr<State> s(new (std::nothrow) State());
+    if (!s) return nullptr;
+    const Config& c = *model->config;
+    s->model = model;
+    s->c = &c;
+    s->device = model->device;
+    s->capacity = context;
+    if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_error(err, errlen, "cannot create a CUDA stream");
+        return nullptr;
+    }
+    const int DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO;
+    const size_t conv = (size_t)DQKV * (c.CK - 1), memory = (size_t)c.VH * c.KD * c.VD;
+    const size_t cache = (size_t)context * c.KVH * c.AD;
+    const int attn_layers = c.N / c.AI, delta_layers = c.N - attn_layers;
+    const int chunk = context < kChunk ? context : kChunk;
+    s->chunk = s->chunk_capacity = chunk;
+    s->recurrent_floats = (size_t)delta_layers * (conv + memory);
+    s->split_len = (context + kAttnSplits - 1) / kAttnSplits;
+    if (s->split_len < 64) s->split_len = 64;
+    const int nsplit = (context + s->split_len - 1) / s->split_len;
+    bool ok = s->alloc(&s->recurrent, s->recurrent_floats) && s->alloc(&s->checkpoint_recurrent, s->recurrent_floats) &&
+              s->alloc(&s->kv, (size_t)attn_layers * 2 * cache) && s->alloc(&s->logits, c.V) &&
+              s->alloc(&s->checkpoint_logits, c.V) && s->alloc(&s->pos, 1) && s->alloc(&s->tokens, chunk) &&
+              s->alloc(&s->argmax_out, 1) && s->alloc(&s->hidden, (size_t)chunk * c.H) &&
+              s->alloc(&s->normed, (size_t)chunk * c.H) && s->alloc(&s->proj, (size_t)chunk * model->P) &&
+              s->alloc(&s->mix, (size_t)chunk * model->mix) &&
+              s->alloc(&s->part, (size_t)chunk * c.AH * nsplit * (c.AD + 2));
+    if (ok && c.experts) {
+        const int S = c.top_k + 1;
+        ok = s->alloc(&s->rlogits, c.experts + 1) && s->alloc(&s->rweights, S) && s->alloc(&s->rids, S) &&
+             s->alloc(&s->gu, (size_t)S * 2 * c.I) && s->alloc(&s->hbuf, (size_t)S * c.I);
+    }
+    if (ok) {
+        q3xk_argmax_workspace_bytes(&s->argmax_ws_bytes);
+        uint8_t* ws = nullptr;
+        ok = s->alloc(&ws, s->argmax_ws_bytes);
+        s->argmax_ws = ws;
+    }
+    if (ok && chunk > 1) {
+        q3xk_gemm_workspace_bytes(chunk, model->maxcols, &s->gemm_ws_bytes);
+        uint8_t* ws = nullptr;
+        ok = s->alloc(&ws, s->gemm_ws_bytes);
+        s->gemm_ws = ws;
+    }
+    if (!ok) {
+        set_error(err, errlen, "State allocation failed model=%s context=%d", c.name, context);
+        return nullptr;
+    }
+    float* r = s->recurrent;
+    float* kv = s->kv;
+    for (int i = 0; i < c.N; ++i) {
+        if (is_delta(c, i)) {
+            s->conv.push_back(r);
+            r += conv;
+            s->memory.push_back(r);
+            r += memory;
+        } else {
+            s->kcache.push_back(kv);
+            kv += cache;
+            s->vcache.push_back(kv);
+            kv += cache;
+        }
+    }
+    // engine.cpp:156-159 reset; logits start at zero as well
+    if (cudaMemsetAsync(s->recurrent, 0, s->recurrent_floats * 4, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->pos, 0, 4, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->logits, 0, (size_t)c.V * 4, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->checkpoint_logits, 0, (size_t)c.V * 4, s->stream) != cudaSuccess ||
+        cudaStreamSynchronize(s->stream) != cudaSuccess) {
+        set_error(err, errlen, "State initialisation failed");
+        return nullptr;
+    }
+    return s.release();
+}
+
+int state_forward_impl(Model* m, State* s, const int* tokens, int count, bool logits) {
+    if (!m || !s || !tokens || count <= 0 || s->model != m) return Q3XK_EINVAL;
+    const Config& c = *m->config;
+    for (int i = 0; i < count; ++i)
+        if (tokens[i] < 0 || tokens[i] >= c.V) return Q3XK_EINVAL;
+    if (count > s->capacity - s->position) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    const int chunk = s->chunk;
+    for (int done = 0; done < count;) {
+        const int T = count - done < chunk ? count - done : chunk;
+        const bool last = done + T == count;
+        if (cudaMemcpyAsync(s->tokens, tokens + done, (size_t)T * 4, cudaMemcpyHostToDevice, s->stream) !=
+            cudaSuccess)
+            return Q3XK_ECUDA;
+        if (T == 1 && last && logits && s->use_graphs) {
+            if (!s->graph_exec) Q3XB_TRY(capture_decode_graph(*m, *s));
+            if (cudaGraphLaunch(s->graph_exec, s->stream) != cudaSuccess) return Q3XK_ECUDA;
+        } else {
+            Q3XB_TRY(forward_chunk(*m, *s, T, logits && last));
+        }
+        s->position += T;
+        done += T;
+    }
+    return Q3XK_OK;
+}
+
+int checkpoint_copy(State* s, bool save) {
+    if (!s) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    float* rd = save ? s->checkpoint_recurrent : s->recurrent;
+    float* rs = save ? s->recurrent : s->checkpoint_recurrent;
+    float* ld = save ? s->checkpoint_logits : s->logits;
+    float* ls = save ? s->logits : s->checkpoint_logits;
+    if (cudaMemcpyAsync(rd, rs, s->recurrent_floats * 4, cudaMemcpyDeviceToDevice, s->stream) != cudaSuccess ||
+        cudaMemcpyAsync(ld, ls, (size_t)s->c->V * 4, cudaMemcpyDeviceToDevice, s->stream) != cudaSuccess)
+        return Q3XK_ECUDA;
+    if (save) {
+        s->checkpoint_position = s->position;
+    } else {
+        // engine.cpp:591-600
+        if (s->checkpoint_position < 0 || s->checkpoint_position > s->capacity) return Q3XK_EINVAL;
+        s->position = s->checkpoint_position;
+        if (cudaMemcpyAsync(s->pos, &s->position, 4, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+            return Q3XK_ECUDA;
+        if (cudaStreamSynchronize(s->stream) != cudaSuccess) return Q3XK_ECUDA;  // &position is host memory
+    }
+    return Q3XK_OK;
+}
+
+int reset_impl(State* s) {
+    if (!s) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    s->position = 0;
+    if (cudaMemsetAsync(s->recurrent, 0, s->recurrent_floats * 4, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->pos, 0, 4, s->stream) != cudaSuccess)
+        return Q3XK_ECUDA;
+    return Q3XK_OK;
+}
+
+int argmax_impl(const State* s, int* token) {
+    if (!s || !token) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    Q3XB_TRY(q3xk_argmax(s->logits, s->c->V, s->argmax_out, s->argmax_ws, s->argmax_ws_bytes, s->stream));
+    if (cudaMemcpyAsync(token, s->argmax_out, 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
+        cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return Q3XK_ECUDA;
+    return Q3XK_OK;
+}
+
+int copy_logits_impl(const State* s, float* out) {
+    if (!s || !out) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    if (cudaMemcpyAsync(out, s->logits, (size_t)s->c->V * 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
+        cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return Q3XK_ECUDA;
+    return Q3XK_OK;
+}
+
+// The reference's Q3X_ASSERT: report, then abort (internal.h:70-80).
+[[noreturn]] void fatal(const char* what, int status) {
+    std::fprintf(stderr, "q3x_backend: %s failed: %s\n", what, q3xk_status_string(status));
+    std::abort();
+}
+
+}  // namespace
+}  // namespace q3xk
+
+// ---- q3x_backend (C++) ------------------------------------------------------------
+
+namespace q3x_backend {
+
+Model* model_create(const char* path, char* err, size_t errlen) {
+    std::unique_ptr<Model> model(new (std::nothrow) Model());
+    const char* message = nullptr;
+    if (!model || !path || !model->load(path, &message)) {
+        if (err && errlen) std::snprintf(err, errlen, "%s", message ? message : "allocation failed");
+        return nullptr;
+    }
+    if (err && errlen) err[0] = '\0';
+    return model.release();
+}
+void model_destroy(Model* model) { delete model; }
+
+State* state_create(Model* model, int context_size) {
+    char err[256];
+    State* s = create_state(model, context_size, err, sizeof err);
+    if (!s) {
+        std::fprintf(stderr, "q3x_backend: %s\n", err);
+        std::abort();
+    }
+    return s;
+}
+void state_destroy(State* state) { delete state; }
+void state_reset(State* state) {
+    const int st = reset_impl(state);
+    if (st != Q3XK_OK) fatal("state_reset", st);
+}
+void state_forward(Model* model, State* state, const int* tokens, int count, bool compute_logits) {
+    const int st = state_forward_impl(model, state, tokens, count, compute_logits);
+    if (st != Q3XK_OK) fatal("state_forward", st);
+}
+void state_checkpoint_save(State* state) {
+    const int st = checkpoint_copy(state, true);
+    if (st != Q3XK_OK) fatal("state_checkpoint_save", st);
+}
+void state_checkpoint_restore(State* state) {
+    const int st = checkpoint_copy(state, false);
+    if (st != Q3XK_OK) fatal("state_checkpoint_restore", st);
+}
+int state_argmax(const State* state) {
+    if (!state) return -1;
+    int token = -1;
+    const int st = argmax_impl(state, &token);
+    if (st != Q3XK_OK) fatal("state_argmax", st);
+    return token;
+}
+void state_copy_logits(const State* state, float* output) {
+    const int st = copy_logits_impl(state, output);
+    if (st != Q3XK_OK) fatal("state_copy_logits", st);
+}
+uint32_t model_id(const Model* model) { return model->config->id; }
+int vocab_size() { return 248320; }
+int max_context() { return kMaxContext; }
+bool token_is_stop(int token) { return token == kEndOfText || token == kImEnd; }
+
+}  // namespace q3x_backend
+
+// ---- C ABI --------------------------------------------------------------------------
+
+extern "C" {
+
+q3xb_model* q3xb_model_create(const char* path, char* err, size_t errlen) {
+    return reinterpret_cast<q3xb_model*>(q3x_backend::model_create(path, err, errlen));
+}
+void q3xb_model_destroy(q3xb_model* model) { delete reinterpret_cast<Model*>(model); }
+uint32_t q3xb_model_id(const q3xb_model* model) {
+    return model ? reinterpret_cast<const Model*>(model)->config->id : 0;
+}
+int q3xb_model_config(const q3xb_model* model, int* f) {
+    if (!model || !f) return Q3XK_EINVAL;
+    const Config& c = *reinterpret_cast<const Model*>(model)->config;
+    const int v[21] = {(int)c.id, c.V,  c.H,  c.I,  c.N,  c.AI,      c.AH,  c.KVH,        c.AD,        c.RD, c.KH,
+                       c.VH,      c.KD, c.VD, c.CK, kMaxContext, c.experts, c.top_k, c.shared_I, c.matrix_type,
+                       (int)c.tied};
+    std::memcpy(f, v, sizeof v);
+    return Q3XK_OK;
+}
+size_t q3xb_model_device_bytes(const q3xb_model* model) {
+    return model ? reinterpret_cast<const Model*>(model)->arena_bytes : 0;
+}
+q3xb_state* q3xb_state_create(q3xb_model* model, int context_size, char* err, size_t errlen) {
+    return reinterpret_cast<q3xb_state*>(create_state(reinterpret_cast<Model*>(model), context_size, err, errlen));
+}
+void q3xb_state_destroy(q3xb_state* state) { delete reinterpret_cast<State*>(state); }
+int q3xb_state_reset(q3xb_state* state) { return reset_impl(reinterpret_cast<State*>(state)); }
+int q3xb_state_forward(q3xb_model* model, q3xb_state* state, const int* tokens, int count, int compute_logits) {
+    return state_forward_impl(reinterpret_cast<Model*>(model), reinterpret_cast<State*>(state), tokens, count,
+                              compute_logits != 0);
+}
+int q3xb_state_checkpoint_save(q3xb_state* state) { return checkpoint_copy(reinterpret_cast<State*>(state), true); }
+int q3xb_state_checkpoint_restore(q3xb_state* state) {
+    return checkpoint_copy(reinterpret_cast<State*>(state), false);
+}
+int q3xb_state_argmax(const q3xb_state* state, int* token) {
+    return argmax_impl(reinterpret_cast<const State*>(state), token);
+}
+int q3xb_state_copy_logits(const q3xb_state* state, float* output) {
+    return copy_logits_impl(reinterpret_cast<const State*>(state), output);
+}
+int q3xb_state_position(const q3xb_state* state) {
+    return state ? reinterpret_cast<const State*>(state)->position : -1;
+}
+int q3xb_state_synchronize(const q3xb_state* state) {
+    if (!state) return Q3XK_EINVAL;
+    const State* s = reinterpret_cast<const State*>(state);
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    return cudaStreamSynchronize(s->stream) == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
+}
+void* q3xb_state_stream(const q3xb_state* state) {
+    return state ? static_cast<void*>(reinterpret_cast<const State*>(state)->stream) : nullptr;
+}
+int q3xb_state_set_exact_prefill(q3xb_state* state, int enabled) {
+    if (!state) return Q3XK_EINVAL;
+    reinterpret_cast<State*>(state)->exact_prefill = enabled != 0;
+    return Q3XK_OK;
+}
+int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens) {
+    if (!state) return Q3XK_EINVAL;
+    State* s = reinterpret_cast<State*>(state);
+    if (tokens < 1 || tokens > s->chunk_capacity) return Q3XK_EINVAL;
+    s->chunk = tokens;
+    return Q3XK_OK;
+}
+int q3xb_state_set_graphs(q3xb_state* state, int enabled) {
+    if (!state) return Q3XK_EINVAL;
+    reinterpret_cast<State*>(state)->use_graphs = enabled != 0;
+    return Q3XK_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,438 @@
+// layers.cu -- the non-matrix steps of the hybrid decoder's forward.
+//
+// These surround the packed-weight matrix path (gemv.cu, gemm.cu, moe.cu)
+// and follow the reference CPU forward's formulas (engine.cpp:181-369); each
+// kernel names the function it restates.  All state and activations are FP32
+// as in the reference.  Positions are read from device memory (`pos`) so a
+// whole decode step can live in one CUDA graph.
+#include "layers.cuh"
+
+namespace q3xk {
+namespace {
+
+constexpr float kEps = 1e-6f;          // engine.cpp:27
+constexpr float kTheta = 10000000.0f;  // engine.cpp:27
+
+// engine.cpp:187-192
+__device__ __forceinline__ float sigmoidf_ref(float x) {
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+    const float e = expf(x);
+    return e / (1.0f + e);
+}
+__device__ __forceinline__ float siluf_ref(float x) { return x * sigmoidf_ref(x); }
+__device__ __forceinline__ float softplusf_ref(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) s += red[i];
+    return s;
+}
+
+// ---- embedding: one decoded row per token (engine.cpp:195-200, arch/cpu.cpp:55-90)
+__global__ void embed_kernel(const uint8_t* __restrict__ w, int64_t row_stride, int64_t qbytes, int type, int cols,
+                             const int* __restrict__ tokens, int T, float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int t = blockIdx.y;
+    if (t >= T) return;
+    const uint8_t* rec = w + (int64_t)tokens[t] * row_stride;
+    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < cols; k += gridDim.x * blockDim.x) {
+        float v;
+        if (type == Q3XK_BF16) {
+            v = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(rec)[k] << 16);
+        } else {
+            const float d = f16_bits_to_float(reinterpret_cast<const uint16_t*>(rec + qbytes)[k >> 5]);
+            if (type == Q3XK_Q8_0) {
+                v = d * (float)(int8_t)(rec[k] ^ 0x80);
+            } else {
+                const int blk = k >> 5, i = k & 31;
+                const uint8_t b = rec[blk * 16 + (i & 15)];
+                v = d * (float)((i < 16 ? (b & 15) : (b >> 4)) - 8);
+            }
+        }
+        out[(int64_t)t * cols + k] = v;
+    }
+}
+
+// ---- RMSNorm with a precomputed (1 + w) (engine.cpp:231-236)
+__global__ void __launch_bounds__(256) rms_kernel(const float* __restrict__ x, const float* __restrict__ w1, int n,
+                                                  float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    __shared__ float red[8];
+    const float* xr = x + (int64_t)blockIdx.x * n;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += 256) ss += xr[i] * xr[i];
+    ss = block_sum<256>(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)n + kEps);
+    float* o = out + (int64_t)blockIdx.x * n;
+    for (int i = threadIdx.x; i < n; i += 256) o[i] = xr[i] * scale * w1[i];
+}
+
+// ---- causal conv1d over T tokens with SiLU and history (engine.cpp:264-273).
+// proj[t][c] for c < channels is replaced by the activated conv output.
+__global__ void conv_kernel(float* __restrict__ proj, int64_t proj_stride, int T, int channels,
+                            const float* __restrict__ w /*[channels][CK]*/, int CK, float* __restrict__ hist) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= channels) return;
+    float h[8];
+    float* hc = hist + (int64_t)c * (CK - 1);
+    for (int i = 0; i < CK - 1; ++i) h[i] = hc[i];
+    const float* wc = w + (int64_t)c * CK;
+    for (int t = 0; t < T; ++t) {
+        float* xp = proj + (int64_t)t * proj_stride + c;
+        const float x = *xp;
+        float sum = x * wc[CK - 1];
+        for (int i = 0; i < CK - 1; ++i) sum += h[i] * wc[i];
+        for (int i = 0; i < CK - 2; ++i) h[i] = h[i + 1];
+        h[CK - 2] = x;
+        *xp = siluf_ref(sum);
+    }
+    for (int i = 0; i < CK - 1; ++i) hc[i] = h[i];
+}
+
+// ---- gated DeltaNet, one head per CTA, T tokens in order (engine.cpp:274-320).
+// 512 threads: thread (v = tid % 128, g = tid / 128) keeps state rows
+// 32g..32g+31 of column v in registers for the whole chunk.
+constexpr int kDeltaThreads = 512;
+__global__ void __launch_bounds__(kDeltaThreads) delta_kernel(const float* __restrict__ proj, int64_t proj_stride,
+                                                              int T, DeltaDims dd, const float* __restrict__ alog,
+                                                              const float* __restrict__ dt,
+                                                              const float* __restrict__ norm,
+                                                              float* __restrict__ state /*[VH][KD][VD]*/,
+                                                              float* __restrict__ out, int64_t out_stride) {
+    griddep_wait();
+    griddep_launch_dependents();
+    constexpr int KD = 128, VD = 128, G = kDeltaThreads / VD, RG = KD / G;  // rows per group
+    const int head = blockIdx.x;
+    const int tid = threadIdx.x, v = tid % VD, g = tid / VD;
+    __shared__ float qs[KD], ks[KD], vs[VD], part[G][VD], red[kDeltaThreads / 32], scal[4];
+    float S[RG];
+    float* st = state + (int64_t)head * KD * VD;
+#pragma unroll
+    for (int r = 0; r < RG; ++r) S[r] = st[(int64_t)(g * RG + r) * VD + v];
+    const int qk_head = head / (dd.VH / dd.KH);
+    const float qscale = sqrtf((float)KD);
+    for (int t = 0; t < T; ++t) {
+        const float* row = proj + (int64_t)t * proj_stride;
+        // q, k: the GQA key head's slices of the conv output; l2-normalised (engine.cpp:246-251)
+        float qv = 0.f, kv = 0.f;
+        if (tid < KD) {
+            qv = row[qk_head * KD + tid];
+            kv = row[dd.KH * KD + qk_head * KD + tid];
+        }
+        const float qss = block_sum<kDeltaThreads>(tid < KD ? qv * qv : 0.f, red);
+        const float kss = block_sum<kDeltaThreads>(tid < KD ? kv * kv : 0.f, red);
+        if (tid < KD) {
+            qs[tid] = qv * (1.0f / sqrtf(qss + kEps)) / qscale;
+            ks[tid] = kv * (1.0f / sqrtf(kss + kEps));
+        }
+        if (tid < VD) vs[tid] = row[2 * dd.KH * KD + head * VD + tid];
+        if (tid == 0) {
+            const float a = row[dd.a_off + head], b = row[dd.b_off + head];
+            scal[0] = sigmoidf_ref(b);                                     // beta
+            scal[1] = expf(-expf(alog[head]) * softplusf_ref(a + dt[head]));  // exp(decay)
+        }
+        __syncthreads();
+        const float beta = scal[0], gdecay = scal[1];
+        // S <- decay * S; pred = k^T S
+        float p = 0.f;
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+            S[r] *= gdecay;
+            p += ks[g * RG + r] * S[r];
+        }
+        part[g][v] = p;
+        __syncthreads();
+        float pred = 0.f;
+#pragma unroll
+        for (int i = 0; i < G; ++i) pred += part[i][v];
+        const float dv = vs[v] - pred;
+        // S += k (beta (v - pred)); o = q^T S
+        float o = 0.f;
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+            S[r] += ks[g * RG + r] * beta * dv;
+            o += qs[g * RG + r] * S[r];
+        }
+        __syncthreads();
+        part[g][v] = o;
+        __syncthreads();
+        float ov = 0.f;
+        if (tid < VD) {
+#pragma unroll
+            for (int i = 0; i < G; ++i) ov += part[i][tid];
+        }
+        // gated RMS: o * rsqrt(mean o^2 + eps) * norm * silu(z) (engine.cpp:237-242)
+        const float oss = block_sum<kDeltaThreads>(tid < VD ? ov * ov : 0.f, red);
+        if (tid < VD) {
+            const float scale = 1.0f / sqrtf(oss / (float)VD + kEps);
+            const float z = row[dd.z_off + head * VD + tid];
+            out[(int64_t)t * out_stride + head * VD + tid] = ov * (scale * norm[tid] * siluf_ref(z));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < RG; ++r) st[(int64_t)(g * RG + r) * VD + v] = S[r];
+}
+
+// ---- attention inputs (engine.cpp:327-346): per token, q/gate split, RMS of
+// q and k with (1 + w), partial RoPE, K/V appended to the cache at pos + t.
+__global__ void __launch_bounds__(256) attn_prep_kernel(float* __restrict__ proj, int64_t proj_stride,
+                                                        AttnDims ad, const float* __restrict__ qn1,
+                                                        const float* __restrict__ kn1, const int* __restrict__ pos,
+                                                        float* __restrict__ kcache, float* __restrict__ vcache) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int t = blockIdx.x, h = blockIdx.y;  // h < AH: query head; AH <= h < AH + KVH: key head
+    const int AD = ad.AD, RD = ad.RD;
+    float* row = proj + (int64_t)t * proj_stride;
+    const int position = *pos + t;
+    const bool is_q = h < ad.AH;
+    float* x = is_q ? row + (int64_t)h * 2 * AD : row + 2 * ad.AH * AD + (int64_t)(h - ad.AH) * AD;
+    const float* w1 = is_q ? qn1 : kn1;
+    __shared__ float red[8], buf[512];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < AD; i += 256) ss += x[i] * x[i];
+    ss = block_sum<256>(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)AD + kEps);
+    for (int i = threadIdx.x; i < AD; i += 256) buf[i] = x[i] * scale * w1[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < AD; i += 256) {
+        float v = buf[i];
+        if (i < RD) {
+            const int half = RD / 2, j = i < half ? i : i - half;
+            const float angle = (float)position / powf(kTheta, 2.0f * (float)j / (float)RD);
+            const float c = cosf(angle), s = sinf(angle);
+            v = i < half ? buf[i] * c - buf[i + half] * s : buf[i] * c + buf[i - half] * s;
+        }
+        if (is_q) {
+            x[i] = v;
+        } else {
+            const int64_t off = ((int64_t)position * ad.KVH + (h - ad.AH)) * AD + i;
+            kcache[off] = v;
+            vcache[off] = row[2 * ad.AH * AD + (int64_t)ad.KVH * AD + (int64_t)(h - ad.AH) * AD + i];
+        }
+    }
+}
+
+// ---- causal attention, split over keys (engine.cpp:347-367).  CTA = (key
+// split, kv head, token): each warp walks keys j = split0 + w, + 8, ... for all
+// G query heads of the kv head with an online softmax; partial (m, l, o) per
+// split go to `part`, merged by attn_merge_kernel.
+constexpr int kAttnWarps = 8;
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const float* __restrict__ proj,
+                                                                     int64_t proj_stride, AttnDims ad,
+                                                                     const int* __restrict__ pos,
+                                                                     const float* __restrict__ kcache,
+                                                                     const float* __restrict__ vcache,
+                                                                     int split_len, float* __restrict__ part) {
+    griddep_wait();
+    griddep_launch_dependents();
+    constexpr int kMaxG = 8, kPerLane = 8;  // AD = 256 = 32 lanes x 8
+    const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
+    const int nsplit = gridDim.x, G = ad.AH / ad.KVH, AD = ad.AD;
+    const int last = *pos + t;  // keys 0..last
+    const int j0 = split * split_len, j1 = min(last + 1, j0 + split_len);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* row = proj + (int64_t)t * proj_stride;
+    const float inv = 1.0f / sqrtf((float)AD);
+    float q[kMaxG][kPerLane], o[kMaxG][kPerLane], m[kMaxG], l[kMaxG];
+#pragma unroll
+    for (int gi = 0; gi < kMaxG; ++gi) {
+        m[gi] = -INFINITY;
+        l[gi] = 0.f;
+#pragma unroll
+        for (int e = 0; e < kPerLane; ++e) {
+            o[gi][e] = 0.f;
+            q[gi][e] = gi < G ? row[(int64_t)(kvh * G + gi) * 2 * AD + lane * kPerLane + e] : 0.f;
+        }
+    }
+    for (int j = j0 + warp; j < j1; j += kAttnWarps) {
+        const float* kr = kcache + ((int64_t)j * ad.KVH + kvh) * AD + lane * kPerLane;
+        const float* vr = vcache + ((int64_t)j * ad.KVH + kvh) * AD + lane * kPerLane;
+        float kv[kPerLane], vv[kPerLane];
+        *reinterpret_cast<float4*>(kv) = *reinterpret_cast<const float4*>(kr);
+        *reinterpret_cast<float4*>(kv + 4) = *reinterpret_cast<const float4*>(kr + 4);
+        *reinterpret_cast<float4*>(vv) = *reinterpret_cast<const float4*>(vr);
+        *reinterpret_cast<float4*>(vv + 4) = *reinterpret_cast<const float4*>(vr + 4);
+#pragma unroll
+        for (int gi = 0; gi < kMaxG; ++gi) {
+            if (gi >= G) break;
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < kPerLane; ++e) d += q[gi][e] * kv[e];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+            const float s = d * inv;
+            const float mn = fmaxf(m[gi], s);
+            const float corr = expf(m[gi] - mn), p = expf(s - mn);
+            l[gi] = l[gi] * corr + p;
+#pragma unroll
+            for (int e = 0; e < kPerLane; ++e) o[gi][e] = o[gi][e] * corr + p * vv[e];
+            m[gi] = mn;
+        }
+    }
+    // merge the 8 warps in shared memory
+    __shared__ float sm[kAttnWarps][kMaxG], sl[kAttnWarps][kMaxG];
+    __shared__ float so[kAttnWarps][256];
+#pragma unroll
+    for (int gi = 0; gi < kMaxG; ++gi) {
+        if (gi < G) {  // uniform over the CTA
+            if (lane == 0) {
+                sm[warp][gi] = m[gi];
+                sl[warp][gi] = l[gi];
+            }
+#pragma unroll
+            for (int e = 0; e < kPerLane; ++e) so[warp][lane * kPerLane + e] = o[gi][e];
+            __syncthreads();
+            if (warp == 0) {
+                float M = -INFINITY;
+                for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm[w][gi]);
+                float L = 0.f, acc[kPerLane] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int w = 0; w < kAttnWarps; ++w) {
+                    const float c = sm[w][gi] == -INFINITY ? 0.f : expf(sm[w][gi] - M);
+                    L += sl[w][gi] * c;
+#pragma unroll
+                    for (int e = 0; e < kPerLane; ++e) acc[e] += so[w][lane * kPerLane + e] * c;
+                }
+                // part[t][h][split] = {m, l, o[AD]}
+                float* dst = part + (((int64_t)t * ad.AH + kvh * G + gi) * nsplit + split) * (AD + 2);
+                if (lane == 0) {
+                    dst[0] = M;
+                    dst[1] = L;
+                }
+#pragma unroll
+                for (int e = 0; e < kPerLane; ++e) dst[2 + lane * kPerLane + e] = acc[e];
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ part, int nsplit,
+                                                         const float* __restrict__ proj, int64_t proj_stride,
+                                                         AttnDims ad, float* __restrict__ out,
+                                                         int64_t out_stride) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int t = blockIdx.x, h = blockIdx.y, AD = ad.AD;
+    const float* p = part + ((int64_t)t * ad.AH + h) * nsplit * (AD + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p[(int64_t)s * (AD + 2)]);
+    const float* gate = proj + (int64_t)t * proj_stride + (int64_t)h * 2 * AD + AD;
+    for (int d = threadIdx.x; d < AD; d += blockDim.x) {
+        float L = 0.f, acc = 0.f;
+        for (int s = 0; s < nsplit; ++s) {
+            const float* ps = p + (int64_t)s * (AD + 2);
+            const float c = ps[0] == -INFINITY ? 0.f : expf(ps[0] - M);
+            L += ps[1] * c;
+            acc += ps[2 + d] * c;
+        }
+        out[(int64_t)t * out_stride + (int64_t)h * AD + d] = acc / L * sigmoidf_ref(gate[d]);
+    }
+}
+
+// dense FFN SwiGLU over T tokens: out[t][i] = silu(g) * u, [g | u] = proj[t]
+__global__ void ffn_swiglu_kernel(const float* __restrict__ proj, int64_t proj_stride, int T, int I,
+                                  float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int64_t n = (int64_t)T * I;
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = k / I, i = k - t * I;
+        const float g = proj[t * proj_stride + i], u = proj[t * proj_stride + I + i];
+        out[k] = siluf_ref(g) * u;  // engine.cpp:374
+    }
+}
+
+__global__ void advance_kernel(int* pos, int by) {
+    griddep_wait();
+    griddep_launch_dependents();
+    *pos += by;
+}
+
+}  // namespace
+
+// ---- launchers -----------------------------------------------------------------
+
+int launch_embed(const q3xk_matrix& m, const int* tokens, int T, float* out, cudaStream_t s) {
+    const dim3 grid((m.cols + 255) / 256, T);
+    if (launch_pdl(embed_kernel, grid, dim3(256), 0, s, (const uint8_t*)m.data, m.row_stride,
+                   quant_bytes(m.type, m.cols), m.type, m.cols, tokens, T, out) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int launch_rms(const float* x, const float* w1, int n, int T, float* out, cudaStream_t s) {
+    if (launch_pdl(rms_kernel, dim3(T), dim3(256), 0, s, x, w1, n, out) != cudaSuccess) return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const float* w, int CK, float* hist,
+                cudaStream_t s) {
+    if (CK < 2 || CK > 9) return Q3XK_EUNSUPPORTED;
+    if (launch_pdl(conv_kernel, dim3((channels + 127) / 128), dim3(128), 0, s, proj, proj_stride, T, channels, w,
+                   CK, hist) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int launch_delta(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
+                 const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
+                 cudaStream_t s) {
+    if (dd.KD != 128 || dd.VD != 128 || dd.VH % dd.KH) return Q3XK_EUNSUPPORTED;
+    if (launch_pdl(delta_kernel, dim3(dd.VH), dim3(kDeltaThreads), 0, s, proj, proj_stride, T, dd, alog, dt, norm,
+                   state, out, out_stride) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int launch_attention(float* proj, int64_t proj_stride, int T, const AttnDims& ad, const float* qn1,
+                     const float* kn1, const int* pos, float* kcache, float* vcache, int capacity, float* part,
+                     int split_len, float* out, int64_t out_stride, cudaStream_t s) {
+    if (ad.AD != 256 || ad.AH % ad.KVH || ad.AH / ad.KVH > 8 || ad.RD > ad.AD) return Q3XK_EUNSUPPORTED;
+    if (launch_pdl(attn_prep_kernel, dim3(T, ad.AH + ad.KVH), dim3(256), 0, s, proj, proj_stride, ad, qn1, kn1, pos,
+                   kcache, vcache) != cudaSuccess)
+        return Q3XK_ECUDA;
+    const int nsplit = (capacity + split_len - 1) / split_len;
+    if (launch_pdl(attn_split_kernel, dim3(nsplit, ad.KVH, T), dim3(kAttnWarps * 32), 0, s, (const float*)proj,
+                   proj_stride, ad, pos, (const float*)kcache, (const float*)vcache, split_len, part) != cudaSuccess)
+        return Q3XK_ECUDA;
+    if (launch_pdl(attn_merge_kernel, dim3(T, ad.AH), dim3(256), 0, s, (const float*)part, nsplit,
+                   (const float*)proj, proj_stride, ad, out, out_stride) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch(3);
+    return Q3XK_OK;
+}
+
+int launch_ffn_swiglu(const float* proj, int64_t proj_stride, int T, int I, float* out, cudaStream_t s) {
+    const int64_t n = (int64_t)T * I;
+    const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    if (launch_pdl(ffn_swiglu_kernel, dim3(blocks), dim3(256), 0, s, proj, proj_stride, T, I, out) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int launch_advance(int* pos, int by, cudaStream_t s) {
+    if (launch_pdl(advance_kernel, dim3(1), dim3(1), 0, s, pos, by) != cudaSuccess) return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+}  // namespace q3xk

@@ -11,10 +11,10 @@ from qwen3x_b200.capi import Matrix, lib
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def declared(header: str):
+def declared(header: str, prefix: str = "q3xk"):
     text = (ROOT / "include" / header).read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(q3xk\w*)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(" + prefix + r"\w*)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -25,6 +25,50 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
     # and the binding knows every one of them
     assert set(names) <= set(capi.declared_symbols())
+
+
+def test_library_exports_the_backend_interface():
+    """q3x_backend.h: the C mirror and the reference's C++ q3x_backend
+    functions (internal.h:16-34), exported with their mangled C++ names."""
+    names = declared("q3x_backend.h", "q3xb")
+    assert "q3xb_state_forward" in names and len(names) >= 17
+    handle = lib()
+    assert not [n for n in names if not hasattr(handle, n)]
+    assert set(names) <= set(capi.declared_symbols())
+    import subprocess
+    out = subprocess.run(["nm", "-DC", "--defined-only", str(capi.LIB_PATH)], capture_output=True,
+                         text=True).stdout
+    for fn in ["model_create(char const*, char*, unsigned long)", "model_destroy(", "state_create(",
+               "state_destroy(", "state_reset(", "state_forward(", "state_checkpoint_save(",
+               "state_checkpoint_restore(", "state_argmax(", "state_copy_logits(", "model_id(",
+               "vocab_size()", "max_context()", "token_is_stop(int)"]:
+        assert "q3x_backend::" + fn in out, fn
+
+
+def test_backend_rejects_bad_model_files(tmp_path):
+    """Model::load's checks and messages (engine.cpp:480-498), no GPU work:
+    each file fails before any device memory is touched."""
+    import struct
+    err = ctypes.create_string_buffer(256)
+    create = lib().q3xb_model_create
+
+    def fails(data):
+        p = tmp_path / "m.bin"
+        p.write_bytes(data)
+        assert not create(str(p).encode(), err, 256)
+        return err.value.decode()
+
+    from qwen3x_b200 import modelfile
+
+    assert not create(str(tmp_path / "absent.bin").encode(), err, 256)
+    assert err.value.decode() == "cannot open model.bin"
+    assert fails(b"short") == "bad model.bin"
+    assert fails(b"NOTMODEL" + bytes(64)) == "wrong model.bin magic"
+    assert fails(b"Q3XMODL\0" + struct.pack("<16I", 1234, *([0] * 15))) == "unsupported Qwen model ID"
+    assert fails(b"Q3XMODL\0" + struct.pack("<16I", 9000, *([0] * 15))) == "Qwen model.bin header mismatch"
+    c = modelfile.CONFIGS[9091]
+    assert fails(c.header() + bytes(1000)) == "truncated model.bin"
+    assert fails(c.header() + bytes(modelfile.file_size(c) - 72 + 64)) == "model.bin size does not match schema"
 
 
 def test_abi_version_and_status_strings():
