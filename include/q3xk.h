@@ -183,6 +183,26 @@ Q3XK_API int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* 
                               void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * q3xk_try_mv_host without a workspace: no allocation at any time.  For
+ * callers that cannot hand over device memory -- code written against the
+ * reference's q3x_cpu::try_mv(w, type, rows, cols, x, y), whose signature has
+ * no workspace argument, and FFI hosts that hold no CUDA allocator -- and that
+ * should not pay a cudaMalloc/cudaFree (an implicit device synchronisation)
+ * on every matvec.  No counterpart in the reference.
+ *
+ * x and y are staged in a fixed device array inside libq3xk.so of 4 MiB per
+ * device: cols rounded up to 4, plus rows, must not exceed 1048576 floats,
+ * otherwise Q3XK_EWORKSPACE is returned before any CUDA call.  The first call
+ * on a device (the current one) looks the array's address up with
+ * cudaGetSymbolAddress; make it before any stream capture.  The array is
+ * shared: calls whose work overlaps on the GPU (other streams or host threads
+ * on the same device) race on it, so run them one at a time.  Nothing in it
+ * needs to start at zero: each call overwrites the x and y it reads.
+ */
+Q3XK_API int q3xk_try_mv_host_noalloc(const q3xk_matrix* w, const float* x_host, float* y_host,
+                                      void* stream);
+
+/*
  * Device-side error word of the current device: bit 0 = a producer gave up
  * waiting for a free stage, bit 1 = a consumer gave up waiting for data.
  * Every device-side wait in these kernels is bounded (about one second);

@@ -55,6 +55,8 @@ _SIGNATURES = {
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "q3xk_try_mv_host": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "q3xk_try_mv_host_noalloc": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p,
+                                                ctypes.c_void_p, ctypes.c_void_p]),
     "q3xk_expert_gemv_rows": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                              ctypes.c_void_p]),

@@ -27,6 +27,8 @@
 //  * Programmatic dependent launch: the first row group's weights are
 //    requested before griddepcontrol.wait, i.e. while the previous kernel in
 //    the stream is still finishing; x and y are only touched after it.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace q3xk {
@@ -583,6 +585,64 @@ int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* y_host, v
     float* xd = static_cast<float*>(workspace);
     float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + y_off);
     if (cudaMemcpyAsync(xd, x_host, x_bytes, cudaMemcpyHostToDevice, s) != cudaSuccess)
+        return Q3XK_ECUDA;
+    const int st = gemv_impl(w, static_cast<const uint8_t*>(w->data), xd, yd, 0, s);
+    if (st != Q3XK_OK) return st;
+    if (cudaMemcpyAsync(y_host, yd, (size_t)w->rows * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return Q3XK_ECUDA;
+    return cuda_status(cudaStreamSynchronize(s));
+}
+
+}  // extern "C"
+
+// ---- q3xk_try_mv_host_noalloc: q3xk_try_mv_host with a fixed scratch ---------------
+//
+// The staging copies of x and y live in this module's own device array instead
+// of a caller workspace.  Its device address is looked up once per device with
+// cudaGetSymbolAddress (on the first call made with that device current) and
+// kept in g_static_scratch; nothing is allocated at any time.
+namespace q3xk {
+namespace {
+
+constexpr size_t kStaticScratchFloats = (size_t)1 << 20;  // 4 MiB: x (cols) + y (rows) floats
+constexpr int kMaxScratchDevices = 64;
+
+static __device__ __align__(256) float g_mv_scratch[kStaticScratchFloats];
+
+std::mutex g_scratch_mutex;
+float* g_static_scratch[kMaxScratchDevices] = {};
+
+// Address of g_mv_scratch on the current device (looked up on first use).
+int static_scratch(float** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return Q3XK_ECUDA;
+    if (dev < 0 || dev >= kMaxScratchDevices) return Q3XK_EUNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_static_scratch[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_mv_scratch) != cudaSuccess || !p) return Q3XK_ECUDA;
+        g_static_scratch[dev] = static_cast<float*>(p);
+    }
+    *out = g_static_scratch[dev];
+    return Q3XK_OK;
+}
+
+}  // namespace
+}  // namespace q3xk
+
+extern "C" {
+
+int q3xk_try_mv_host_noalloc(const q3xk_matrix* w, const float* x_host, float* y_host, void* stream) {
+    if (!w || !x_host || !y_host || w->rows <= 0 || w->cols <= 0) return Q3XK_EINVAL;
+    const size_t y_off = ((size_t)w->cols + 3) & ~(size_t)3;  // y starts 16-byte aligned
+    if (y_off + (size_t)w->rows > kStaticScratchFloats) return Q3XK_EWORKSPACE;
+    float* scratch = nullptr;
+    const int st0 = static_scratch(&scratch);
+    if (st0 != Q3XK_OK) return st0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* xd = scratch;
+    float* yd = scratch + y_off;
+    if (cudaMemcpyAsync(xd, x_host, (size_t)w->cols * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
         return Q3XK_ECUDA;
     const int st = gemv_impl(w, static_cast<const uint8_t*>(w->data), xd, yd, 0, s);
     if (st != Q3XK_OK) return st;
