@@ -328,6 +328,144 @@ def cpu_reference_gbs(mtype: int, threads: int, budget_s: float, rows_cap=None):
     return gbs, kind, f"{calls} x Q{'8' if mtype == 1 else '4'}_0 matvec {rows}x{COLS} in {el:.1f} s"
 
 
+def decode_bytes_per_token(c, position: int) -> int:
+    """Algorithmic HBM bytes of one decode step at `position`: every matrix
+    once (model.bin packed size; one embedding row), the DeltaNet memory and
+    conv history read and written, the KV cache read up to `position`."""
+    from qwen3x_b200 import modelfile
+
+    entries, _ = modelfile.layout(c)
+    weights = sum(b for name, kind, shape, off, b in entries
+                  if kind == "matrix" and name != "embedding")
+    weights += modelfile.nbytes(c, "matrix", (1, c.H))
+    if c.experts:  # only top_k routed experts of each pool are read
+        pools = sum(b for name, kind, shape, off, b in entries if name.endswith(("moe.gate_up", "moe.down")))
+        weights -= pools - pools * c.top_k // c.experts
+    attn = c.N // c.AI
+    delta = c.N - attn
+    state = delta * (c.VH * c.KD * c.VD + c.DQKV * (c.CK - 1)) * 4 * 2
+    kv = attn * position * c.KVH * c.AD * 4 * 2
+    return weights + state + kv
+
+
+def model_file_dir(size: int) -> str:
+    import shutil
+    import tempfile
+
+    for d in ("/dev/shm", tempfile.gettempdir()):
+        if os.path.isdir(d) and shutil.disk_usage(d).free > size + (4 << 30):
+            return d
+    return tempfile.gettempdir()
+
+
+def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sample: bool):
+    """The backend end to end (q3x_backend.h via qwen3x_b200.backend) on a
+    seeded synthetic model.bin of config `cfg_id`: prefill `prompt_len`
+    uniform-random tokens in one state_forward call, then `decode_steps`
+    greedy steps (state_argmax + state_forward of that token), as the
+    reference's runtime drives the backend.  Times are CUDA events on the
+    state's stream; weights (GBs) are far larger than L2."""
+    import numpy as np
+    import torch
+
+    from qwen3x_b200 import modelfile
+    from qwen3x_b200.backend import Model, State
+
+    c = modelfile.CONFIGS[cfg_id]
+    size = modelfile.file_size(c)
+    path = os.path.join(model_file_dir(size), f"q3x_bench_{cfg_id}_{os.getpid()}.bin")
+    out = {"config": f"{cfg_id} ({c.name})", "prompt_tokens": prompt_len, "decode_steps": decode_steps}
+    t0 = time.time()
+    try:
+        modelfile.write_model(path, c, seed=7, device=device)
+        out["model_write_s"] = round(time.time() - t0, 1)
+        t1 = time.time()
+        model = Model(path)
+        out["model_load_s"] = round(time.time() - t1, 1)
+        out["model_device_gb"] = round(model.device_bytes / 1e9, 2)
+        st = State(model, prompt_len + decode_steps + 72)
+        stream = torch.cuda.ExternalStream(st.stream)
+        prompt = np.random.default_rng(11).integers(0, c.V, prompt_len).astype(np.int32)
+        for _ in range(3):  # warm-up: a short prompt and a few decode steps (captures the graph)
+            st.forward(prompt[:min(64, prompt_len)])
+            for _ in range(4):
+                st.forward([st.argmax()])
+            st.reset()
+        st.synchronize()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        with ClockSampler(device.index) as clk:
+            torch.cuda.nvtx.range_push("prefill")  # ncu --nvtx-include "prefill/"
+            e0.record(stream)
+            st.forward(prompt)
+            e1.record(stream)
+            torch.cuda.nvtx.range_pop()
+            tokens = []
+            for _ in range(decode_steps):
+                tokens.append(st.argmax())
+                st.forward([tokens[-1]])
+            e2.record(stream)
+            e2.synchronize()
+            # decode without the per-step host round trip (graph replays back to back)
+            e3, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push("decode")  # ncu --nvtx-include "decode/" selects these launches
+            e3.record(stream)
+            for t in tokens[:64]:
+                st.forward([t])
+            e4.record(stream)
+            e4.synchronize()
+            torch.cuda.nvtx.range_pop()
+        prefill_s = e0.elapsed_time(e1) / 1e3
+        decode_s = e1.elapsed_time(e2) / 1e3
+        dev_step_s = e3.elapsed_time(e4) / 1e3 / len(tokens[:64])
+        mid = prompt_len + decode_steps // 2
+        bpt = decode_bytes_per_token(c, mid)
+        peak, peak_kind = measured_peaks()
+        out.update({
+            "prefill_tok_s": round(prompt_len / prefill_s, 1),
+            "prefill_ms": round(prefill_s * 1e3, 2),
+            "decode_tok_s": round(decode_steps / decode_s, 2),
+            "decode_ms_per_token": round(decode_s / decode_steps * 1e3, 3),
+            "decode_device_ms_per_token": round(dev_step_s * 1e3, 3),
+            "decode_bytes_per_token": bpt,
+            "decode_roofline": {"bound": "hbm", "achieved": round(bpt / dev_step_s / 1e9, 1), "peak": peak,
+                                "peak_kind": peak_kind, "unit": "GB/s",
+                                "frac": round(bpt / dev_step_s / 1e9 / peak, 4)},
+            "clocks": clk.summary(),
+            "first_tokens": tokens[:8],
+        })
+        st.close()
+        model.close()
+        if cpu_sample:
+            out["cpu_baseline"] = cpu_engine_tok_s(path, c)
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    return out
+
+
+def cpu_engine_tok_s(path, c, prompt=2, steps=2):
+    """The reference CPU forward (engine.cpp via oracle/_ref; single-threaded,
+    one token per forward as the reference runs) on the same model.bin: a
+    bounded sample of prompt + decode tokens."""
+    import numpy as np
+
+    import oracle
+
+    if oracle.reference() is None:
+        return None
+    e = oracle.RefEngine(path, c if c.id not in (800, 4000, 9000, 36035, 38027) else None, context=64)
+    toks = np.random.default_rng(11).integers(0, c.V, prompt).astype(np.int32)
+    t0 = time.time()
+    e.forward(toks)
+    for _ in range(steps):
+        e.forward([e.argmax()])
+    dt = time.time() - t0
+    e.close()
+    return {"value": round((prompt + steps) / dt, 4), "unit": "tok/s", "cores": 1, "kind": "reference",
+            "sample": f"{prompt}-token prompt + {steps} greedy steps of the same model.bin (reference forward "
+                      "is one token at a time, so prefill and decode rates coincide)"}
+
+
 def run_reference(args):
     """--impl reference: the reference CPU path with all host threads."""
     rank = int(os.environ.get("RANK", "0"))
@@ -382,7 +520,10 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling)")
-    ap.add_argument("--only", choices=["gemv", "gemm"], default=None,
+    ap.add_argument("--no-engine", action="store_true", help="skip the end-to-end model legs")
+    ap.add_argument("--engine-prompt", type=int, default=4096)
+    ap.add_argument("--engine-decode", type=int, default=256)
+    ap.add_argument("--only", choices=["gemv", "gemm", "engine"], default=None,
                     help="run one kernel family only (for profiling; no JSON line)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
@@ -401,6 +542,11 @@ def main(argv=None):
             if rank == 0:
                 print(f"gemm type={mtype} T=4096: {secs * 1e6:.1f} us "
                       f"{2 * 4096 * ROWS * COLS / secs / 1e12:.1f} TFLOP/s", flush=True)
+        return 0
+
+    if args.only == "engine":
+        print(json.dumps(time_engine(9000, args.engine_prompt, args.engine_decode, device,
+                                     rank == 0 and not args.no_cpu_baseline)), flush=True)
         return 0
 
     secs, launches, clocks = time_gemv(1, args.steps, args.warmup, device, world, rank == 0)
@@ -435,6 +581,11 @@ def main(argv=None):
         gemm["peak_tflops"] = peak_tf[0]
         gemm["peak_kind"] = peak_tf[1]
 
+    engine = None
+    if args.only is None and not args.no_engine:
+        engine = time_engine(9000, args.engine_prompt, args.engine_decode, device,
+                             rank == 0 and world == 1 and not args.no_cpu_baseline)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, kind, sample = cpu_reference_gbs(1, threads=1, budget_s=10.0)
@@ -464,6 +615,7 @@ def main(argv=None):
                               "bytes_per_launch": q4_bytes},
                 "gemm_cfg2": dict(gemm, workload="cfg2: Y[T,12288] = X[T,4096] W^T, dequant-GEMM on "
                                                   "tcgen05 (FP16 x FP16 -> FP32), T sweep"),
+                "engine_9b": engine,
             },
         }
         print(json.dumps(line), flush=True)

@@ -112,6 +112,45 @@ Q3XK_API int q3xk_gemv(const q3xk_matrix* w, const float* x, float* y, int accum
               void* stream);
 
 /*
+ * Input transforms for the _ex GEMVs: the elementwise pass that produces a
+ * GEMV's input in the reference is applied while the GEMV stages x, so the
+ * intermediate vector is never written.  No counterpart in the reference
+ * (which runs these as separate loops / kernels); each follows its formula:
+ *   RMS        x[k] * rsqrt(mean(x^2) + 1e-6) * w[k], w = 1 + w'     engine.cpp:231-236
+ *   GATED_RMS  per group of `group` elements:
+ *              x[k] * (rsqrt(mean_g(x^2) + 1e-6) * w[k % group] * silu(z[k]))
+ *                                                                 engine.cpp:237-242
+ *   SWIGLU     x holds [g | u] pairs of width `group` (one pair per segment):
+ *              silu(g[i]) * u[i], times seg_weights[s] when given  engine.cpp:374, :415-416
+ * Limits: GATED_RMS needs cols % group == 0 and cols / group <= 64 (plain
+ * GEMV only); SWIGLU's group must equal the matrix's cols.
+ */
+typedef enum q3xk_xform_kind {
+    Q3XK_XFORM_NONE = 0,
+    Q3XK_XFORM_RMS = 1,
+    Q3XK_XFORM_GATED_RMS = 2,
+    Q3XK_XFORM_SWIGLU = 3
+} q3xk_xform_kind;
+
+typedef struct q3xk_xform {
+    int32_t kind;             /* q3xk_xform_kind */
+    int32_t group;            /* GATED_RMS group size; SWIGLU pair width */
+    const float* w;           /* RMS: 1 + w' [cols]; GATED_RMS: norm [group] */
+    const float* z;           /* GATED_RMS: gate [cols] */
+    const float* seg_weights; /* SWIGLU: one weight per segment, or NULL */
+} q3xk_xform;
+
+/* q3xk_gemv / q3xk_expert_gemv_rows / q3xk_expert_gemv_segments with an
+ * input transform (xf may be NULL = none). */
+Q3XK_API int q3xk_gemv_ex(const q3xk_matrix* w, const float* x, float* y, int accumulate,
+                          const q3xk_xform* xf, void* stream);
+Q3XK_API int q3xk_expert_gemv_rows_ex(const q3xk_matrix* pool, const int* ids, int slots, const float* x,
+                                      float* y, int accumulate, const q3xk_xform* xf, void* stream);
+Q3XK_API int q3xk_expert_gemv_segments_ex(const q3xk_matrix* pool, const int* ids, int slots,
+                                          const float* x, float* y, int accumulate, const q3xk_xform* xf,
+                                          void* stream);
+
+/*
  * GEMV of one expert of a pool: y = W[expert] x.  `expert` is a host int.
  * Replaces engine.cpp:214-224 expert_mv.
  */

@@ -32,6 +32,21 @@ class Matrix(ctypes.Structure):
     ]
 
 
+class XForm(ctypes.Structure):
+    """struct q3xk_xform."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("group", ctypes.c_int32),
+        ("w", ctypes.c_void_p),
+        ("z", ctypes.c_void_p),
+        ("seg_weights", ctypes.c_void_p),
+    ]
+
+
+XFORM_NONE, XFORM_RMS, XFORM_GATED_RMS, XFORM_SWIGLU = range(4)
+
+
 class Q3xkError(RuntimeError):
     def __init__(self, status: int, what: str):
         self.status = status
@@ -51,6 +66,14 @@ _SIGNATURES = {
     "q3xk_repack": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p]),
     "q3xk_gemv": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
                                  ctypes.c_int, ctypes.c_void_p]),
+    "q3xk_gemv_ex": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int, ctypes.POINTER(XForm), ctypes.c_void_p]),
+    "q3xk_expert_gemv_rows_ex": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
+                                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                ctypes.POINTER(XForm), ctypes.c_void_p]),
+    "q3xk_expert_gemv_segments_ex": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
+                                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                    ctypes.POINTER(XForm), ctypes.c_void_p]),
     "q3xk_expert_gemv": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "q3xk_try_mv_host": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_void_p,

@@ -23,6 +23,13 @@ inline int last_launch_status() {
     return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
 }
 
+// The reference's sigmoid (engine.cpp:187-191): same branches, CUDA's expf.
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+    const float e = expf(x);
+    return e / (1.0f + e);
+}
+
 // Bytes of the quantised part of one row record.
 __host__ __device__ inline int64_t quant_bytes(int type, int cols) {
     return type == Q3XK_Q8_0 ? (int64_t)cols : type == Q3XK_Q4_0 ? (int64_t)cols / 2

@@ -111,7 +111,8 @@ struct Layer {
     q3xk_matrix out{};      // delta.out / attention.out
     float *conv = nullptr, *alog = nullptr, *dt = nullptr, *dnorm = nullptr;  // DeltaNet
     float *qn1 = nullptr, *kn1 = nullptr;                                     // attention
-    q3xk_matrix gate_up{};  // FFN [gate | up]; MoE pool [experts + 1][2I] (shared last)
+    q3xk_matrix gate_up{};  // FFN gate|up, rows interleaved g g u u (repack_swiglu);
+                            // MoE pool [experts + 1][2I] the same way (shared expert last)
     q3xk_matrix down{};     // FFN down; MoE pool [experts + 1][H]
     q3xk_matrix router{};   // MoE: BF16 [experts + 1][H] = router rows + shared gate row
 };
@@ -168,7 +169,8 @@ struct State {
     void* argmax_ws = nullptr;
     size_t argmax_ws_bytes = 0;
     float *hidden = nullptr, *normed = nullptr, *proj = nullptr, *mix = nullptr, *part = nullptr;
-    float *rlogits = nullptr, *rweights = nullptr, *gu = nullptr, *hbuf = nullptr;
+    float *rlogits = nullptr, *rweights = nullptr, *hbuf = nullptr;
+    float* delta_work = nullptr;  // chunked DeltaNet workspace (prefill)
     int* rids = nullptr;
     void* gemm_ws = nullptr;
     size_t gemm_ws_bytes = 0;
@@ -290,6 +292,26 @@ struct Loader {
         const int st = q3xk_repack(&d, staging, stream);
         if (st != Q3XK_OK) status = st;
     }
+    // Packed [gate | up] rows (src_rows of them, counted from row_offset) into
+    // dst with the SwiGLU row interleave (repack_swiglu).
+    void upload_swiglu(const q3xk_matrix& dst, const uint8_t* src, int64_t src_rows, int half, int row_offset) {
+        if (pass == 0 || status != Q3XK_OK) return;
+        size_t bytes = 0;
+        if (dst.type == Q3XK_BF16)
+            bytes = (size_t)src_rows * dst.cols * 2;
+        else if (q3xk_quantized_bytes(dst.type, 1, dst.cols, &bytes) == Q3XK_OK)
+            bytes *= (size_t)src_rows;
+        if (bytes > staging_bytes) {
+            status = Q3XK_EINVAL;
+            return;
+        }
+        if (cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+            status = Q3XK_ECUDA;
+            return;
+        }
+        const int st = repack_swiglu(&dst, staging, src_rows, half, row_offset, stream);
+        if (st != Q3XK_OK) status = st;
+    }
     void need_staging(int type, int rows, int cols) {
         size_t b = 0;
         if (type == Q3XK_BF16)
@@ -373,17 +395,17 @@ struct Loader {
                 l.router = matrix(Q3XK_BF16, E + 1, c.H, 1);
                 upload(view(l.router, 0, 0, E), packed(Q3XK_BF16, E, c.H), 1);
                 l.gate_up = matrix(type, 2 * c.I, c.H, E + 1);
-                upload(view(l.gate_up, 0, 0, 2 * c.I), packed(type, E * 2 * c.I, c.H), E);
+                upload_swiglu(l.gate_up, packed(type, E * 2 * c.I, c.H), (int64_t)E * 2 * c.I, c.I, 0);
                 l.down = matrix(type, c.H, c.I, E + 1);
                 upload(view(l.down, 0, 0, c.H), packed(type, E * c.H, c.I), E);
-                upload(view(l.gate_up, E, 0, c.I), packed(type, c.shared_I, c.H), 1);
-                upload(view(l.gate_up, E, c.I, c.I), packed(type, c.shared_I, c.H), 1);
+                upload_swiglu(view(l.gate_up, E, 0, 2 * c.I), packed(type, c.shared_I, c.H), c.I, c.I, 0);
+                upload_swiglu(view(l.gate_up, E, 0, 2 * c.I), packed(type, c.shared_I, c.H), c.I, c.I, c.I);
                 upload(view(l.down, E, 0, c.H), packed(type, c.H, c.shared_I), 1);
                 upload(view(l.router, 0, E, 1), packed(Q3XK_BF16, 1, c.H), 1);
             } else {
                 l.gate_up = matrix(type, 2 * c.I, c.H, 1);
-                upload(view(l.gate_up, 0, 0, c.I), packed(type, c.I, c.H), 1);
-                upload(view(l.gate_up, 0, c.I, c.I), packed(type, c.I, c.H), 1);
+                upload_swiglu(l.gate_up, packed(type, c.I, c.H), c.I, c.I, 0);
+                upload_swiglu(l.gate_up, packed(type, c.I, c.H), c.I, c.I, c.I);
                 l.down = matrix(type, c.H, c.I, 1);
                 upload(l.down, packed(type, c.H, c.I), 1);
             }
@@ -474,8 +496,118 @@ int mm(State& s, const q3xk_matrix& w, const float* X, int T, float* Y, int accu
     return q3xk_gemm(&w, X, T, Y, accumulate, s.gemm_ws, s.gemm_ws_bytes, s.stream);
 }
 
-// One pass over T <= kChunk tokens already in s.tokens (engine.cpp:431-458).
+q3xk_xform rms_xf(const float* w1) {
+    q3xk_xform xf{};
+    xf.kind = Q3XK_XFORM_RMS;
+    xf.w = w1;
+    return xf;
+}
+
+// Measured on B200 (9B-shaped decode, 512-token context): RMSNorm and the
+// DeltaNet gated RMS as separate kernels 2.88 ms/token; fused into the
+// consuming GEMVs' staging of x (every CTA recomputes the statistics) 3.20 ms.
+#ifndef Q3XB_FUSE_RMS
+#define Q3XB_FUSE_RMS 0
+#endif
+#ifndef Q3XB_FUSE_GATED
+#define Q3XB_FUSE_GATED 0
+#endif
+
+// Input of a decode GEMV that reads RMSNorm(x) (engine.cpp:231-236): with
+// Q3XB_FUSE_RMS the GEMV normalises x while staging it (*xf is set), else
+// the norm runs as its own kernel into `normed` (returned).
+int rms_input(State& s, const float* x, const float* w1, int n, q3xk_xform* xf, const float** in) {
+    if (Q3XB_FUSE_RMS) {
+        *xf = rms_xf(w1);
+        *in = x;
+        return Q3XK_OK;
+    }
+    *xf = q3xk_xform{};
+    *in = s.normed;
+    return launch_rms(x, w1, n, 1, s.normed, s.stream);
+}
+
+// MoE FFN of token t (engine.cpp:406-430): router logits (+ the shared-expert
+// gate as one more row) from RMS(hidden_t), device top-k, gate|up rows of the
+// selected experts with the weighted SwiGLU in their epilogue, then the down
+// projections of all slots added to hidden_t.
+int moe_token(State& s, const Config& c, const Layer& l, int t) {
+    const cudaStream_t st = s.stream;
+    const int S = c.top_k + 1;  // routed slots + the shared expert
+    float* h = s.hidden + (size_t)t * c.H;
+    q3xk_xform xr;
+    const float* in = nullptr;
+    Q3XB_TRY(rms_input(s, h, l.post_norm, c.H, &xr, &in));
+    Q3XB_TRY(q3xk_gemv_ex(&l.router, in, s.rlogits, 0, &xr, st));
+    Q3XB_TRY(q3xk_router_topk(s.rlogits, c.experts, c.top_k, 1, s.rids, s.rweights, st));
+    Q3XB_TRY(gemv_swiglu(&l.gate_up, in, s.hbuf, s.rids, S, s.rweights, &xr, st));
+    return q3xk_expert_gemv_segments(&l.down, s.rids, S, s.hbuf, h, 1, st);
+}
+
+// One decode token (T = 1): every elementwise step that feeds a GEMV is
+// fused into that GEMV's staging of x (RMSNorm, DeltaNet gated RMS, SwiGLU);
+// residual adds are the GEMVs' accumulate.
+int forward_token(Model& m, State& s, bool logits) {
+    const Config& c = *m.config;
+    const cudaStream_t st = s.stream;
+    const int DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO, AS = c.AH * c.AD;
+    Q3XB_TRY(launch_embed(m.embedding, s.tokens, 1, s.hidden, st));
+    int di = 0, ai = 0;
+    for (int i = 0; i < c.N; ++i) {
+        const Layer& l = m.layer[i];
+        const int P = l.in_proj.rows;
+        q3xk_xform xin;
+        const float* in = nullptr;
+        Q3XB_TRY(rms_input(s, s.hidden, l.in_norm, c.H, &xin, &in));
+        Q3XB_TRY(q3xk_gemv_ex(&l.in_proj, in, s.proj, 0, &xin, st));
+        if (l.delta) {
+            Q3XB_TRY(launch_conv(s.proj, P, 1, DQKV, l.conv, c.CK, s.conv[di], st));
+            const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
+            // the gated RMS runs in the out projection's staging of x (Q3XB_FUSE_GATED) or in the delta kernel
+            Q3XB_TRY(launch_delta(s.proj, P, 1, dd, l.alog, l.dt, Q3XB_FUSE_GATED ? nullptr : l.dnorm, s.memory[di],
+                                  s.mix, DO, st));
+            q3xk_xform xg{};
+            if (Q3XB_FUSE_GATED) {
+                xg.kind = Q3XK_XFORM_GATED_RMS;
+                xg.group = c.VD;
+                xg.w = l.dnorm;
+                xg.z = s.proj + DQKV;
+            }
+            Q3XB_TRY(q3xk_gemv_ex(&l.out, s.mix, s.hidden, 1, &xg, st));
+            ++di;
+        } else {
+            const AttnDims ad{c.AH, c.KVH, c.AD, c.RD};
+            Q3XB_TRY(launch_attention(s.proj, P, 1, ad, l.qn1, l.kn1, s.pos, s.kcache[ai], s.vcache[ai], s.capacity,
+                                      s.part, s.split_len, s.mix, AS, st));
+            Q3XB_TRY(q3xk_gemv(&l.out, s.mix, s.hidden, 1, st));
+            ++ai;
+        }
+        if (c.experts) {
+            Q3XB_TRY(moe_token(s, c, l, 0));
+        } else {
+            q3xk_xform xpost;
+            const float* pin = nullptr;
+            Q3XB_TRY(rms_input(s, s.hidden, l.post_norm, c.H, &xpost, &pin));
+            Q3XB_TRY(gemv_swiglu(&l.gate_up, pin, s.mix, nullptr, 0, nullptr, &xpost, st));
+            Q3XB_TRY(q3xk_gemv(&l.down, s.mix, s.hidden, 1, st));
+        }
+    }
+    if (logits) {
+        q3xk_xform xf;
+        const float* fin = nullptr;
+        Q3XB_TRY(rms_input(s, s.hidden, m.final_norm, c.H, &xf, &fin));
+        Q3XB_TRY(q3xk_gemv_ex(&m.lm_head, fin, s.logits, 0, &xf, st));
+    }
+    return launch_advance(s.pos, 1, st);
+}
+
+// One pass over T <= chunk tokens already in s.tokens (engine.cpp:431-458).
+#ifndef Q3XB_FUSED_DECODE
+#define Q3XB_FUSED_DECODE 1
+#endif
+
 int forward_chunk(Model& m, State& s, int T, bool logits) {
+    if (Q3XB_FUSED_DECODE && T == 1 && !s.exact_prefill) return forward_token(m, s, logits);
     const Config& c = *m.config;
     const cudaStream_t st = s.stream;
     const int H = c.H, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO, AS = c.AH * c.AD;
@@ -489,7 +621,8 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
         if (l.delta) {
             Q3XB_TRY(launch_conv(s.proj, P, T, DQKV, l.conv, c.CK, s.conv[di], st));
             const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
-            Q3XB_TRY(launch_delta(s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di], s.mix, DO, st));
+            Q3XB_TRY(launch_delta_chunked(s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di], s.mix, DO,
+                                          s.delta_work, st));
             Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
             ++di;
         } else {
@@ -499,26 +632,18 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
             Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
             ++ai;
         }
-        Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
         if (c.experts) {
-            const int S = c.top_k + 1;  // routed slots + the shared expert
-            for (int t = 0; t < T; ++t) {
-                const float* x = s.normed + (size_t)t * H;
-                Q3XB_TRY(q3xk_gemv(&l.router, x, s.rlogits, 0, st));
-                Q3XB_TRY(q3xk_router_topk(s.rlogits, c.experts, c.top_k, 1, s.rids, s.rweights, st));
-                Q3XB_TRY(q3xk_expert_gemv_rows(&l.gate_up, s.rids, S, x, s.gu, 0, st));
-                Q3XB_TRY(q3xk_swiglu(s.gu, s.rweights, S, c.I, s.hbuf, st));
-                Q3XB_TRY(q3xk_expert_gemv_segments(&l.down, s.rids, S, s.hbuf, s.hidden + (size_t)t * H, 1, st));
-            }
+            for (int t = 0; t < T; ++t) Q3XB_TRY(moe_token(s, c, l, t));
         } else {
+            Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
             Q3XB_TRY(mm(s, l.gate_up, s.normed, T, s.proj, 0));
             Q3XB_TRY(launch_ffn_swiglu(s.proj, 2 * c.I, T, c.I, s.mix, st));
             Q3XB_TRY(mm(s, l.down, s.mix, T, s.hidden, 1));
         }
     }
     if (logits) {
-        Q3XB_TRY(launch_rms(s.hidden + (size_t)(T - 1) * H, m.final_norm, H, 1, s.normed, st));
-        Q3XB_TRY(q3xk_gemv(&m.lm_head, s.normed, s.logits, 0, st));
+        const q3xk_xform xf = rms_xf(m.final_norm);
+        Q3XB_TRY(q3xk_gemv_ex(&m.lm_head, s.hidden + (size_t)(T - 1) * H, s.logits, 0, &xf, st));
     }
     return launch_advance(s.pos, T, st);
 }
@@ -590,8 +715,10 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
     if (ok && c.experts) {
         const int S = c.top_k + 1;
         ok = s->alloc(&s->rlogits, c.experts + 1) && s->alloc(&s->rweights, S) && s->alloc(&s->rids, S) &&
-             s->alloc(&s->gu, (size_t)S * 2 * c.I) && s->alloc(&s->hbuf, (size_t)S * c.I);
+             s->alloc(&s->hbuf, (size_t)S * c.I);
     }
+    if (ok && chunk > 1 && delta_layers > 0)
+        ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4);
     if (ok) {
         q3xk_argmax_workspace_bytes(&s->argmax_ws_bytes);
         uint8_t* ws = nullptr;

@@ -30,6 +30,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "layers.cuh"
 
 namespace q3xk {
 namespace {
@@ -39,6 +40,17 @@ namespace {
 #endif
 #ifndef Q3XK_GEMV_MIN_BLOCKS
 #define Q3XK_GEMV_MIN_BLOCKS 3
+#endif
+// 1: the first row group's weights are prefetched into L2 before the
+// prologue (no registers held across it) and loaded after it;
+// 0: they are loaded into registers before the prologue.
+#ifndef Q3XK_GEMV_PREFETCH
+#define Q3XK_GEMV_PREFETCH 0
+#endif
+// Batches ahead of the one being loaded whose weights are prefetched into
+// L2 (no registers held), so DRAM keeps streaming while a warp computes.
+#ifndef Q3XK_GEMV_L2_AHEAD
+#define Q3XK_GEMV_L2_AHEAD 0
 #endif
 
 constexpr int kThreads = 256;
@@ -78,7 +90,20 @@ struct GemvParams {
     int64_t expert_stride;
     int rows_per_expert;  // row gather: virtual row r = expert ids[r / rpe], row r % rpe
     int units_per_seg;    // segment gather: unit u reads expert ids[u / ups]
+    // Input transform applied while x is staged (q3xk_xform): x_eff = f(x).
+    int xform;
+    const float* xw;   // RMS: (1 + w)[cols]; gated RMS: norm[group]
+    const float* xz;   // gated RMS: gate z[cols]
+    const float* xsw;  // SwiGLU: per-segment weights (or null)
+    int xgroup;        // gated RMS: group size; SwiGLU: width W of [g | u] pairs
+    // Epilogue: 1 = SwiGLU over interleaved rows (g g u u per 4-row group),
+    // y[row / 2 + {0,1}] = (ew[slot] *) silu(g) * u.
+    int epi;
+    const float* ew;
 };
+
+constexpr int kMaxXGroups = 64;
+constexpr float kXEps = 1e-6f;  // engine.cpp:27
 
 // Row addressing modes of the GEMV kernel.
 enum GemvMode { kPlain = 0, kRowGather = 1, kSegGather = 2 };
@@ -240,6 +265,31 @@ __device__ __forceinline__ void load_batch(Batch<TYPE>& bt, const GemvParams& p,
     }
 }
 
+template <int TYPE, int KS, int MODE>
+__device__ __forceinline__ void prefetch_batch(const GemvParams& p, const uint8_t* const* rec, int lane, int ks,
+                                               const int64_t* seg_off, int b = 0) {
+    constexpr int kBatch = Codec<TYPE>::kBatch;
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+        int u = unit_of(lane, b, i, kBatch, ks, KS);
+        if (u < p.units) {
+            int64_t off = 0;
+            if (MODE == kSegGather) {
+                const int seg = u / p.units_per_seg;
+                off = seg_off[seg];
+                u -= seg * p.units_per_seg;
+            }
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(rec[j] + off + (int64_t)u * 16));
+                if (TYPE != Q3XK_BF16 && (u % (8 * Codec<TYPE>::kUnitsPerBlock)) == 0)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(rec[j] + off + p.qbytes +
+                                                                  2 * (u / Codec<TYPE>::kUnitsPerBlock)));
+            }
+        }
+    }
+}
+
 // Returns this warp's partial sum of row (b4 ? 2 : 0) + (b3 ? 1 : 0) in lanes
 // 0, 8, 16 and 24 (transposed butterfly over the 4 rows).
 template <int TYPE, bool FAST, int KS, int MODE>
@@ -255,7 +305,9 @@ __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* c
     const int span = 32 * kBatch * KS;
     const int nb = (p.units + span - 1) / span;  // batches per row group and slice
     for (int b = 0; b < nb; ++b) {
-        if (b > 0) load_batch<TYPE, KS, MODE>(A, p, rec, lane, b, ks, seg_off);
+        if (Q3XK_GEMV_L2_AHEAD && b + Q3XK_GEMV_L2_AHEAD < nb)
+            prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off, b + Q3XK_GEMV_L2_AHEAD);
+        if (b > 0 || Q3XK_GEMV_PREFETCH) load_batch<TYPE, KS, MODE>(A, p, rec, lane, b, ks, seg_off);
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
             const int u = unit_of(lane, b, i, kBatch, ks, KS);
@@ -286,7 +338,98 @@ __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* c
     return k;
 }
 
-template <int TYPE, int KS, int MODE>
+// Writes elements [u N, u N + N) of the transformed input vector, in natural
+// order, to dst (the unit's own slot of the staging area), 4 at a time:
+//   RMS        x * scale * w1                 (engine.cpp:231-236, w1 = 1 + w')
+//   gated RMS  x * (scale_g * norm * silu(z)) (engine.cpp:237-242), per group
+//   SwiGLU     [wt_s *] silu(g) * u           (engine.cpp:374, :415-416)
+template <int N>
+__device__ __forceinline__ void stage_x(const GemvParams& p, int u, float* dst, const float* xstat) {
+    const int e0 = u * N;  // every group / pair width is a multiple of N
+    if (p.xform == Q3XK_XFORM_SWIGLU) {
+        const int seg = e0 / p.xgroup;
+        const float* g = p.x + e0 + seg * p.xgroup;  // g of pair `seg`; u follows at + W
+        const float wt = p.xsw ? __ldg(p.xsw + seg) : 1.f;
+#pragma unroll 2
+        for (int i = 0; i < N / 4; ++i) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(g) + i);
+            const float4 b = __ldg(reinterpret_cast<const float4*>(g + p.xgroup) + i);
+            float4 h = make_float4(a.x * sigmoid_ref(a.x) * b.x, a.y * sigmoid_ref(a.y) * b.y,
+                                   a.z * sigmoid_ref(a.z) * b.z, a.w * sigmoid_ref(a.w) * b.w);
+            if (p.xsw) h = make_float4(wt * h.x, wt * h.y, wt * h.z, wt * h.w);
+            reinterpret_cast<float4*>(dst)[i] = h;
+        }
+    } else if (p.xform == Q3XK_XFORM_RMS) {
+        const float scale = xstat[0];
+#pragma unroll 2
+        for (int i = 0; i < N / 4; ++i) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(p.x + e0) + i);
+            const float4 w = __ldg(reinterpret_cast<const float4*>(p.xw + e0) + i);
+            reinterpret_cast<float4*>(dst)[i] =
+                make_float4(a.x * scale * w.x, a.y * scale * w.y, a.z * scale * w.z, a.w * scale * w.w);
+        }
+    } else {  // gated RMS
+        const int g = e0 / p.xgroup, k0 = e0 - g * p.xgroup;
+        const float scale = xstat[g];
+#pragma unroll 2
+        for (int i = 0; i < N / 4; ++i) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(p.x + e0) + i);
+            const float4 z = __ldg(reinterpret_cast<const float4*>(p.xz + e0) + i);
+            const float4 n = __ldg(reinterpret_cast<const float4*>(p.xw + k0) + i);
+            reinterpret_cast<float4*>(dst)[i] = make_float4(
+                a.x * (scale * n.x * (z.x * sigmoid_ref(z.x))), a.y * (scale * n.y * (z.y * sigmoid_ref(z.y))),
+                a.z * (scale * n.z * (z.z * sigmoid_ref(z.z))), a.w * (scale * n.w * (z.w * sigmoid_ref(z.w))));
+        }
+    }
+}
+
+// Elements [u N, u N + N) of the GEMV input: straight from x, or (XF) from
+// the unit's staging slot that stage_x filled.
+template <int N, bool XF>
+__device__ __forceinline__ void unit_x(const GemvParams& p, int u, float (&v)[N], const float4* slot) {
+    const float4* src = XF ? slot : reinterpret_cast<const float4*>(p.x + (int64_t)u * N);
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+        const float4 t = XF ? src[i] : __ldg(src + i);
+        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+}
+
+// Statistics of the input transform, once per CTA into xstat (shared):
+// RMS: xstat[0] = 1 / sqrt(mean(x^2) + eps); gated RMS: the same per group.
+__device__ __forceinline__ void x_stats(const GemvParams& p, float* xstat, float* red) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (p.xform == Q3XK_XFORM_RMS) {
+        float ss = 0.f;
+        for (int k = tid * 4; k < p.cols; k += kThreads * 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(p.x + k));
+            ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.f;
+            for (int w = 0; w < kWarps; ++w) t += red[w];
+            xstat[0] = 1.0f / sqrtf(t / (float)p.cols + kXEps);
+        }
+    } else if (p.xform == Q3XK_XFORM_GATED_RMS) {
+        const int G = p.xgroup, groups = p.cols / G;
+        for (int g = warp; g < groups; g += kWarps) {
+            float ss = 0.f;
+            for (int k = lane; k < G; k += 32) {
+                const float t = __ldg(p.x + (int64_t)g * G + k);
+                ss += t * t;
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) xstat[g] = 1.0f / sqrtf(ss / (float)G + kXEps);
+        }
+    }
+    __syncthreads();
+}
+
+// XF: the input transform is compiled in (p.xform may be non-zero).
+template <int TYPE, int KS, int MODE, bool XF>
 __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(const GemvParams p) {
     using C = Codec<TYPE>;
     static_assert(kRows == 4, "the transposed row reduction is written for 4 rows");
@@ -308,7 +451,11 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
 #pragma unroll
         for (int j = 0; j < kRows; ++j) rec[j] = p.w + (int64_t)min(row0 + j, p.rows - 1) * p.row_stride;
         // The first batch of weights is requested before waiting on the previous kernel.
+#if Q3XK_GEMV_PREFETCH
+        if (row0 < p.rows) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
+#else
         if (row0 < p.rows) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+#endif
         griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
     } else {
         griddep_wait();  // the expert ids come from the previous kernel
@@ -325,19 +472,22 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
             else
                 rec[j] = p.w + (int64_t)row * p.row_stride;
         }
+#if Q3XK_GEMV_PREFETCH
+        if (row0 < p.rows) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
+#else
         if (row0 < p.rows) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+#endif
     }
+
+    __shared__ float xstat[XF ? kMaxXGroups : 1], xred[kWarps];
+    if (XF && (p.xform == Q3XK_XFORM_RMS || p.xform == Q3XK_XFORM_GATED_RMS)) x_stats(p, xstat, xred);
 
     // Prescale x per unit into shared memory (16-byte chunks, swizzled).
     int slow = 0;
     for (int u = tid; u < p.units; u += kThreads) {
-        const float* xu = p.x + (int64_t)u * C::kCols;
         float v[C::kCols];
-#pragma unroll
-        for (int i = 0; i < C::kCols / 4; ++i) {
-            const float4 t = __ldg(reinterpret_cast<const float4*>(xu) + i);
-            v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
-        }
+        if (XF) stage_x<C::kCols>(p, u, reinterpret_cast<float*>(xs4 + u * C::kChunks), xstat);
+        unit_x<C::kCols, XF>(p, u, v, xs4 + u * C::kChunks);
         int P = 0;
         float2 gu = f2(1.f, 0.f);
         if (TYPE != Q3XK_BF16) {
@@ -370,12 +520,14 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
     if (any_slow) {
         // Exact fallback for the whole CTA: unscaled x in the same slot order.
         for (int u = tid; u < p.units; u += kThreads) {
-            const float* xu = p.x + (int64_t)u * C::kCols;
+            float v[C::kCols];
+            if (XF) stage_x<C::kCols>(p, u, reinterpret_cast<float*>(xs4 + u * C::kChunks), xstat);
+            unit_x<C::kCols, XF>(p, u, v, xs4 + u * C::kChunks);
 #pragma unroll
             for (int j = 0; j < C::kChunks; ++j)
                 xs4[u * C::kChunks + swz<TYPE>(u, j)] =
-                    make_float4(xu[C::element(4 * j)], xu[C::element(4 * j + 1)],
-                                xu[C::element(4 * j + 2)], xu[C::element(4 * j + 3)]);
+                    make_float4(v[C::element(4 * j)], v[C::element(4 * j + 1)],
+                                v[C::element(4 * j + 2)], v[C::element(4 * j + 3)]);
         }
         __syncthreads();
         if (row0 < p.rows) k = warp_rows<TYPE, false, KS, MODE>(p, rec, lane, ks, A, xs4, gg, seg_off);
@@ -384,6 +536,15 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
     }
     const int r = (lane & 16 ? 2 : 0) + (lane & 8 ? 1 : 0);
     if (KS == 1) {
+        if (p.epi) {
+            const float u = __shfl_down_sync(0xffffffffu, k, 16);  // lanes 0, 8 <- rows 2, 3
+            if ((lane == 0 || lane == 8) && row0 < p.rows) {
+                float h = k * sigmoid_ref(k) * u;
+                if (p.ew) h = __ldg(p.ew + row0 / p.rows_per_expert) * h;
+                p.y[row0 / 2 + (lane >> 3)] = h;
+            }
+            return;
+        }
         if ((lane & 7) == 0 && row0 + r < p.rows) {
             float* yp = p.y + row0 + r;
             *yp = p.accumulate ? *yp + k : k;
@@ -393,6 +554,24 @@ __global__ void __launch_bounds__(kThreads, Q3XK_GEMV_MIN_BLOCKS) gemv_kernel(co
     // Slices of a row group meet in shared memory, added in slice order.
     if ((lane & 7) == 0) part[warp * kRows + r] = k;
     __syncthreads();
+    if (p.epi) {
+        if (tid < groups_per_cta * 2) {
+            const int g = tid / 2, rr = tid % 2;
+            const int grow = (blockIdx.x * groups_per_cta + g) * kRows;
+            if (grow < p.rows) {
+                float vg = 0.f, vu = 0.f;
+#pragma unroll
+                for (int s = 0; s < KS; ++s) {
+                    vg += part[(g * KS + s) * kRows + rr];
+                    vu += part[(g * KS + s) * kRows + rr + 2];
+                }
+                float h = vg * sigmoid_ref(vg) * vu;
+                if (p.ew) h = __ldg(p.ew + grow / p.rows_per_expert) * h;
+                p.y[grow / 2 + rr] = h;
+            }
+        }
+        return;
+    }
     if (tid < groups_per_cta * kRows) {
         const int g = tid / kRows, rr = tid % kRows;
         const int row = (blockIdx.x * groups_per_cta + g) * kRows + rr;
@@ -420,7 +599,11 @@ int sm_count_cached() {
 // fill the GPU: the smallest split (1, 2, 4) whose grid keeps at least half
 // of the resident CTA slots busy.  Every CTA prescales all of x, so small
 // CTAs (large splits) pay that prologue over fewer rows.
+#ifndef Q3XK_GEMV_FORCE_KS
+#define Q3XK_GEMV_FORCE_KS 0  // tuning builds only: fixed K split (1, 2, 4, 8)
+#endif
 int choose_ksplit(int rows, int units, int slots) {
+    if (Q3XK_GEMV_FORCE_KS) return units >= 32 * Q3XK_GEMV_FORCE_KS ? Q3XK_GEMV_FORCE_KS : 1;
     for (int ks = 1; ks <= 4; ks *= 2) {
         if (ks > 1 && units < 32 * ks) return ks / 2;
         const int64_t per = (int64_t)(kWarps / ks) * kRows;
@@ -436,11 +619,11 @@ size_t smem_bytes(const GemvParams& p) {
     return (size_t)p.units * Codec<TYPE>::kCols * 4 + (size_t)p.units * 8 + kWarps * kRows * 4;
 }
 
-template <int TYPE, int KS, int MODE>
+template <int TYPE, int KS, int MODE, bool XF>
 int launch_ks(const GemvParams& p, size_t smem, cudaStream_t s) {
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
-        if (cudaFuncSetAttribute(gemv_kernel<TYPE, KS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(gemv_kernel<TYPE, KS, MODE, XF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  200 * 1024) != cudaSuccess)
             return Q3XK_ECUDA;
         configured = 200 * 1024;
@@ -448,24 +631,30 @@ int launch_ks(const GemvParams& p, size_t smem, cudaStream_t s) {
     constexpr int rows_per_cta = (kWarps / KS) * kRows;
     const int64_t grid = (p.rows + rows_per_cta - 1) / rows_per_cta;
 #if Q3XK_GEMV_PDL
-    const cudaError_t e = launch_pdl(gemv_kernel<TYPE, KS, MODE>, dim3((unsigned)grid), dim3(kThreads), smem, s, p);
+    const cudaError_t e =
+        launch_pdl(gemv_kernel<TYPE, KS, MODE, XF>, dim3((unsigned)grid), dim3(kThreads), smem, s, p);
 #else
-    gemv_kernel<TYPE, KS, MODE><<<(unsigned)grid, kThreads, smem, s>>>(p);
+    gemv_kernel<TYPE, KS, MODE, XF><<<(unsigned)grid, kThreads, smem, s>>>(p);
     const cudaError_t e = cudaGetLastError();
 #endif
     return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
+}
+
+template <int TYPE, int MODE, bool XF>
+int launch_xf(const GemvParams& p, size_t smem, cudaStream_t s) {
+    switch (p.ksplit) {
+    case 1: return launch_ks<TYPE, 1, MODE, XF>(p, smem, s);
+    case 2: return launch_ks<TYPE, 2, MODE, XF>(p, smem, s);
+    case 4: return launch_ks<TYPE, 4, MODE, XF>(p, smem, s);
+    default: return launch_ks<TYPE, 8, MODE, XF>(p, smem, s);
+    }
 }
 
 template <int TYPE, int MODE>
 int launch(const GemvParams& p, cudaStream_t s) {
     const size_t smem = smem_bytes<TYPE>(p);
     if (smem > 200 * 1024) return Q3XK_EUNSUPPORTED;
-    switch (p.ksplit) {
-    case 1: return launch_ks<TYPE, 1, MODE>(p, smem, s);
-    case 2: return launch_ks<TYPE, 2, MODE>(p, smem, s);
-    case 4: return launch_ks<TYPE, 4, MODE>(p, smem, s);
-    default: return launch_ks<TYPE, 8, MODE>(p, smem, s);
-    }
+    return p.xform ? launch_xf<TYPE, MODE, true>(p, smem, s) : launch_xf<TYPE, MODE, false>(p, smem, s);
 }
 
 template <int MODE>
@@ -503,12 +692,41 @@ GemvParams base_params(const q3xk_matrix* m, const uint8_t* base, const float* x
     return p;
 }
 
+// Validates `xf` for a matrix of `cols` inputs (per segment) and fills p.
+int set_xform(GemvParams& p, const q3xk_xform* xf, int cols, int mode) {
+    if (!xf || xf->kind == Q3XK_XFORM_NONE) return Q3XK_OK;
+    switch (xf->kind) {
+    case Q3XK_XFORM_RMS:
+        if (!xf->w || mode == kSegGather) return Q3XK_EINVAL;
+        break;
+    case Q3XK_XFORM_GATED_RMS:
+        if (!xf->w || !xf->z || xf->group <= 0 || xf->group % 32 || cols % xf->group) return Q3XK_EINVAL;
+        if (cols / xf->group > kMaxXGroups || mode != kPlain) return Q3XK_EUNSUPPORTED;
+        break;
+    case Q3XK_XFORM_SWIGLU:
+        if (xf->group != cols) return Q3XK_EINVAL;
+        if (mode == kRowGather) return Q3XK_EUNSUPPORTED;
+        break;
+    default:
+        return Q3XK_EINVAL;
+    }
+    if (((uintptr_t)xf->w & 15) || ((uintptr_t)xf->z & 15)) return Q3XK_EALIGN;
+    p.xform = xf->kind;
+    p.xgroup = xf->group;
+    p.xw = xf->w;
+    p.xz = xf->z;
+    p.xsw = xf->seg_weights;
+    return Q3XK_OK;
+}
+
 int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* y,
-              int accumulate, cudaStream_t s) {
+              int accumulate, cudaStream_t s, const q3xk_xform* xf = nullptr) {
     int st = check_matrix(m);
     if (st != Q3XK_OK || !base || !x || !y) return Q3XK_EINVAL;
     if (((uintptr_t)base & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
     GemvParams p = base_params(m, base, x, y, accumulate);
+    st = set_xform(p, xf, m->cols, kPlain);
+    if (st != Q3XK_OK) return st;
     p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * Q3XK_GEMV_MIN_BLOCKS);
     st = launch_type<kPlain>(m->type, p, s);
     if (st != Q3XK_OK) return st;
@@ -517,6 +735,30 @@ int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* 
 }
 
 }  // namespace
+
+int gemv_swiglu(const q3xk_matrix* m, const float* x, float* y, const int* ids, int slots, const float* slot_w,
+                const q3xk_xform* xf, cudaStream_t s) {
+    int st = check_matrix(m);
+    if (st != Q3XK_OK || !x || !y || m->rows % 4) return Q3XK_EINVAL;
+    if (((uintptr_t)m->data & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
+    GemvParams p = base_params(m, static_cast<const uint8_t*>(m->data), x, y, 0);
+    st = set_xform(p, xf, m->cols, ids ? kRowGather : kPlain);
+    if (st != Q3XK_OK) return st;
+    p.epi = 1;
+    p.rows_per_expert = m->rows;
+    if (ids) {
+        if (slots <= 0 || m->expert_stride != m->row_stride * m->rows) return Q3XK_EINVAL;
+        p.ids = ids;
+        p.rows = m->rows * slots;
+        p.ew = slot_w;
+    }
+    p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * Q3XK_GEMV_MIN_BLOCKS);
+    st = ids ? launch_type<kRowGather>(m->type, p, s) : launch_type<kPlain>(m->type, p, s);
+    if (st != Q3XK_OK) return st;
+    count_launch();
+    return last_launch_status();
+}
+
 }  // namespace q3xk
 
 using namespace q3xk;
@@ -537,13 +779,27 @@ int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, float* y,
     return gemv_impl(w, base, x, y, accumulate, static_cast<cudaStream_t>(stream));
 }
 
+int q3xk_gemv_ex(const q3xk_matrix* w, const float* x, float* y, int accumulate, const q3xk_xform* xf,
+                 void* stream) {
+    if (!w) return Q3XK_EINVAL;
+    return gemv_impl(w, static_cast<const uint8_t*>(w->data), x, y, accumulate,
+                     static_cast<cudaStream_t>(stream), xf);
+}
+
 int q3xk_expert_gemv_rows(const q3xk_matrix* pool, const int* ids, int slots, const float* x, float* y,
                           int accumulate, void* stream) {
+    return q3xk_expert_gemv_rows_ex(pool, ids, slots, x, y, accumulate, nullptr, stream);
+}
+
+int q3xk_expert_gemv_rows_ex(const q3xk_matrix* pool, const int* ids, int slots, const float* x, float* y,
+                             int accumulate, const q3xk_xform* xf, void* stream) {
     int st = check_matrix(pool);
     if (st != Q3XK_OK || !ids || !x || !y || slots <= 0) return Q3XK_EINVAL;
     if (pool->expert_stride != pool->row_stride * pool->rows) return Q3XK_EINVAL;
     if (((uintptr_t)pool->data & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
     GemvParams p = base_params(pool, static_cast<const uint8_t*>(pool->data), x, y, accumulate);
+    st = set_xform(p, xf, pool->cols, kRowGather);
+    if (st != Q3XK_OK) return st;
     p.ids = ids;
     p.rows_per_expert = pool->rows;
     p.rows = pool->rows * slots;
@@ -556,12 +812,19 @@ int q3xk_expert_gemv_rows(const q3xk_matrix* pool, const int* ids, int slots, co
 
 int q3xk_expert_gemv_segments(const q3xk_matrix* pool, const int* ids, int slots, const float* x, float* y,
                               int accumulate, void* stream) {
+    return q3xk_expert_gemv_segments_ex(pool, ids, slots, x, y, accumulate, nullptr, stream);
+}
+
+int q3xk_expert_gemv_segments_ex(const q3xk_matrix* pool, const int* ids, int slots, const float* x, float* y,
+                                 int accumulate, const q3xk_xform* xf, void* stream) {
     int st = check_matrix(pool);
     if (st != Q3XK_OK || !ids || !x || !y || slots <= 0) return Q3XK_EINVAL;
     if (slots > kMaxSegments) return Q3XK_EUNSUPPORTED;
     if (pool->expert_stride != pool->row_stride * pool->rows) return Q3XK_EINVAL;
     if (((uintptr_t)pool->data & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return Q3XK_EALIGN;
     GemvParams p = base_params(pool, static_cast<const uint8_t*>(pool->data), x, y, accumulate);
+    st = set_xform(p, xf, pool->cols, kSegGather);
+    if (st != Q3XK_OK) return st;
     p.ids = ids;
     p.units_per_seg = p.units;
     p.units = p.units * slots;

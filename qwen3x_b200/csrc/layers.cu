@@ -78,27 +78,51 @@ __global__ void __launch_bounds__(256) rms_kernel(const float* __restrict__ x, c
 }
 
 // ---- causal conv1d over T tokens with SiLU and history (engine.cpp:264-273).
-// proj[t][c] for c < channels is replaced by the activated conv output.
+// proj[t][c] for c < channels is replaced by the activated conv output.  One
+// thread per channel; KC is the kernel width when known at compile time
+// (0: runtime `CK`, at most 9).
+template <int KC>
 __global__ void conv_kernel(float* __restrict__ proj, int64_t proj_stride, int T, int channels,
-                            const float* __restrict__ w /*[channels][CK]*/, int CK, float* __restrict__ hist) {
+                            const float* __restrict__ w /*[channels][CK]*/, int CK_rt, float* __restrict__ hist) {
     griddep_wait();
     griddep_launch_dependents();
+    const int CK = KC ? KC : CK_rt;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= channels) return;
-    float h[8];
+    float h[KC ? KC : 8], wc[KC ? KC + 1 : 9];
     float* hc = hist + (int64_t)c * (CK - 1);
-    for (int i = 0; i < CK - 1; ++i) h[i] = hc[i];
-    const float* wc = w + (int64_t)c * CK;
-    for (int t = 0; t < T; ++t) {
-        float* xp = proj + (int64_t)t * proj_stride + c;
-        const float x = *xp;
-        float sum = x * wc[CK - 1];
-        for (int i = 0; i < CK - 1; ++i) sum += h[i] * wc[i];
-        for (int i = 0; i < CK - 2; ++i) h[i] = h[i + 1];
-        h[CK - 2] = x;
-        *xp = siluf_ref(sum);
+#pragma unroll
+    for (int i = 0; i < (KC ? KC - 1 : 8); ++i)
+        if (i < CK - 1) h[i] = hc[i];
+#pragma unroll
+    for (int i = 0; i < (KC ? KC : 9); ++i)
+        if (i < CK) wc[i] = w[(int64_t)c * CK + i];
+    constexpr int kTile = 16;  // tokens whose inputs are loaded before any is written back
+    for (int t0 = 0; t0 < T; t0 += kTile) {
+        float xs[kTile];
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) xs[i] = t0 + i < T ? proj[(int64_t)(t0 + i) * proj_stride + c] : 0.f;
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) {
+            if (t0 + i >= T) break;  // T is uniform: no divergence
+            const float x = xs[i];
+            float sum = x * wc[CK - 1];
+#pragma unroll
+            for (int j = 0; j < (KC ? KC - 1 : 8); ++j)
+                if (j < CK - 1) sum += h[j] * wc[j];
+#pragma unroll
+            for (int j = 0; j < (KC ? KC - 2 : 7); ++j)
+                if (j < CK - 2) h[j] = h[j + 1];
+            h[CK - 2] = x;
+            xs[i] = siluf_ref(sum);
+        }
+#pragma unroll
+        for (int i = 0; i < kTile; ++i)
+            if (t0 + i < T) proj[(int64_t)(t0 + i) * proj_stride + c] = xs[i];
     }
-    for (int i = 0; i < CK - 1; ++i) hc[i] = h[i];
+#pragma unroll
+    for (int i = 0; i < (KC ? KC - 1 : 8); ++i)
+        if (i < CK - 1) hc[i] = h[i];
 }
 
 // ---- gated DeltaNet, one head per CTA, T tokens in order (engine.cpp:274-320).
@@ -173,12 +197,16 @@ __global__ void __launch_bounds__(kDeltaThreads) delta_kernel(const float* __res
 #pragma unroll
             for (int i = 0; i < G; ++i) ov += part[i][tid];
         }
-        // gated RMS: o * rsqrt(mean o^2 + eps) * norm * silu(z) (engine.cpp:237-242)
-        const float oss = block_sum<kDeltaThreads>(tid < VD ? ov * ov : 0.f, red);
-        if (tid < VD) {
-            const float scale = 1.0f / sqrtf(oss / (float)VD + kEps);
-            const float z = row[dd.z_off + head * VD + tid];
-            out[(int64_t)t * out_stride + head * VD + tid] = ov * (scale * norm[tid] * siluf_ref(z));
+        if (norm) {
+            // gated RMS: o * rsqrt(mean o^2 + eps) * norm * silu(z) (engine.cpp:237-242)
+            const float oss = block_sum<kDeltaThreads>(tid < VD ? ov * ov : 0.f, red);
+            if (tid < VD) {
+                const float scale = 1.0f / sqrtf(oss / (float)VD + kEps);
+                const float z = row[dd.z_off + head * VD + tid];
+                out[(int64_t)t * out_stride + head * VD + tid] = ov * (scale * norm[tid] * siluf_ref(z));
+            }
+        } else if (tid < VD) {
+            out[(int64_t)t * out_stride + head * VD + tid] = ov;  // gated RMS left to the out projection
         }
         __syncthreads();
     }
@@ -343,7 +371,148 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict
     }
 }
 
-// dense FFN SwiGLU over T tokens: out[t][i] = silu(g) * u, [g | u] = proj[t]
+// ---- causal attention for a prompt (T > 1): flash-style tiles on CUDA cores.
+// CTA = 64 query tokens of one query head; key/value tiles of 32 positions
+// stream through shared memory with an online softmax (engine.cpp:347-367
+// computes the same softmax(q.k / sqrt(AD)) V per token); the output is
+// already gated by sigmoid(gate) (engine.cpp:368).
+constexpr int kFBQ = 64, kFBK = 32, kFD = 256, kFLd = kFD + 4;
+constexpr size_t kFlashSmem = (size_t)(kFBQ * kFLd + kFBK * kFLd + kFBK * kFD + kFBQ * (kFBK + 1)) * 4;
+
+__global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restrict__ proj, int64_t proj_stride, int T,
+                                                           AttnDims ad, const int* __restrict__ pos,
+                                                           const float* __restrict__ kcache,
+                                                           const float* __restrict__ vcache, float* __restrict__ out,
+                                                           int64_t out_stride) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ __align__(16) float fsm[];
+    float* Qs = fsm;                 // [kFBQ][kFLd]
+    float* Ks = Qs + kFBQ * kFLd;    // [kFBK][kFLd]
+    float* Vs = Ks + kFBK * kFLd;    // [kFBK][kFD]
+    float* Ps = Vs + kFBK * kFD;     // [kFBQ][kFBK + 1]
+    const int qt = blockIdx.x, h = blockIdx.y;
+    const int G = ad.AH / ad.KVH, kvh = h / G;
+    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+    const int t0 = qt * kFBQ;
+    const int pos0 = *pos;
+    const int rows = min(kFBQ, T - t0);
+    const int last_key = pos0 + t0 + rows - 1;
+    const float inv = 1.0f / sqrtf((float)kFD);
+    // Q tile (already RMS-normalised and rotated by attn_prep_kernel)
+    for (int e = tid; e < kFBQ * kFD / 4; e += 256) {
+        const int r = e / (kFD / 4), d4 = e % (kFD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rows) v = reinterpret_cast<const float4*>(proj + (int64_t)(t0 + r) * proj_stride + (int64_t)h * 2 * kFD)[d4];
+        reinterpret_cast<float4*>(Qs + r * kFLd)[d4] = v;
+    }
+    const int r0 = ty * 2;  // this thread's two query rows; S keys tx + 8i; O dims tx*4 + 32j
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    float o[2][32];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[a][j] = 0.f;
+    const int qpos[2] = {pos0 + t0 + r0, pos0 + t0 + r0 + 1};
+    for (int k0 = 0; k0 <= last_key; k0 += kFBK) {
+        __syncthreads();  // previous tile consumed
+        for (int e = tid; e < kFBK * kFD / 4; e += 256) {
+            const int r = e / (kFD / 4), d4 = e % (kFD / 4);
+            const int j = k0 + r;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (j <= last_key) {
+                const int64_t off = ((int64_t)j * ad.KVH + kvh) * kFD;
+                kv = reinterpret_cast<const float4*>(kcache + off)[d4];
+                vv = reinterpret_cast<const float4*>(vcache + off)[d4];
+            }
+            reinterpret_cast<float4*>(Ks + r * kFLd)[d4] = kv;
+            reinterpret_cast<float4*>(Vs + r * kFD)[d4] = vv;
+        }
+        __syncthreads();
+        // S = Q K^T for rows r0, r0+1 and keys tx + 8i
+        float sc[2][4];
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sc[a][i] = 0.f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < kFD / 4; ++d4) {
+            const float4 q0 = reinterpret_cast<const float4*>(Qs + r0 * kFLd)[d4];
+            const float4 q1 = reinterpret_cast<const float4*>(Qs + (r0 + 1) * kFLd)[d4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 kk = reinterpret_cast<const float4*>(Ks + (tx + 8 * i) * kFLd)[d4];
+                sc[0][i] += q0.x * kk.x + q0.y * kk.y + q0.z * kk.z + q0.w * kk.w;
+                sc[1][i] += q1.x * kk.x + q1.y * kk.y + q1.z * kk.z + q1.w * kk.w;
+            }
+        }
+        // online softmax per row over this tile (8 threads share a row pair)
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int j = k0 + tx + 8 * i;
+                sc[a][i] = j <= qpos[a] ? sc[a][i] * inv : -INFINITY;
+                tmax = fmaxf(tmax, sc[a][i]);
+            }
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+            const float mn = fmaxf(m[a], tmax);
+            const float corr = mn == -INFINITY ? 1.f : expf(m[a] - mn);
+            float psum = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float pv = sc[a][i] == -INFINITY ? 0.f : expf(sc[a][i] - mn);
+                psum += pv;
+                Ps[(r0 + a) * (kFBK + 1) + tx + 8 * i] = pv;
+            }
+            psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+            psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+            psum += __shfl_xor_sync(0xffffffffu, psum, 4);
+            l[a] = l[a] * corr + psum;
+            m[a] = mn;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[a][j] *= corr;
+        }
+        __syncwarp();
+        // O += P V (rows r0, r0+1; dims tx*4 + 32 jj)
+        for (int j = 0; j < kFBK; ++j) {
+            const float p0 = Ps[r0 * (kFBK + 1) + j], p1 = Ps[(r0 + 1) * (kFBK + 1) + j];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                const float4 v = reinterpret_cast<const float4*>(Vs + j * kFD)[tx + 8 * jj];
+                o[0][4 * jj] += p0 * v.x; o[0][4 * jj + 1] += p0 * v.y;
+                o[0][4 * jj + 2] += p0 * v.z; o[0][4 * jj + 3] += p0 * v.w;
+                o[1][4 * jj] += p1 * v.x; o[1][4 * jj + 1] += p1 * v.y;
+                o[1][4 * jj + 2] += p1 * v.z; o[1][4 * jj + 3] += p1 * v.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+        const int r = r0 + a;
+        if (r >= rows) continue;
+        const float* gate = proj + (int64_t)(t0 + r) * proj_stride + (int64_t)h * 2 * kFD + kFD;
+        float* dst = out + (int64_t)(t0 + r) * out_stride + (int64_t)h * kFD;
+        const float invl = 1.0f / l[a];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+            const int d = tx * 4 + 32 * jj;
+            const float4 g = *reinterpret_cast<const float4*>(gate + d);
+            float4 res;
+            res.x = o[a][4 * jj] * invl * sigmoidf_ref(g.x);
+            res.y = o[a][4 * jj + 1] * invl * sigmoidf_ref(g.y);
+            res.z = o[a][4 * jj + 2] * invl * sigmoidf_ref(g.z);
+            res.w = o[a][4 * jj + 3] * invl * sigmoidf_ref(g.w);
+            *reinterpret_cast<float4*>(dst + d) = res;
+        }
+    }
+}
+
+// dense FFN SwiGLU over T tokens: out[t][i] = silu(g_i) * u_i; proj[t] holds
+// the gate|up rows interleaved in fours, g(2j) g(2j+1) u(2j) u(2j+1).
 __global__ void ffn_swiglu_kernel(const float* __restrict__ proj, int64_t proj_stride, int T, int I,
                                   float* __restrict__ out) {
     griddep_wait();
@@ -351,7 +520,8 @@ __global__ void ffn_swiglu_kernel(const float* __restrict__ proj, int64_t proj_s
     const int64_t n = (int64_t)T * I;
     for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
         const int64_t t = k / I, i = k - t * I;
-        const float g = proj[t * proj_stride + i], u = proj[t * proj_stride + I + i];
+        const int64_t c = (i >> 1) * 4 + (i & 1);
+        const float g = proj[t * proj_stride + c], u = proj[t * proj_stride + c + 2];
         out[k] = siluf_ref(g) * u;  // engine.cpp:374
     }
 }
@@ -384,9 +554,12 @@ int launch_rms(const float* x, const float* w1, int n, int T, float* out, cudaSt
 int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const float* w, int CK, float* hist,
                 cudaStream_t s) {
     if (CK < 2 || CK > 9) return Q3XK_EUNSUPPORTED;
-    if (launch_pdl(conv_kernel, dim3((channels + 127) / 128), dim3(128), 0, s, proj, proj_stride, T, channels, w,
-                   CK, hist) != cudaSuccess)
-        return Q3XK_ECUDA;
+    const dim3 grid((channels + 127) / 128);
+    const cudaError_t e = CK == 4 ? launch_pdl(conv_kernel<4>, grid, dim3(128), 0, s, proj, proj_stride, T, channels,
+                                               w, CK, hist)
+                                  : launch_pdl(conv_kernel<0>, grid, dim3(128), 0, s, proj, proj_stride, T, channels,
+                                               w, CK, hist);
+    if (e != cudaSuccess) return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;
 }
@@ -409,6 +582,21 @@ int launch_attention(float* proj, int64_t proj_stride, int T, const AttnDims& ad
     if (launch_pdl(attn_prep_kernel, dim3(T, ad.AH + ad.KVH), dim3(256), 0, s, proj, proj_stride, ad, qn1, kn1, pos,
                    kcache, vcache) != cudaSuccess)
         return Q3XK_ECUDA;
+    if (T > 1) {
+        static bool configured = false;
+        if (!configured) {
+            if (cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kFlashSmem) != cudaSuccess)
+                return Q3XK_ECUDA;
+            configured = true;
+        }
+        if (launch_pdl(attn_prefill_kernel, dim3((T + kFBQ - 1) / kFBQ, ad.AH), dim3(256), kFlashSmem, s,
+                       (const float*)proj, proj_stride, T, ad, pos, (const float*)kcache, (const float*)vcache, out,
+                       out_stride) != cudaSuccess)
+            return Q3XK_ECUDA;
+        count_launch(2);
+        return Q3XK_OK;
+    }
     const int nsplit = (capacity + split_len - 1) / split_len;
     if (launch_pdl(attn_split_kernel, dim3(nsplit, ad.KVH, T), dim3(kAttnWarps * 32), 0, s, (const float*)proj,
                    proj_stride, ad, pos, (const float*)kcache, (const float*)vcache, split_len, part) != cudaSuccess)

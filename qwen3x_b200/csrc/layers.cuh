@@ -16,13 +16,34 @@ struct AttnDims {
     int AH, KVH, AD, RD;
 };
 
+// Repack `src_rows` packed rows of [gate (half) | up (half)] matrices (one
+// per 2*half source rows, counted from row_offset) into m's rows with the
+// SwiGLU interleave g(2j) g(2j+1) u(2j) u(2j+1) (layout.cu).
+int repack_swiglu(const q3xk_matrix* m, const void* packed, int64_t src_rows, int half, int row_offset,
+                  cudaStream_t s);
+
+// GEMV whose epilogue applies SwiGLU to the interleaved rows: y[i] =
+// (w[slot] *) silu(g_i) * u_i, rows/2 outputs (gemv.cu).  ids/rows mode when
+// ids != nullptr (MoE gate|up of the selected experts; w per slot).
+int gemv_swiglu(const q3xk_matrix* w, const float* x, float* y, const int* ids, int slots, const float* slot_w,
+                const q3xk_xform* xf, cudaStream_t s);
+
 int launch_embed(const q3xk_matrix& m, const int* tokens, int T, float* out, cudaStream_t s);
 int launch_rms(const float* x, const float* w1, int n, int T, float* out, cudaStream_t s);
 int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const float* w, int CK, float* hist,
                 cudaStream_t s);
+// norm == nullptr: write the raw delta-rule output (the gated RMS is then
+// applied by the consumer, q3xk_gemv_ex with Q3XK_XFORM_GATED_RMS).
 int launch_delta(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
                  const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
                  cudaStream_t s);
+// Chunked gated DeltaNet over T > 1 tokens (delta.cu): same inputs and
+// results as launch_delta with a norm, in parallel over 64-token chunks.
+// `work` holds delta_chunked_workspace_bytes(T, VH) bytes.
+size_t delta_chunked_workspace_bytes(int T, int VH);
+int launch_delta_chunked(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
+                         const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
+                         float* work, cudaStream_t s);
 int launch_attention(float* proj, int64_t proj_stride, int T, const AttnDims& ad, const float* qn1,
                      const float* kn1, const int* pos, float* kcache, float* vcache, int capacity, float* part,
                      int split_len, float* out, int64_t out_stride, cudaStream_t s);

@@ -16,11 +16,23 @@ void count_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_r
 
 namespace {
 
+// Destination row of source row r.  half == 0: r.  half == I > 0: the rows
+// of [gate (I) | up (I)] matrices (one per 2I source rows, r counted from
+// row_offset) are interleaved in fours, g(2j) g(2j+1) u(2j) u(2j+1), so that a
+// GEMV warp's 4-row group holds both operands of two SwiGLU outputs.
+__device__ __forceinline__ int64_t dest_row(int64_t r, int64_t half, int64_t row_offset) {
+    if (half == 0) return r;
+    r += row_offset;
+    const int64_t e = r / (2 * half), i = r - e * 2 * half;
+    const int64_t up = i >= half, k = up ? i - half : i;
+    return e * 2 * half + (k >> 1) * 4 + 2 * up + (k & 1);
+}
+
 // One thread per packed block.  Q8_0 quants are stored as q XOR 0x80 (offset
 // binary) so the kernels can turn a byte into an exact float with one PRMT.
 __global__ void repack_q8_kernel(const uint8_t* __restrict__ packed, uint8_t* __restrict__ out,
                                  int64_t total_rows, int blocks_per_row, int64_t row_stride,
-                                 int64_t quant_bytes, int pad_slots) {
+                                 int64_t quant_bytes, int pad_slots, int64_t half = 0, int64_t row_offset = 0) {
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= total_rows * blocks_per_row) return;
     const int64_t row = t / blocks_per_row;
@@ -30,7 +42,7 @@ __global__ void repack_q8_kernel(const uint8_t* __restrict__ packed, uint8_t* __
 #pragma unroll
     for (int i = 0; i < 8; ++i)
         q[i] = ((uint32_t)src[1 + 2 * i] | ((uint32_t)src[2 + 2 * i] << 16)) ^ 0x80808080u;
-    uint8_t* rec = out + row * row_stride;
+    uint8_t* rec = out + dest_row(row, half, row_offset) * row_stride;
     uint4* dst = reinterpret_cast<uint4*>(rec + (int64_t)blk * kBlock);
     dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
     dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
@@ -42,7 +54,7 @@ __global__ void repack_q8_kernel(const uint8_t* __restrict__ packed, uint8_t* __
 
 __global__ void repack_q4_kernel(const uint8_t* __restrict__ packed, uint8_t* __restrict__ out,
                                  int64_t total_rows, int blocks_per_row, int64_t row_stride,
-                                 int64_t quant_bytes, int pad_slots) {
+                                 int64_t quant_bytes, int pad_slots, int64_t half = 0, int64_t row_offset = 0) {
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= total_rows * blocks_per_row) return;
     const int64_t row = t / blocks_per_row;
@@ -51,7 +63,7 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ packed, uint8_t* __
     uint32_t q[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) q[i] = (uint32_t)src[1 + 2 * i] | ((uint32_t)src[2 + 2 * i] << 16);
-    uint8_t* rec = out + row * row_stride;
+    uint8_t* rec = out + dest_row(row, half, row_offset) * row_stride;
     *reinterpret_cast<uint4*>(rec + (int64_t)blk * 16) = make_uint4(q[0], q[1], q[2], q[3]);
     uint16_t* scales = reinterpret_cast<uint16_t*>(rec + quant_bytes);
     scales[blk] = src[0];
@@ -61,17 +73,48 @@ __global__ void repack_q4_kernel(const uint8_t* __restrict__ packed, uint8_t* __
 
 // BF16 rows: copy, zero the tail padding.  One thread per 2-byte slot.
 __global__ void repack_bf16_kernel(const uint16_t* __restrict__ packed, uint8_t* __restrict__ out,
-                                   int64_t total_rows, int cols, int64_t row_stride) {
+                                   int64_t total_rows, int cols, int64_t row_stride, int64_t half = 0,
+                                   int64_t row_offset = 0) {
     const int slots = (int)(row_stride / 2);
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= total_rows * slots) return;
     const int64_t row = t / slots;
     const int c = (int)(t - row * slots);
-    uint16_t* rec = reinterpret_cast<uint16_t*>(out + row * row_stride);
+    uint16_t* rec = reinterpret_cast<uint16_t*>(out + dest_row(row, half, row_offset) * row_stride);
     rec[c] = c < cols ? packed[row * cols + c] : (uint16_t)0;
 }
 
 }  // namespace
+
+int repack_swiglu(const q3xk_matrix* m, const void* packed, int64_t src_rows, int half, int row_offset,
+                  cudaStream_t s) {
+    if (!m || !m->data || !packed || src_rows <= 0 || half <= 0 || (half & 1)) return Q3XK_EINVAL;
+    if (m->row_stride != row_record_bytes(m->type, m->cols)) return Q3XK_EINVAL;
+    const int threads = 256;
+    if (m->type == Q3XK_BF16) {
+        const int64_t n = src_rows * (m->row_stride / 2);
+        repack_bf16_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, s>>>(
+            static_cast<const uint16_t*>(packed), static_cast<uint8_t*>(m->data), src_rows, m->cols, m->row_stride,
+            half, row_offset);
+    } else {
+        const int bpr = m->cols / kBlock;
+        const int64_t n = src_rows * bpr;
+        const unsigned grid = (unsigned)((n + threads - 1) / threads);
+        if (m->type == Q3XK_Q8_0)
+            repack_q8_kernel<<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(packed),
+                                                      static_cast<uint8_t*>(m->data), src_rows, bpr, m->row_stride,
+                                                      quant_bytes(m->type, m->cols), scale_slots(m->cols), half,
+                                                      row_offset);
+        else
+            repack_q4_kernel<<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(packed),
+                                                      static_cast<uint8_t*>(m->data), src_rows, bpr, m->row_stride,
+                                                      quant_bytes(m->type, m->cols), scale_slots(m->cols), half,
+                                                      row_offset);
+    }
+    count_launch();
+    return last_launch_status();
+}
+
 }  // namespace q3xk
 
 using namespace q3xk;

@@ -20,12 +20,6 @@ namespace {
 
 constexpr int kMaxPerLane = 16;  // experts <= 512
 
-// engine.cpp:187-191 (same branches, correctly rounded expf)
-__device__ __forceinline__ float sigmoid_ref(float x) {
-    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
-    const float e = expf(x);
-    return e / (1.0f + e);
-}
 
 __global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict__ logits, int experts, int top_k,
                                                          int with_shared, int* __restrict__ ids,
