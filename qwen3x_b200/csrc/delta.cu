@@ -26,8 +26,11 @@ constexpr int kD = 128;           // KD = VD
 constexpr int kLd = kD + 4;       // padded smem row (floats)
 constexpr int kCols = 32;         // S columns per scan CTA
 constexpr float kEps = 1e-6f;     // engine.cpp:27
-// Workspace block of one (head, chunk): Q~, W, K~, U' [kC][kD] each, M [kC][kC], gamma.
+// Workspace block of one (head, chunk), laid out for the scan's register
+// tiles: Q~^T [kD][kC], W^T [kD][kC], K~ [kC][kD], U' [kC][kD], M^T [kC][kC], gamma.
 constexpr int64_t kBlockFloats = 4 * kC * kD + kC * kC + 4;
+constexpr int kOffQT = 0, kOffWT = kC * kD, kOffK = 2 * kC * kD, kOffU = 3 * kC * kD, kOffMT = 4 * kC * kD,
+              kOffGamma = 4 * kC * kD + kC * kC;
 
 __device__ __forceinline__ float sigm(float x) { return sigmoid_ref(x); }
 __device__ __forceinline__ float softplus_ref(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
@@ -37,7 +40,8 @@ __device__ __forceinline__ float* block_ptr(float* work, int head, int chunk, in
 }
 
 // ---- prep: one CTA per (chunk, head), 256 threads --------------------------------
-__global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict__ proj, int64_t proj_stride, int T,
+__global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict__ qkv, int64_t qkv_stride,
+                                                         const float* __restrict__ proj, int64_t proj_stride, int T,
                                                          DeltaDims dd, const float* __restrict__ alog,
                                                          const float* __restrict__ dt, float* __restrict__ work) {
     griddep_wait();
@@ -60,13 +64,14 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict
     for (int i = warp; i < kC; i += 8) {
         float q[4], k[4], v[4];
         const bool live = i < n;
-        const float* row = proj + (int64_t)(t0 + i) * proj_stride;
+        const float* crow = qkv + (int64_t)(t0 + i) * qkv_stride;  // conv output: q | k | v
+        const float* row = proj + (int64_t)(t0 + i) * proj_stride;  // a, b
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int d = lane + 32 * e;
-            q[e] = live ? row[qk_head * kD + d] : 0.f;
-            k[e] = live ? row[dd.KH * kD + qk_head * kD + d] : 0.f;
-            v[e] = live ? row[2 * dd.KH * kD + head * kD + d] : 0.f;
+            q[e] = live ? crow[qk_head * kD + d] : 0.f;
+            k[e] = live ? crow[dd.KH * kD + qk_head * kD + d] : 0.f;
+            v[e] = live ? crow[2 * dd.KH * kD + head * kD + d] : 0.f;
         }
         float qs = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
         float ks = k[0] * k[0] + k[1] * k[1] + k[2] * k[2] + k[3] * k[3];
@@ -103,7 +108,7 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict
     __syncthreads();
 
     // 2. A (strictly lower) and M (lower incl. diagonal) from 128-long dots
-    float* Mo = out + 4 * kC * kD;
+    float* Mo = out + kOffMT;
     for (int e = tid; e < kC * kC; e += 256) {
         const int i = e / kC, j = e % kC;
         float a = 0.f, m = 0.f;
@@ -123,17 +128,17 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict
             if (j < i) a = beta[i] * gam * dk;
         }
         As[i * (kC + 1) + j] = a;
-        Mo[e] = m;
+        Mo[j * kC + i] = m;  // M^T
     }
     // Q~ = exp(G) q, K~ = exp(G_last - G) k, straight to the workspace
     const float Glast = G[n - 1];
     for (int e = tid; e < kC * kD; e += 256) {
         const int i = e / kD, d = e % kD;
-        const bool live = i < n;
-        out[e] = live ? expf(G[i]) * Qs[i * kLd + d] : 0.f;                       // Q~
-        out[2 * kC * kD + e] = live ? expf(Glast - G[i]) * Ks[i * kLd + d] : 0.f;  // K~
+        out[kOffK + e] = i < n ? expf(Glast - G[i]) * Ks[i * kLd + d] : 0.f;  // K~
+        const int dt_ = e / kC, it = e % kC;
+        out[kOffQT + e] = it < n ? expf(G[it]) * Qs[it * kLd + dt_] : 0.f;     // Q~^T
     }
-    if (tid == 0) out[4 * kC * kD + kC * kC] = expf(Glast);
+    if (tid == 0) out[kOffGamma] = expf(Glast);
     __syncthreads();
 
     // 3. forward substitution: rows t of U' (in Vs) and W (in Qs), in order
@@ -150,88 +155,116 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict
     }
     for (int e = tid; e < kC * kD; e += 256) {
         const int i = e / kD, d = e % kD;
-        const bool live = i < n;
-        out[kC * kD + e] = live ? Qs[i * kLd + d] : 0.f;      // W
-        out[3 * kC * kD + e] = live ? Vs[i * kLd + d] : 0.f;  // U'
+        out[kOffU + e] = i < n ? Vs[i * kLd + d] : 0.f;  // U'
+        const int dt_ = e / kC, it = e % kC;
+        out[kOffWT + e] = it < n ? Qs[it * kLd + dt_] : 0.f;  // W^T
     }
 }
 
 // ---- scan: one CTA per (head, 32-column block), chunks in order ----------------
+// Register tiles: U and O as 4 rows x 2 columns per thread, S as 4 x 4.
 __global__ void __launch_bounds__(256) delta_scan_kernel(const float* __restrict__ work, int T,
                                                          float* __restrict__ state /*[VH][KD][VD]*/,
                                                          float* __restrict__ out, int64_t out_stride) {
     griddep_wait();
     griddep_launch_dependents();
     extern __shared__ __align__(16) float sm[];
-    float* S = sm;                 // [kD][kCols]
-    float* U = S + kD * kCols;     // [kC][kCols]
-    float* A1 = U + kC * kCols;    // [kC][kLd]  W, then K~
-    float* A2 = A1 + kC * kLd;     // [kC][kLd]  Q~
-    float* Ms = A2 + kC * kLd;     // [kC][kC + 1]
+    float* S = sm;               // [kD][kCols]
+    float* U = S + kD * kCols;   // [kC][kCols]
+    float* A1 = U + kC * kCols;  // W^T [kD][kC], then K~ [kC][kD]
+    float* A2 = A1 + kC * kD;    // Q~^T [kD][kC]
+    float* Ms = A2 + kC * kD;    // M^T [kC][kC]
     const int head = blockIdx.x, cb = blockIdx.y;
     const int nchunks = (T + kC - 1) / kC;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int c = lane;  // this thread's S column within the block
+    const int tid = threadIdx.x;
+    const int i0 = 4 * (tid & 15), c0 = 2 * (tid >> 4);  // U / O tile
+    const int r0 = 4 * (tid & 31), c4 = 4 * (tid >> 5);  // S tile
     float* st = state + (int64_t)head * kD * kD + cb * kCols;
     for (int e = tid; e < kD * kCols; e += 256) S[e] = st[(e / kCols) * kD + e % kCols];
 
+    auto stage = [&](float* dst, const float* src, int n4) {
+        for (int e = tid; e < n4; e += 256) reinterpret_cast<float4*>(dst)[e] = reinterpret_cast<const float4*>(src)[e];
+    };
     for (int chunk = 0; chunk < nchunks; ++chunk) {
         const float* blk = work + ((int64_t)head * nchunks + chunk) * kBlockFloats;
         const int t0 = chunk * kC, n = min(kC, T - t0);
         __syncthreads();  // S final for this chunk; A1/A2/Ms free
-        for (int e = tid; e < kC * kD / 4; e += 256) {
-            const int i = e / (kD / 4), d4 = e % (kD / 4);
-            reinterpret_cast<float4*>(A1 + i * kLd)[d4] = reinterpret_cast<const float4*>(blk + kC * kD)[e];  // W
-            reinterpret_cast<float4*>(A2 + i * kLd)[d4] = reinterpret_cast<const float4*>(blk)[e];            // Q~
-        }
-        for (int e = tid; e < kC * kC; e += 256) Ms[(e / kC) * (kC + 1) + e % kC] = blk[4 * kC * kD + e];
+        stage(A1, blk + kOffWT, kC * kD / 4);
+        stage(A2, blk + kOffQT, kC * kD / 4);
+        stage(Ms, blk + kOffMT, kC * kC / 4);
         __syncthreads();
-        // U = U' - W S   (rows i = warp + 8 k)
-        float u[kC / 8];
+        // U = U' - W S
+        float u[4][2];
 #pragma unroll
-        for (int k = 0; k < kC / 8; ++k) u[k] = blk[3 * kC * kD + (warp + 8 * k) * kD + cb * kCols + c];
+        for (int a = 0; a < 4; ++a) {
+            const float2 up = *reinterpret_cast<const float2*>(blk + kOffU + (i0 + a) * kD + cb * kCols + c0);
+            u[a][0] = up.x;
+            u[a][1] = up.y;
+        }
+#pragma unroll 4
         for (int r = 0; r < kD; ++r) {
-            const float s = S[r * kCols + c];
-#pragma unroll
-            for (int k = 0; k < kC / 8; ++k) u[k] -= A1[(warp + 8 * k) * kLd + r] * s;
+            const float4 w = *reinterpret_cast<const float4*>(A1 + r * kC + i0);
+            const float2 sv = *reinterpret_cast<const float2*>(S + r * kCols + c0);
+            u[0][0] -= w.x * sv.x; u[0][1] -= w.x * sv.y;
+            u[1][0] -= w.y * sv.x; u[1][1] -= w.y * sv.y;
+            u[2][0] -= w.z * sv.x; u[2][1] -= w.z * sv.y;
+            u[3][0] -= w.w * sv.x; u[3][1] -= w.w * sv.y;
         }
 #pragma unroll
-        for (int k = 0; k < kC / 8; ++k) U[(warp + 8 * k) * kCols + c] = u[k];
+        for (int a = 0; a < 4; ++a) *reinterpret_cast<float2*>(U + (i0 + a) * kCols + c0) = make_float2(u[a][0], u[a][1]);
         __syncthreads();
         // O = Q~ S + M U
-        float o[kC / 8];
-#pragma unroll
-        for (int k = 0; k < kC / 8; ++k) o[k] = 0.f;
+        float o[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll 4
         for (int r = 0; r < kD; ++r) {
-            const float s = S[r * kCols + c];
-#pragma unroll
-            for (int k = 0; k < kC / 8; ++k) o[k] += A2[(warp + 8 * k) * kLd + r] * s;
+            const float4 q = *reinterpret_cast<const float4*>(A2 + r * kC + i0);
+            const float2 sv = *reinterpret_cast<const float2*>(S + r * kCols + c0);
+            o[0][0] += q.x * sv.x; o[0][1] += q.x * sv.y;
+            o[1][0] += q.y * sv.x; o[1][1] += q.y * sv.y;
+            o[2][0] += q.z * sv.x; o[2][1] += q.z * sv.y;
+            o[3][0] += q.w * sv.x; o[3][1] += q.w * sv.y;
         }
+#pragma unroll 4
         for (int j = 0; j < kC; ++j) {
-            const float uj = U[j * kCols + c];
-#pragma unroll
-            for (int k = 0; k < kC / 8; ++k) o[k] += Ms[(warp + 8 * k) * (kC + 1) + j] * uj;
+            const float4 mm = *reinterpret_cast<const float4*>(Ms + j * kC + i0);
+            const float2 uv = *reinterpret_cast<const float2*>(U + j * kCols + c0);
+            o[0][0] += mm.x * uv.x; o[0][1] += mm.x * uv.y;
+            o[1][0] += mm.y * uv.x; o[1][1] += mm.y * uv.y;
+            o[2][0] += mm.z * uv.x; o[2][1] += mm.z * uv.y;
+            o[3][0] += mm.w * uv.x; o[3][1] += mm.w * uv.y;
         }
 #pragma unroll
-        for (int k = 0; k < kC / 8; ++k) {
-            const int i = warp + 8 * k;
-            if (i < n) out[(int64_t)(t0 + i) * out_stride + head * kD + cb * kCols + c] = o[k];
-        }
-        __syncthreads();  // A1 (W) no longer needed
-        for (int e = tid; e < kC * kD / 4; e += 256) {
-            const int i = e / (kD / 4), d4 = e % (kD / 4);
-            reinterpret_cast<float4*>(A1 + i * kLd)[d4] =
-                reinterpret_cast<const float4*>(blk + 2 * kC * kD)[e];  // K~
-        }
+        for (int a = 0; a < 4; ++a)
+            if (i0 + a < n)
+                *reinterpret_cast<float2*>(out + (int64_t)(t0 + i0 + a) * out_stride + head * kD + cb * kCols + c0) =
+                    make_float2(o[a][0], o[a][1]);
+        __syncthreads();  // W^T no longer needed
+        stage(A1, blk + kOffK, kC * kD / 4);
         __syncthreads();
-        // S = gamma S + K~^T U   (rows r = warp + 8 k, 16 per thread)
-        const float gam = blk[4 * kC * kD + kC * kC];
-        for (int k = 0; k < kD / 8; ++k) {
-            const int r = warp + 8 * k;
-            float acc = gam * S[r * kCols + c];
-            for (int j = 0; j < kC; ++j) acc += A1[j * kLd + r] * U[j * kCols + c];
-            S[r * kCols + c] = acc;
+        // S = gamma S + K~^T U
+        const float gam = blk[kOffGamma];
+        float sacc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const float4 sv = *reinterpret_cast<const float4*>(S + (r0 + a) * kCols + c4);
+            sacc[a][0] = gam * sv.x; sacc[a][1] = gam * sv.y; sacc[a][2] = gam * sv.z; sacc[a][3] = gam * sv.w;
         }
+#pragma unroll 4
+        for (int j = 0; j < kC; ++j) {
+            const float4 kk = *reinterpret_cast<const float4*>(A1 + j * kD + r0);
+            const float4 uv = *reinterpret_cast<const float4*>(U + j * kCols + c4);
+            const float kr[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                sacc[a][0] += kr[a] * uv.x; sacc[a][1] += kr[a] * uv.y;
+                sacc[a][2] += kr[a] * uv.z; sacc[a][3] += kr[a] * uv.w;
+            }
+        }
+        __syncthreads();  // every thread has read S (U and O phases) before it changes
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+            *reinterpret_cast<float4*>(S + (r0 + a) * kCols + c4) =
+                make_float4(sacc[a][0], sacc[a][1], sacc[a][2], sacc[a][3]);
     }
     __syncthreads();
     for (int e = tid; e < kD * kCols; e += 256) st[(e / kCols) * kD + e % kCols] = S[e];
@@ -265,7 +298,7 @@ __global__ void __launch_bounds__(256) gated_rms_kernel(float* __restrict__ out,
 }
 
 constexpr size_t kPrepSmem = (size_t)(3 * kC * kLd + kC * (kC + 1) + 3 * kC) * 4;
-constexpr size_t kScanSmem = (size_t)(kD * kCols + kC * kCols + 2 * kC * kLd + kC * (kC + 1)) * 4;
+constexpr size_t kScanSmem = (size_t)(kD * kCols + kC * kCols + 2 * kC * kD + kC * kC) * 4;
 
 }  // namespace
 
@@ -274,9 +307,9 @@ size_t delta_chunked_workspace_bytes(int T, int VH) {
     return (size_t)(VH * nchunks * kBlockFloats) * 4;
 }
 
-int launch_delta_chunked(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
-                         const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
-                         float* work, cudaStream_t s) {
+int launch_delta_chunked(const float* qkv, int64_t qkv_stride, const float* proj, int64_t proj_stride, int T,
+                         const DeltaDims& dd, const float* alog, const float* dt, const float* norm, float* state,
+                         float* out, int64_t out_stride, float* work, cudaStream_t s) {
     if (dd.KD != kD || dd.VD != kD || dd.VH % dd.KH || T < 1 || !work || !norm) return Q3XK_EUNSUPPORTED;
     static bool configured = false;
     if (!configured) {
@@ -288,8 +321,8 @@ int launch_delta_chunked(const float* proj, int64_t proj_stride, int T, const De
         configured = true;
     }
     const int nchunks = (T + kC - 1) / kC;
-    if (launch_pdl(delta_prep_kernel, dim3(nchunks, dd.VH), dim3(256), kPrepSmem, s, proj, proj_stride, T, dd, alog,
-                   dt, work) != cudaSuccess)
+    if (launch_pdl(delta_prep_kernel, dim3(nchunks, dd.VH), dim3(256), kPrepSmem, s, qkv, qkv_stride, proj,
+                   proj_stride, T, dd, alog, dt, work) != cudaSuccess)
         return Q3XK_ECUDA;
     if (launch_pdl(delta_scan_kernel, dim3(dd.VH, kD / kCols), dim3(256), kScanSmem, s, (const float*)work, T, state,
                    out, out_stride) != cudaSuccess)

@@ -40,7 +40,6 @@ constexpr int kMaxContext = 262144;                 // model_config.h:13
 constexpr size_t kHeaderSize = 8 + 16 * 4;          // model_config.h:10-12
 constexpr int kEndOfText = 248044, kImEnd = 248046;  // engine.cpp:28
 constexpr int kChunk = 2048;                        // prefill tokens per pass
-constexpr int kAttnSplits = 32;                     // key splits of decode attention
 constexpr size_t kAlign = 256;
 
 struct Config {
@@ -171,6 +170,7 @@ struct State {
     float *hidden = nullptr, *normed = nullptr, *proj = nullptr, *mix = nullptr, *part = nullptr;
     float *rlogits = nullptr, *rweights = nullptr, *hbuf = nullptr;
     float* delta_work = nullptr;  // chunked DeltaNet workspace (prefill)
+    float* qkv = nullptr;         // conv output q | k | v of a prefill pass [chunk][DQKV]
     int* rids = nullptr;
     void* gemm_ws = nullptr;
     size_t gemm_ws_bytes = 0;
@@ -619,10 +619,16 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
         const int P = l.in_proj.rows;
         Q3XB_TRY(mm(s, l.in_proj, s.normed, T, s.proj, 0));
         if (l.delta) {
-            Q3XB_TRY(launch_conv(s.proj, P, T, DQKV, l.conv, c.CK, s.conv[di], st));
             const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
-            Q3XB_TRY(launch_delta_chunked(s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di], s.mix, DO,
-                                          s.delta_work, st));
+            if (c.CK == 4) {
+                Q3XB_TRY(launch_conv_prefill(s.proj, P, T, DQKV, l.conv, c.CK, s.conv[di], s.qkv, st));
+                Q3XB_TRY(launch_delta_chunked(s.qkv, DQKV, s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di],
+                                              s.mix, DO, s.delta_work, st));
+            } else {
+                Q3XB_TRY(launch_conv(s.proj, P, T, DQKV, l.conv, c.CK, s.conv[di], st));
+                Q3XB_TRY(launch_delta_chunked(s.proj, P, s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di],
+                                              s.mix, DO, s.delta_work, st));
+            }
             Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
             ++di;
         } else {
@@ -702,8 +708,7 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
     const int chunk = context < kChunk ? context : kChunk;
     s->chunk = s->chunk_capacity = chunk;
     s->recurrent_floats = (size_t)delta_layers * (conv + memory);
-    s->split_len = (context + kAttnSplits - 1) / kAttnSplits;
-    if (s->split_len < 64) s->split_len = 64;
+    s->split_len = 128;  // decode attention: 128-key splits (attn_decode_kernel)
     const int nsplit = (context + s->split_len - 1) / s->split_len;
     bool ok = s->alloc(&s->recurrent, s->recurrent_floats) && s->alloc(&s->checkpoint_recurrent, s->recurrent_floats) &&
               s->alloc(&s->kv, (size_t)attn_layers * 2 * cache) && s->alloc(&s->logits, c.V) &&
@@ -718,7 +723,8 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
              s->alloc(&s->hbuf, (size_t)S * c.I);
     }
     if (ok && chunk > 1 && delta_layers > 0)
-        ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4);
+        ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4) &&
+             s->alloc(&s->qkv, (size_t)chunk * DQKV);
     if (ok) {
         q3xk_argmax_workspace_bytes(&s->argmax_ws_bytes);
         uint8_t* ws = nullptr;

@@ -6,6 +6,7 @@
 // as in the reference.  Positions are read from device memory (`pos`) so a
 // whole decode step can live in one CUDA graph.
 #include "layers.cuh"
+#include "stream.cuh"
 
 namespace q3xk {
 namespace {
@@ -123,6 +124,55 @@ __global__ void conv_kernel(float* __restrict__ proj, int64_t proj_stride, int T
 #pragma unroll
     for (int i = 0; i < (KC ? KC - 1 : 8); ++i)
         if (i < CK - 1) hc[i] = h[i];
+}
+
+// ---- the same conv over a prompt, out of place: CTA = (128 channels, 64-token
+// segment).  A segment's history is the raw input of the CK-1 tokens before it
+// (or the stored history for the first segment, whose CTA also writes the new
+// history).
+constexpr int kConvSeg = 64;
+__global__ void __launch_bounds__(128) conv_prefill_kernel(const float* __restrict__ proj, int64_t proj_stride, int T,
+                                                           int channels, const float* __restrict__ w,
+                                                           float* __restrict__ hist, float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch_dependents();
+    constexpr int CK = 4;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int t0 = blockIdx.y * kConvSeg, t1 = min(T, t0 + kConvSeg);
+    if (c >= channels) return;
+    float h[CK - 1], wc[CK];
+#pragma unroll
+    for (int i = 0; i < CK; ++i) wc[i] = w[(int64_t)c * CK + i];
+#pragma unroll
+    for (int i = 0; i < CK - 1; ++i) {
+        const int t = t0 - (CK - 1) + i;  // token whose raw input is history slot i
+        h[i] = t >= 0 ? proj[(int64_t)t * proj_stride + c] : hist[(int64_t)c * (CK - 1) + (t + (CK - 1))];
+    }
+    constexpr int kTile = 16;
+    for (int tb = t0; tb < t1; tb += kTile) {
+        float xs[kTile];
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) xs[i] = tb + i < t1 ? proj[(int64_t)(tb + i) * proj_stride + c] : 0.f;
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) {
+            if (tb + i >= t1) break;
+            const float x = xs[i];
+            float sum = x * wc[CK - 1];
+#pragma unroll
+            for (int j = 0; j < CK - 1; ++j) sum += h[j] * wc[j];
+#pragma unroll
+            for (int j = 0; j < CK - 2; ++j) h[j] = h[j + 1];
+            h[CK - 2] = x;
+            out[(int64_t)(tb + i) * channels + c] = siluf_ref(sum);
+        }
+    }
+    // The first segment's CTA alone reads the stored history, so it alone
+    // writes the new one: the raw inputs of the last CK-1 tokens.
+    if (blockIdx.y == 0) {
+#pragma unroll
+        for (int i = 0; i < CK - 1; ++i)
+            hist[(int64_t)c * (CK - 1) + i] = t1 == T ? h[i] : proj[(int64_t)(T - (CK - 1) + i) * proj_stride + c];
+    }
 }
 
 // ---- gated DeltaNet, one head per CTA, T tokens in order (engine.cpp:274-320).
@@ -348,6 +398,144 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(const float
     }
 }
 
+// ---- decode attention (T = 1): CTA = (128-key split, kv head), 8 warps of 16
+// keys.  Each warp streams 4 keys at a time (K and V rows, 8 KB) into its own
+// two-stage shared-memory ring with cp.async, so its next keys are in flight
+// while it computes; lanes own 8 of the 256 dims.  Partials (m, l, o) per
+// (split, query head) go to `part` for attn_merge_kernel, as attn_split_kernel.
+constexpr int kDecSplit = 128, kDecKeys = 4, kDecWarps = 8;
+constexpr size_t kDecSmem = (size_t)kDecWarps * 2 * kDecKeys * 2 * 256 * 4;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+template <int kMaxG>  // query heads per kv head, at most
+__global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const float* __restrict__ proj, AttnDims ad,
+                                                                     const int* __restrict__ pos,
+                                                                     const float* __restrict__ kcache,
+                                                                     const float* __restrict__ vcache,
+                                                                     float* __restrict__ part) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ __align__(16) float dsm[];
+    constexpr int kPer = 8;
+    const int split = blockIdx.x, kvh = blockIdx.y, nsplit = gridDim.x;
+    const int G = ad.AH / ad.KVH, AD = 256;
+    const int last = *pos;  // keys 0..last (the new key is already in the cache)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w0 = split * kDecSplit + warp * (kDecSplit / kDecWarps);
+    const int w1 = min(last + 1, w0 + kDecSplit / kDecWarps);
+    float* ring = dsm + warp * (2 * kDecKeys * 2 * AD);  // [stage][key][K | V][256]
+    const float inv = 1.0f / sqrtf((float)AD);
+    float q[kMaxG][kPer], o[kMaxG][kPer], m[kMaxG], l[kMaxG];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+            o[g][e] = 0.f;
+            q[g][e] = g < G ? proj[(int64_t)(kvh * G + g) * 2 * AD + lane * kPer + e] : 0.f;
+        }
+    }
+    auto issue = [&](int stage, int j0) {
+#pragma unroll
+        for (int kk = 0; kk < kDecKeys; ++kk) {
+            const int j = j0 + kk;
+            if (j < w1) {
+                const int64_t off = ((int64_t)j * ad.KVH + kvh) * AD;
+                float* dk = ring + (stage * kDecKeys + kk) * 2 * AD;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    cp_async16(dk + (lane + 32 * c) * 4, kcache + off + (lane + 32 * c) * 4);
+                    cp_async16(dk + AD + (lane + 32 * c) * 4, vcache + off + (lane + 32 * c) * 4);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    if (w0 < w1) {
+        issue(0, w0);
+        issue(1, w0 + kDecKeys);
+        int stage = 0;
+        for (int j0 = w0; j0 < w1; j0 += kDecKeys, stage ^= 1) {
+            cp_async_wait<1>();
+            __syncwarp();
+            const float* base = ring + stage * kDecKeys * 2 * AD;
+#pragma unroll
+            for (int kk = 0; kk < kDecKeys; ++kk) {
+                if (j0 + kk >= w1) break;
+                const float* kr = base + kk * 2 * AD + lane * kPer;
+                const float4 k0 = *reinterpret_cast<const float4*>(kr);
+                const float4 k1 = *reinterpret_cast<const float4*>(kr + 4);
+                const float4 v0 = *reinterpret_cast<const float4*>(kr + AD);
+                const float4 v1 = *reinterpret_cast<const float4*>(kr + AD + 4);
+                const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+                const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int g = 0; g < kMaxG; ++g) {
+                    if (g >= G) break;
+                    float d = 0.f;
+#pragma unroll
+                    for (int e = 0; e < kPer; ++e) d += q[g][e] * kv[e];
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+                    const float sc = d * inv;
+                    const float mn = fmaxf(m[g], sc);
+                    const float corr = expf(m[g] - mn), p = expf(sc - mn);
+                    l[g] = l[g] * corr + p;
+#pragma unroll
+                    for (int e = 0; e < kPer; ++e) o[g][e] = o[g][e] * corr + p * vv[e];
+                    m[g] = mn;
+                }
+            }
+            __syncwarp();  // the stage is free again
+            issue(stage, j0 + 2 * kDecKeys);
+        }
+        cp_async_wait<0>();
+    }
+    // merge the warps of the CTA per query head (shared memory reuses the ring)
+    __syncthreads();
+    float* sm_m = dsm;                         // [kDecWarps][kMaxG]
+    float* sm_l = sm_m + kDecWarps * kMaxG;    // [kDecWarps][kMaxG]
+    float* sm_o = sm_l + kDecWarps * kMaxG;    // [kDecWarps][256]
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+        if (g >= G) break;  // uniform over the CTA
+        if (lane == 0) {
+            sm_m[warp * kMaxG + g] = m[g];
+            sm_l[warp * kMaxG + g] = l[g];
+        }
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) sm_o[warp * AD + lane * kPer + e] = o[g][e];
+        __syncthreads();
+        if (warp == 0) {
+            float M = -INFINITY;
+            for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, sm_m[w * kMaxG + g]);
+            float L = 0.f, acc[kPer] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int w = 0; w < kDecWarps; ++w) {
+                const float mw = sm_m[w * kMaxG + g];
+                const float cw = mw == -INFINITY ? 0.f : expf(mw - M);
+                L += sm_l[w * kMaxG + g] * cw;
+#pragma unroll
+                for (int e = 0; e < kPer; ++e) acc[e] += sm_o[w * AD + lane * kPer + e] * cw;
+            }
+            float* dst = part + ((int64_t)(kvh * G + g) * nsplit + split) * (AD + 2);
+            if (lane == 0) {
+                dst[0] = M;
+                dst[1] = L;
+            }
+#pragma unroll
+            for (int e = 0; e < kPer; ++e) dst[2 + lane * kPer + e] = acc[e];
+        }
+        __syncthreads();
+    }
+}
+
 __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ part, int nsplit,
                                                          const float* __restrict__ proj, int64_t proj_stride,
                                                          AttnDims ad, float* __restrict__ out,
@@ -564,6 +752,17 @@ int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const flo
     return Q3XK_OK;
 }
 
+int launch_conv_prefill(const float* proj, int64_t proj_stride, int T, int channels, const float* w, int CK,
+                        float* hist, float* out, cudaStream_t s) {
+    if (CK != 4) return Q3XK_EUNSUPPORTED;
+    const dim3 grid((channels + 127) / 128, (T + kConvSeg - 1) / kConvSeg);
+    if (launch_pdl(conv_prefill_kernel, grid, dim3(128), 0, s, proj, proj_stride, T, channels, w, hist, out) !=
+        cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
 int launch_delta(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
                  const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
                  cudaStream_t s) {
@@ -595,6 +794,30 @@ int launch_attention(float* proj, int64_t proj_stride, int T, const AttnDims& ad
                        out_stride) != cudaSuccess)
             return Q3XK_ECUDA;
         count_launch(2);
+        return Q3XK_OK;
+    }
+    if (T == 1 && split_len == kDecSplit) {
+        static bool dec_configured = false;
+        if (!dec_configured) {
+            if (cudaFuncSetAttribute(attn_decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kDecSmem) != cudaSuccess ||
+                cudaFuncSetAttribute(attn_decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kDecSmem) != cudaSuccess)
+                return Q3XK_ECUDA;
+            dec_configured = true;
+        }
+        const int nsplit = (capacity + kDecSplit - 1) / kDecSplit;
+        const int G = ad.AH / ad.KVH;
+        const cudaError_t e =
+            G <= 4 ? launch_pdl(attn_decode_kernel<4>, dim3(nsplit, ad.KVH), dim3(kDecWarps * 32), kDecSmem, s,
+                                (const float*)proj, ad, pos, (const float*)kcache, (const float*)vcache, part)
+                   : launch_pdl(attn_decode_kernel<8>, dim3(nsplit, ad.KVH), dim3(kDecWarps * 32), kDecSmem, s,
+                                (const float*)proj, ad, pos, (const float*)kcache, (const float*)vcache, part);
+        if (e != cudaSuccess) return Q3XK_ECUDA;
+        if (launch_pdl(attn_merge_kernel, dim3(T, ad.AH), dim3(256), 0, s, (const float*)part, nsplit,
+                       (const float*)proj, proj_stride, ad, out, out_stride) != cudaSuccess)
+            return Q3XK_ECUDA;
+        count_launch(3);
         return Q3XK_OK;
     }
     const int nsplit = (capacity + split_len - 1) / split_len;

@@ -37,13 +37,18 @@ int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const flo
 int launch_delta(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
                  const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
                  cudaStream_t s);
-// Chunked gated DeltaNet over T > 1 tokens (delta.cu): same inputs and
-// results as launch_delta with a norm, in parallel over 64-token chunks.
+// Chunked gated DeltaNet over T > 1 tokens (delta.cu): same results as
+// launch_delta with a norm, in parallel over 64-token chunks.  q | k | v come
+// from `qkv` (the conv output, launch_conv_prefill), a, b, z from `proj`.
 // `work` holds delta_chunked_workspace_bytes(T, VH) bytes.
 size_t delta_chunked_workspace_bytes(int T, int VH);
-int launch_delta_chunked(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
-                         const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
-                         float* work, cudaStream_t s);
+int launch_delta_chunked(const float* qkv, int64_t qkv_stride, const float* proj, int64_t proj_stride, int T,
+                         const DeltaDims& dd, const float* alog, const float* dt, const float* norm, float* state,
+                         float* out, int64_t out_stride, float* work, cudaStream_t s);
+// Causal conv1d + SiLU over T tokens, out of place (out[t][c], stride
+// `channels`), parallel over 64-token segments; updates the history.
+int launch_conv_prefill(const float* proj, int64_t proj_stride, int T, int channels, const float* w, int CK,
+                        float* hist, float* out, cudaStream_t s);
 int launch_attention(float* proj, int64_t proj_stride, int T, const AttnDims& ad, const float* qn1,
                      const float* kn1, const int* pos, float* kcache, float* vcache, int capacity, float* part,
                      int split_len, float* out, int64_t out_stride, cudaStream_t s);
