@@ -172,6 +172,7 @@ struct State {
     float* delta_work = nullptr;  // chunked DeltaNet workspace (prefill)
     float* qkv = nullptr;         // conv output q | k | v of a prefill pass [chunk][DQKV]
     int* rids = nullptr;
+    int* group_count = nullptr;  // [KH] arrival counts of the fused-conv delta kernel (kept zero)
     void* gemm_ws = nullptr;
     size_t gemm_ws_bytes = 0;
     int split_len = 0;
@@ -561,11 +562,14 @@ int forward_token(Model& m, State& s, bool logits) {
         Q3XB_TRY(rms_input(s, s.hidden, l.in_norm, c.H, &xin, &in));
         Q3XB_TRY(q3xk_gemv_ex(&l.in_proj, in, s.proj, 0, &xin, st));
         if (l.delta) {
-            Q3XB_TRY(launch_conv(s.proj, P, 1, DQKV, l.conv, c.CK, s.conv[di], st));
             const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
-            // the gated RMS runs in the out projection's staging of x (Q3XB_FUSE_GATED) or in the delta kernel
+            // the conv runs inside the delta kernel (CK = 4); the gated RMS in the out
+            // projection's staging of x (Q3XB_FUSE_GATED) or in the delta kernel
+            const bool fuse_conv = c.CK == 4;
+            if (!fuse_conv) Q3XB_TRY(launch_conv(s.proj, P, 1, DQKV, l.conv, c.CK, s.conv[di], st));
             Q3XB_TRY(launch_delta(s.proj, P, 1, dd, l.alog, l.dt, Q3XB_FUSE_GATED ? nullptr : l.dnorm, s.memory[di],
-                                  s.mix, DO, st));
+                                  s.mix, DO, st, fuse_conv ? l.conv : nullptr, fuse_conv ? s.conv[di] : nullptr,
+                                  c.CK, s.group_count));
             q3xk_xform xg{};
             if (Q3XB_FUSE_GATED) {
                 xg.kind = Q3XK_XFORM_GATED_RMS;
@@ -713,7 +717,8 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
     bool ok = s->alloc(&s->recurrent, s->recurrent_floats) && s->alloc(&s->checkpoint_recurrent, s->recurrent_floats) &&
               s->alloc(&s->kv, (size_t)attn_layers * 2 * cache) && s->alloc(&s->logits, c.V) &&
               s->alloc(&s->checkpoint_logits, c.V) && s->alloc(&s->pos, 1) && s->alloc(&s->tokens, chunk) &&
-              s->alloc(&s->argmax_out, 1) && s->alloc(&s->hidden, (size_t)chunk * c.H) &&
+              s->alloc(&s->argmax_out, 1) && s->alloc(&s->group_count, c.KH > 0 ? c.KH : 1) &&
+              s->alloc(&s->hidden, (size_t)chunk * c.H) &&
               s->alloc(&s->normed, (size_t)chunk * c.H) && s->alloc(&s->proj, (size_t)chunk * model->P) &&
               s->alloc(&s->mix, (size_t)chunk * model->mix) &&
               s->alloc(&s->part, (size_t)chunk * c.AH * nsplit * (c.AD + 2));
@@ -759,6 +764,7 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
     // engine.cpp:156-159 reset; logits start at zero as well
     if (cudaMemsetAsync(s->recurrent, 0, s->recurrent_floats * 4, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->pos, 0, 4, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->group_count, 0, sizeof(int) * (c.KH > 0 ? c.KH : 1), s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->logits, 0, (size_t)c.V * 4, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->checkpoint_logits, 0, (size_t)c.V * 4, s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess) {

@@ -179,31 +179,75 @@ __global__ void __launch_bounds__(128) conv_prefill_kernel(const float* __restri
 // 512 threads: thread (v = tid % 128, g = tid / 128) keeps state rows
 // 32g..32g+31 of column v in registers for the whole chunk.
 constexpr int kDeltaThreads = 512;
+// conv_w != nullptr (T = 1 only): the causal conv + SiLU of this head's q, k
+// and v channels (engine.cpp:264-273) is computed here from the raw
+// projections and the history `hist`, which it updates.  The q/k channels are
+// shared by the VH/KH heads of a key group: each of their CTAs reads the old
+// history, counts itself in group_count[key head], and the last one to arrive
+// writes the new history and resets the count to zero.
 __global__ void __launch_bounds__(kDeltaThreads) delta_kernel(const float* __restrict__ proj, int64_t proj_stride,
                                                               int T, DeltaDims dd, const float* __restrict__ alog,
                                                               const float* __restrict__ dt,
                                                               const float* __restrict__ norm,
                                                               float* __restrict__ state /*[VH][KD][VD]*/,
-                                                              float* __restrict__ out, int64_t out_stride) {
+                                                              float* __restrict__ out, int64_t out_stride,
+                                                              const float* __restrict__ conv_w,
+                                                              float* __restrict__ hist,
+                                                              int* __restrict__ group_count) {
     griddep_wait();
     griddep_launch_dependents();
     constexpr int KD = 128, VD = 128, G = kDeltaThreads / VD, RG = KD / G;  // rows per group
+    constexpr int CK = 4;
     const int head = blockIdx.x;
     const int tid = threadIdx.x, v = tid % VD, g = tid / VD;
-    __shared__ float qs[KD], ks[KD], vs[VD], part[G][VD], red[kDeltaThreads / 32], scal[4];
+    __shared__ float qs[KD], ks[KD], vs[VD], part[G][VD], red[kDeltaThreads / 32], scal[4], cx[3 * KD];
     float S[RG];
     float* st = state + (int64_t)head * KD * VD;
 #pragma unroll
     for (int r = 0; r < RG; ++r) S[r] = st[(int64_t)(g * RG + r) * VD + v];
     const int qk_head = head / (dd.VH / dd.KH);
     const float qscale = sqrtf((float)KD);
+    if (conv_w) {
+        // threads 0..127: q channel, 128..255: k channel, 256..383: v channel
+        const int part_ = tid / KD, d = tid % KD;
+        const int c = part_ == 0 ? qk_head * KD + d : part_ == 1 ? dd.KH * KD + qk_head * KD + d
+                                                                : 2 * dd.KH * KD + head * VD + d;
+        float x = 0.f, h[CK - 1];
+        if (tid < 3 * KD) {
+            x = proj[c];
+            float w[CK];
+#pragma unroll
+            for (int i = 0; i < CK - 1; ++i) h[i] = hist[(int64_t)c * (CK - 1) + i];
+#pragma unroll
+            for (int i = 0; i < CK; ++i) w[i] = conv_w[(int64_t)c * CK + i];
+            float sum = x * w[CK - 1];
+#pragma unroll
+            for (int i = 0; i < CK - 1; ++i) sum += h[i] * w[i];
+            cx[tid] = siluf_ref(sum);
+        }
+        __syncthreads();  // every read of the old history of this CTA is done
+        if (tid == 0) {
+            __threadfence();
+            const int ratio = dd.VH / dd.KH;
+            const int prev = atomicAdd(group_count + qk_head, 1);
+            scal[2] = prev == ratio - 1 ? 1.f : 0.f;
+            if (prev == ratio - 1) group_count[qk_head] = 0;
+        }
+        __syncthreads();
+        const bool write_qk = scal[2] != 0.f;
+        if (tid < 3 * KD && (part_ == 2 || write_qk)) {
+#pragma unroll
+            for (int i = 0; i < CK - 2; ++i) hist[(int64_t)c * (CK - 1) + i] = h[i + 1];
+            hist[(int64_t)c * (CK - 1) + CK - 2] = x;
+        }
+    }
     for (int t = 0; t < T; ++t) {
         const float* row = proj + (int64_t)t * proj_stride;
         // q, k: the GQA key head's slices of the conv output; l2-normalised (engine.cpp:246-251)
         float qv = 0.f, kv = 0.f;
         if (tid < KD) {
-            qv = row[qk_head * KD + tid];
-            kv = row[dd.KH * KD + qk_head * KD + tid];
+            qv = conv_w ? cx[tid] : row[qk_head * KD + tid];
+            kv = conv_w ? cx[KD + tid] : row[dd.KH * KD + qk_head * KD + tid];
         }
         const float qss = block_sum<kDeltaThreads>(tid < KD ? qv * qv : 0.f, red);
         const float kss = block_sum<kDeltaThreads>(tid < KD ? kv * kv : 0.f, red);
@@ -211,7 +255,7 @@ __global__ void __launch_bounds__(kDeltaThreads) delta_kernel(const float* __res
             qs[tid] = qv * (1.0f / sqrtf(qss + kEps)) / qscale;
             ks[tid] = kv * (1.0f / sqrtf(kss + kEps));
         }
-        if (tid < VD) vs[tid] = row[2 * dd.KH * KD + head * VD + tid];
+        if (tid < VD) vs[tid] = conv_w ? cx[2 * KD + tid] : row[2 * dd.KH * KD + head * VD + tid];
         if (tid == 0) {
             const float a = row[dd.a_off + head], b = row[dd.b_off + head];
             scal[0] = sigmoidf_ref(b);                                     // beta
@@ -536,26 +580,57 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const float
     }
 }
 
+// Merge of the key splits of one (token, query head): softmax weights of the
+// splits once in shared memory, then one output dim per thread (AD <= 256).
 __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ part, int nsplit,
                                                          const float* __restrict__ proj, int64_t proj_stride,
                                                          AttnDims ad, float* __restrict__ out,
                                                          int64_t out_stride) {
     griddep_wait();
     griddep_launch_dependents();
+    __shared__ float cw[256], red[8];
     const int t = blockIdx.x, h = blockIdx.y, AD = ad.AD;
-    const float* p = part + ((int64_t)t * ad.AH + h) * nsplit * (AD + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p[(int64_t)s * (AD + 2)]);
-    const float* gate = proj + (int64_t)t * proj_stride + (int64_t)h * 2 * AD + AD;
-    for (int d = threadIdx.x; d < AD; d += blockDim.x) {
-        float L = 0.f, acc = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float* ps = p + (int64_t)s * (AD + 2);
-            const float c = ps[0] == -INFINITY ? 0.f : expf(ps[0] - M);
-            L += ps[1] * c;
-            acc += ps[2 + d] * c;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t stride = AD + 2;
+    const float* p = part + ((int64_t)t * ad.AH + h) * nsplit * stride;
+    float mx = -INFINITY;
+    for (int sp = tid; sp < nsplit; sp += 256) mx = fmaxf(mx, p[sp * stride]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) M = fmaxf(M, red[w]);
+    __syncthreads();
+    float Lp = 0.f, acc = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += 256) {
+        const int sp = s0 + tid;
+        float c = 0.f;
+        if (sp < nsplit) {
+            const float ms = p[sp * stride];
+            c = ms == -INFINITY ? 0.f : expf(ms - M);
+            Lp += c * p[sp * stride + 1];
         }
-        out[(int64_t)t * out_stride + (int64_t)h * AD + d] = acc / L * sigmoidf_ref(gate[d]);
+        cw[tid] = c;
+        __syncthreads();
+        const int n = min(256, nsplit - s0);
+        if (tid < AD) {
+            const float* col = p + (int64_t)s0 * stride + 2 + tid;
+#pragma unroll 4
+            for (int k = 0; k < n; ++k) acc += col[k * stride] * cw[k];
+        }
+        __syncthreads();
+    }
+    Lp = warp_sum(Lp);
+    if (lane == 0) red[warp] = Lp;
+    __syncthreads();
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) L += red[w];
+    if (tid < AD) {
+        const float gate = proj[(int64_t)t * proj_stride + (int64_t)h * 2 * AD + AD + tid];
+        out[(int64_t)t * out_stride + (int64_t)h * AD + tid] = acc / L * sigmoidf_ref(gate);
     }
 }
 
@@ -765,10 +840,11 @@ int launch_conv_prefill(const float* proj, int64_t proj_stride, int T, int chann
 
 int launch_delta(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
                  const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
-                 cudaStream_t s) {
+                 cudaStream_t s, const float* conv_w, float* hist, int CK, int* group_count) {
     if (dd.KD != 128 || dd.VD != 128 || dd.VH % dd.KH) return Q3XK_EUNSUPPORTED;
+    if (conv_w && (T != 1 || CK != 4 || !hist || !group_count)) return Q3XK_EUNSUPPORTED;
     if (launch_pdl(delta_kernel, dim3(dd.VH), dim3(kDeltaThreads), 0, s, proj, proj_stride, T, dd, alog, dt, norm,
-                   state, out, out_stride) != cudaSuccess)
+                   state, out, out_stride, conv_w, hist, group_count) != cudaSuccess)
         return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;

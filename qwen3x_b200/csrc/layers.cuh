@@ -34,9 +34,13 @@ int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const flo
                 cudaStream_t s);
 // norm == nullptr: write the raw delta-rule output (the gated RMS is then
 // applied by the consumer, q3xk_gemv_ex with Q3XK_XFORM_GATED_RMS).
+// conv_w/hist given (T = 1, CK = 4): the causal conv runs inside the kernel
+// on the raw projections (no launch_conv before it); group_count is a device
+// int[KH], zero between launches (the kernel leaves it zero).
 int launch_delta(const float* proj, int64_t proj_stride, int T, const DeltaDims& dd, const float* alog,
                  const float* dt, const float* norm, float* state, float* out, int64_t out_stride,
-                 cudaStream_t s);
+                 cudaStream_t s, const float* conv_w = nullptr, float* hist = nullptr, int CK = 0,
+                 int* group_count = nullptr);
 // Chunked gated DeltaNet over T > 1 tokens (delta.cu): same results as
 // launch_delta with a norm, in parallel over 64-token chunks.  q | k | v come
 // from `qkv` (the conv output, launch_conv_prefill), a, b, z from `proj`.
