@@ -446,6 +446,89 @@ __device__ __forceinline__ void x_stats(const GemvParams& p, float* xstat, float
     __syncthreads();
 }
 
+// Rows of pass `it` for the warp's row group: row0, live, rec[].
+template <int MODE>
+__device__ __forceinline__ void pass_rows(const GemvParams& p, int gb, int ge, int it, int gpc, int group,
+                                          const uint8_t** rec, int& row0, bool& live) {
+    const int gi = gb + it * gpc + group;
+    live = gi < ge;
+    row0 = gi * kRows;
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+        const int row = min(row0 + j, p.rows - 1);
+        if (MODE == kRowGather)
+            rec[j] = p.w + (int64_t)p.ids[row / p.rows_per_expert] * p.expert_stride +
+                     (int64_t)(row % p.rows_per_expert) * p.row_stride;
+        else
+            rec[j] = p.w + (int64_t)row * p.row_stride;
+    }
+}
+
+// The CTA's passes over its row groups [gb, ge): dot products, then the
+// epilogue (y write / accumulate / SwiGLU), K slices combined in shared memory.
+template <int TYPE, bool FAST, int KS, int MODE, bool DB>
+__device__ __forceinline__ void gemv_passes(const GemvParams& p, const uint8_t** rec, Batch<TYPE>& A,
+                                            const float4* xs4, const float2* gg, float* part,
+                                            const int64_t* seg_off, int gb, int ge, int passes, int row0,
+                                            bool live) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ks = warp % KS, group = warp / KS;
+    constexpr int groups_per_cta = kWarps / KS;
+    const int r = (lane & 16 ? 2 : 0) + (lane & 8 ? 1 : 0);
+    for (int it = 0; it < passes; ++it) {
+        if (it > 0) {
+            pass_rows<MODE>(p, gb, ge, it, groups_per_cta, group, rec, row0, live);
+            if (live) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+        }
+        const float k = live ? warp_rows<TYPE, FAST, KS, MODE, DB>(p, rec, lane, ks, A, xs4, gg, seg_off) : 0.f;
+        if (KS == 1) {
+            if (p.epi) {
+                const float u = __shfl_down_sync(0xffffffffu, k, 16);  // lanes 0, 8 <- rows 2, 3
+                if ((lane == 0 || lane == 8) && live && row0 < p.rows) {
+                    float h = k * sigmoid_ref(k) * u;
+                    if (p.ew) h = __ldg(p.ew + row0 / p.rows_per_expert) * h;
+                    p.y[row0 / 2 + (lane >> 3)] = h;
+                }
+            } else if ((lane & 7) == 0 && live && row0 + r < p.rows) {
+                float* yp = p.y + row0 + r;
+                *yp = p.accumulate ? *yp + k : k;
+            }
+            continue;
+        }
+        // Slices of a row group meet in shared memory, added in slice order.
+        if ((lane & 7) == 0) part[warp * kRows + r] = k;
+        __syncthreads();
+        const int gbase = gb + it * groups_per_cta;
+        if (p.epi) {
+            if (tid < groups_per_cta * 2) {
+                const int g = tid / 2, rr = tid % 2;
+                const int grow = (gbase + g) * kRows;
+                if (gbase + g < ge && grow < p.rows) {
+                    float vg = 0.f, vu = 0.f;
+#pragma unroll
+                    for (int sl = 0; sl < KS; ++sl) {
+                        vg += part[(g * KS + sl) * kRows + rr];
+                        vu += part[(g * KS + sl) * kRows + rr + 2];
+                    }
+                    float h = vg * sigmoid_ref(vg) * vu;
+                    if (p.ew) h = __ldg(p.ew + grow / p.rows_per_expert) * h;
+                    p.y[grow / 2 + rr] = h;
+                }
+            }
+        } else if (tid < groups_per_cta * kRows) {
+            const int g = tid / kRows, rr = tid % kRows;
+            const int row = (gbase + g) * kRows + rr;
+            if (gbase + g < ge && row < p.rows) {
+                float v = 0.f;
+#pragma unroll
+                for (int sl = 0; sl < KS; ++sl) v += part[(g * KS + sl) * kRows + rr];
+                p.y[row] = p.accumulate ? p.y[row] + v : v;
+            }
+        }
+        __syncthreads();  // part[] is reused by the next pass
+    }
+}
+
 // XF: the input transform is compiled in (p.xform may be non-zero).
 // DB: two register batches per warp (kDbBlocks CTAs per SM instead of 3).
 template <int TYPE, int KS, int MODE, bool XF, bool DB>
@@ -460,20 +543,24 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
     griddep_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ks = warp % KS;                 // K slice of this warp
-    constexpr int groups_per_cta = kWarps / KS;  // row groups per CTA
+    constexpr int groups_per_cta = kWarps / KS;  // row groups per CTA and pass
     const int group = warp / KS;
-    const int row0 = (blockIdx.x * groups_per_cta + group) * kRows;
+    // This CTA's balanced share of the row groups (4 rows each): [gb, ge).
+    const int64_t gt = (p.rows + kRows - 1) / kRows;
+    const int gb = (int)(blockIdx.x * gt / gridDim.x), ge = (int)((blockIdx.x + 1) * gt / gridDim.x);
+    const int passes = (ge - gb + groups_per_cta - 1) / groups_per_cta;  // uniform over the CTA
     __shared__ int64_t seg_off[kMaxSegments];
     const uint8_t* rec[kRows];
     Batch<TYPE> A;
+    int row0 = 0;
+    bool live = false;
     if (MODE == kPlain) {
-#pragma unroll
-        for (int j = 0; j < kRows; ++j) rec[j] = p.w + (int64_t)min(row0 + j, p.rows - 1) * p.row_stride;
+        pass_rows<MODE>(p, gb, ge, 0, groups_per_cta, group, rec, row0, live);
         // The first batch of weights is requested before waiting on the previous kernel.
 #if Q3XK_GEMV_PREFETCH
-        if (row0 < p.rows) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
+        if (live) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
 #else
-        if (row0 < p.rows) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+        if (live) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
 #endif
         griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
     } else {
@@ -482,19 +569,11 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
             if (tid < p.units / p.units_per_seg) seg_off[tid] = (int64_t)p.ids[tid] * p.expert_stride;
             __syncthreads();
         }
-#pragma unroll
-        for (int j = 0; j < kRows; ++j) {
-            const int row = min(row0 + j, p.rows - 1);
-            if (MODE == kRowGather)
-                rec[j] = p.w + (int64_t)p.ids[row / p.rows_per_expert] * p.expert_stride +
-                         (int64_t)(row % p.rows_per_expert) * p.row_stride;
-            else
-                rec[j] = p.w + (int64_t)row * p.row_stride;
-        }
+        pass_rows<MODE>(p, gb, ge, 0, groups_per_cta, group, rec, row0, live);
 #if Q3XK_GEMV_PREFETCH
-        if (row0 < p.rows) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
+        if (live) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
 #else
-        if (row0 < p.rows) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
+        if (live) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
 #endif
     }
 
@@ -535,7 +614,6 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
         gg[u] = gu;
     }
     const int any_slow = __syncthreads_or(slow);
-    float k = 0.f;
     if (any_slow) {
         // Exact fallback for the whole CTA: unscaled x in the same slot order.
         for (int u = tid; u < p.units; u += kThreads) {
@@ -549,58 +627,11 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
                                 v[C::element(4 * j + 2)], v[C::element(4 * j + 3)]);
         }
         __syncthreads();
-        if (row0 < p.rows) k = warp_rows<TYPE, false, KS, MODE, DB>(p, rec, lane, ks, A, xs4, gg, seg_off);
-    } else {
-        if (row0 < p.rows) k = warp_rows<TYPE, true, KS, MODE, DB>(p, rec, lane, ks, A, xs4, gg, seg_off);
     }
-    const int r = (lane & 16 ? 2 : 0) + (lane & 8 ? 1 : 0);
-    if (KS == 1) {
-        if (p.epi) {
-            const float u = __shfl_down_sync(0xffffffffu, k, 16);  // lanes 0, 8 <- rows 2, 3
-            if ((lane == 0 || lane == 8) && row0 < p.rows) {
-                float h = k * sigmoid_ref(k) * u;
-                if (p.ew) h = __ldg(p.ew + row0 / p.rows_per_expert) * h;
-                p.y[row0 / 2 + (lane >> 3)] = h;
-            }
-            return;
-        }
-        if ((lane & 7) == 0 && row0 + r < p.rows) {
-            float* yp = p.y + row0 + r;
-            *yp = p.accumulate ? *yp + k : k;
-        }
-        return;
-    }
-    // Slices of a row group meet in shared memory, added in slice order.
-    if ((lane & 7) == 0) part[warp * kRows + r] = k;
-    __syncthreads();
-    if (p.epi) {
-        if (tid < groups_per_cta * 2) {
-            const int g = tid / 2, rr = tid % 2;
-            const int grow = (blockIdx.x * groups_per_cta + g) * kRows;
-            if (grow < p.rows) {
-                float vg = 0.f, vu = 0.f;
-#pragma unroll
-                for (int s = 0; s < KS; ++s) {
-                    vg += part[(g * KS + s) * kRows + rr];
-                    vu += part[(g * KS + s) * kRows + rr + 2];
-                }
-                float h = vg * sigmoid_ref(vg) * vu;
-                if (p.ew) h = __ldg(p.ew + grow / p.rows_per_expert) * h;
-                p.y[grow / 2 + rr] = h;
-            }
-        }
-        return;
-    }
-    if (tid < groups_per_cta * kRows) {
-        const int g = tid / kRows, rr = tid % kRows;
-        const int row = (blockIdx.x * groups_per_cta + g) * kRows + rr;
-        if (row < p.rows) {
-            float v = 0.f;
-#pragma unroll
-            for (int s = 0; s < KS; ++s) v += part[(g * KS + s) * kRows + rr];
-            p.y[row] = p.accumulate ? p.y[row] + v : v;
-        }
-    }
+    if (any_slow)
+        gemv_passes<TYPE, false, KS, MODE, DB>(p, rec, A, xs4, gg, part, seg_off, gb, ge, passes, row0, live);
+    else
+        gemv_passes<TYPE, true, KS, MODE, DB>(p, rec, A, xs4, gg, part, seg_off, gb, ge, passes, row0, live);
 }
 
 int sm_count_cached() {
@@ -647,8 +678,11 @@ int launch_ks(const GemvParams& p, size_t smem, cudaStream_t s) {
             return Q3XK_ECUDA;
         configured = 200 * 1024;
     }
-    constexpr int rows_per_cta = (kWarps / KS) * kRows;
-    const int64_t grid = (p.rows + rows_per_cta - 1) / rows_per_cta;
+    // One CTA per resident slot (or per row group when there are fewer), each
+    // with a balanced share of the row groups: every SM streams the same bytes.
+    const int64_t groups = (p.rows + kRows - 1) / kRows;
+    const int64_t slots = (int64_t)sm_count_cached() * (DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCKS);
+    const int64_t grid = groups < slots ? groups : slots;
 #if Q3XK_GEMV_PDL
     const cudaError_t e =
         launch_pdl(gemv_kernel<TYPE, KS, MODE, XF, DB>, dim3((unsigned)grid), dim3(kThreads), smem, s, p);
