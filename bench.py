@@ -521,7 +521,10 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling)")
     ap.add_argument("--no-engine", action="store_true", help="skip the end-to-end model legs")
-    ap.add_argument("--engine-prompt", type=int, default=4096)
+    ap.add_argument("--engine-config", type=int, default=9000,
+                    help="model ID of the end-to-end leg: 9000 (cfg3, 9B Q8_0), 36035 (cfg4, 35B-A3B "
+                         "MoE Q4_0), 27008 (cfg5, 27B-shaped Q8_0)")
+    ap.add_argument("--engine-prompt", type=int, default=None, help="prompt tokens (default per config)")
     ap.add_argument("--engine-decode", type=int, default=256)
     ap.add_argument("--only", choices=["gemv", "gemm", "engine"], default=None,
                     help="run one kernel family only (for profiling; no JSON line)")
@@ -544,8 +547,11 @@ def main(argv=None):
                       f"{2 * 4096 * ROWS * COLS / secs / 1e12:.1f} TFLOP/s", flush=True)
         return 0
 
+    prompts = {9000: 4096, 36035: 2048, 27008: 16384}  # BASELINE configs 3, 4, 5
+    if args.engine_prompt is None:
+        args.engine_prompt = prompts.get(args.engine_config, 4096)
     if args.only == "engine":
-        print(json.dumps(time_engine(9000, args.engine_prompt, args.engine_decode, device,
+        print(json.dumps(time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
                                      rank == 0 and not args.no_cpu_baseline)), flush=True)
         return 0
 
@@ -583,7 +589,7 @@ def main(argv=None):
 
     engine = None
     if args.only is None and not args.no_engine:
-        engine = time_engine(9000, args.engine_prompt, args.engine_decode, device,
+        engine = time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
                              rank == 0 and world == 1 and not args.no_cpu_baseline)
 
     cpu = None

@@ -721,7 +721,7 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
               s->alloc(&s->hidden, (size_t)chunk * c.H) &&
               s->alloc(&s->normed, (size_t)chunk * c.H) && s->alloc(&s->proj, (size_t)chunk * model->P) &&
               s->alloc(&s->mix, (size_t)chunk * model->mix) &&
-              s->alloc(&s->part, (size_t)chunk * c.AH * nsplit * (c.AD + 2));
+              s->alloc(&s->part, (size_t)c.AH * nsplit * (c.AD + 2));  // decode attention partials
     if (ok && c.experts) {
         const int S = c.top_k + 1;
         ok = s->alloc(&s->rlogits, c.experts + 1) && s->alloc(&s->rweights, S) && s->alloc(&s->rids, S) &&
