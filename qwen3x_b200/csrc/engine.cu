@@ -171,6 +171,7 @@ struct State {
     float *rlogits = nullptr, *rweights = nullptr, *hbuf = nullptr;
     float* delta_work = nullptr;  // chunked DeltaNet workspace (prefill)
     float* qkv = nullptr;         // conv output q | k | v of a prefill pass [chunk][DQKV]
+    MoePrefillArgs moe{};         // work buffers of the grouped MoE prompt path
     int* rids = nullptr;
     int* group_count = nullptr;  // [KH] arrival counts of the fused-conv delta kernel (kept zero)
     void* gemm_ws = nullptr;
@@ -642,7 +643,20 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
             Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
             ++ai;
         }
-        if (c.experts) {
+        if (c.experts && !s.exact_prefill) {
+            // grouped expert GEMMs on tcgen05 for the whole pass
+            Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
+            MoePrefillArgs a = s.moe;
+            a.router = &l.router;
+            a.gate_up = &l.gate_up;
+            a.down = &l.down;
+            a.experts = c.experts;
+            a.top_k = c.top_k;
+            a.T = T;
+            a.x = s.normed;
+            a.hidden = s.hidden;
+            Q3XB_TRY(moe_prefill(a, st));
+        } else if (c.experts) {
             for (int t = 0; t < T; ++t) Q3XB_TRY(moe_token(s, c, l, t));
         } else {
             Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
@@ -726,6 +740,17 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
         const int S = c.top_k + 1;
         ok = s->alloc(&s->rlogits, c.experts + 1) && s->alloc(&s->rweights, S) && s->alloc(&s->rids, S) &&
              s->alloc(&s->hbuf, (size_t)S * c.I);
+    }
+    if (ok && c.experts && chunk > 1) {
+        const int S = c.top_k + 1, E1 = c.experts + 1;
+        const size_t P = (size_t)chunk * S;
+        MoePrefillArgs& a = s->moe;
+        ok = s->alloc(&a.logits, (size_t)chunk * E1) && s->alloc(&a.ids, P) && s->alloc(&a.weights, P) &&
+             s->alloc(&a.xoff, E1 + 1) && s->alloc(&a.tile_gu, E1 + 1) && s->alloc(&a.tile_dn, E1 + 1) &&
+             s->alloc(&a.pos, P) && s->alloc(&a.pair_token, P) && s->alloc(&a.pair_weight, P) &&
+             s->alloc(&a.x16, (size_t)chunk * c.H) && s->alloc(&a.scale, chunk) && s->alloc(&a.x16g, P * c.H) &&
+             s->alloc(&a.scale_g, P) && s->alloc(&a.gu, P * 2 * c.I) && s->alloc(&a.h16, P * c.I) &&
+             s->alloc(&a.scale_h, P) && s->alloc(&a.out, P * c.H);
     }
     if (ok && chunk > 1 && delta_layers > 0)
         ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4) &&

@@ -19,6 +19,7 @@
 //    walk the tiles; every mbarrier wait is bounded.
 #include <cuda.h>
 
+#include "layers.cuh"
 #include "tc.cuh"
 
 namespace q3xk {
@@ -64,7 +65,42 @@ struct GemmParams {
     float* y;
     int accumulate;
     int tiles_w, tiles_t, ksteps;
+    // Expert-grouped mode (groups > 0): X rows [xoff[e], xoff[e+1]) use expert
+    // e of the pool (weight rows e*N ..), their tiles are [tile_off[e],
+    // tile_off[e+1]) of the tile space; both arrays live on the device.
+    int groups;
+    const int* xoff;
+    const int* tile_off;
 };
+
+// One tile of work: weight rows (TMA row of the pool), output columns, X/Y rows.
+struct TileCoord {
+    int w_row, n0, x_row, t_valid;
+};
+
+template <int BN>
+__device__ __forceinline__ TileCoord tile_coord(const GemmParams& p, int tile) {
+    if (!p.groups) {
+        const int wt = tile / p.tiles_t, tt = tile % p.tiles_t;
+        return {wt * BM, wt * BM, tt * BN, min(BN, p.T - tt * BN)};
+    }
+    int lo = 0, hi = p.groups;  // largest e with tile_off[e] <= tile
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (__ldg(p.tile_off + mid) <= tile) lo = mid;
+        else hi = mid;
+    }
+    const int x0 = __ldg(p.xoff + lo), count = __ldg(p.xoff + lo + 1) - x0;
+    const int tt_e = (count + BN - 1) / BN;
+    const int local = tile - __ldg(p.tile_off + lo);
+    const int wt = local / tt_e, tt = local % tt_e;
+    return {lo * p.N + wt * BM, wt * BM, x0 + tt * BN, min(BN, count - tt * BN)};
+}
+
+template <int BN>
+__device__ __forceinline__ int tile_count(const GemmParams& p) {
+    return p.groups ? __ldg(p.tile_off + p.groups) : p.tiles_w * p.tiles_t;
+}
 
 // Per token-tile-width geometry: BN tokens per tile = MMA N (64, 128, 256).
 template <int BN>
@@ -257,18 +293,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem = *tmem_base_p;
     griddep_launch_dependents();
-
-    const int tiles = p.tiles_w * p.tiles_t;
+    griddep_wait();  // X16, the scales and (grouped) the tile table come from earlier kernels
+    const int tiles = tile_count<BN>(p);
 
     if (warp == 0) {
         // ---------------- TMA producer: X16 tiles and raw weight stages ----------------
-        griddep_wait();  // X16 is written by the conversion kernel
         if (lane == 0) {
             const int qdiv = TYPE == Q3XK_Q4_0 ? 2 : 1;  // quant bytes per column
             const uint32_t raw_tx = (uint32_t)(BM * (RAWK / qdiv) + kRawScaleBytes);
             int it = 0, rit = 0;
             for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x) {
-                const int wt = tile / p.tiles_t, tt = tile % p.tiles_t;
+                const TileCoord tc = tile_coord<BN>(p, tile);
                 bool ok = true;
                 for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
                     if (ks % (RAWK / BK) == 0) {
@@ -279,8 +314,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                         }
                         uint8_t* dst = sraw + r * kRawBytes;
                         mbar_arrive_expect_tx(&raw_full[r], raw_tx);
-                        tma_load_2d(dst, &qmap, ks * BK / qdiv, wt * BM, &raw_full[r]);
-                        tma_load_2d(dst + kRawQuantBytes, &smap, ks * BK / 32, wt * BM, &raw_full[r]);
+                        tma_load_2d(dst, &qmap, ks * BK / qdiv, tc.w_row, &raw_full[r]);
+                        tma_load_2d(dst + kRawQuantBytes, &smap, ks * BK / 32, tc.w_row, &raw_full[r]);
                         ++rit;
                     }
                     const int s = it % kStages;
@@ -289,7 +324,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                         break;
                     }
                     mbar_arrive_expect_tx(&full[s], kTileBytesX);
-                    tma_load_2d(sx + s * kTileBytesX, &xmap, ks * BK, tt * BN, &full[s]);
+                    tma_load_2d(sx + s * kTileBytesX, &xmap, ks * BK, tc.x_row, &full[s]);
                 }
                 if (!ok) break;
             }
@@ -364,27 +399,25 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         }
     } else {
         // ---------------- epilogue (TMEM -> Y) ----------------
-        griddep_wait();  // Y may be read (accumulate) and must not be written early
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         int lt = 0;
         for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x, ++lt) {
-            const int wt = tile / p.tiles_t, tt = tile % p.tiles_t;
+            const TileCoord tc = tile_coord<BN>(p, tile);
             const int b = lt % kAcc;
             int good = 1;
             if (lane == 0) good = wait_or_flag(&acc_full[b], (lt / kAcc) & 1, cta_err);
             good = __shfl_sync(0xffffffffu, good, 0);
             if (!good) break;
             tc_fence_after();
-            const int n = wt * BM + 32 * q + lane;
+            const int n = tc.n0 + 32 * q + lane;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t r[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + b * BN + c0, r);
-                const int t0 = tt * BN + c0;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int t = t0 + j;
-                    if (t < p.T && n < p.N) {
+                    if (c0 + j < tc.t_valid && n < p.N) {
+                        const int t = tc.x_row + c0 + j;
                         const float v = __uint_as_float(r[j]) * __ldg(&p.tok_scale[t]);
                         float* yp = p.y + (int64_t)t * p.N + n;
                         *yp = p.accumulate ? *yp + v : v;
@@ -438,6 +471,98 @@ int sm_count() {
 }
 
 }  // namespace
+
+int launch_x_to_f16(const float* x, int T, int K, __half* x16, float* tok_scale, cudaStream_t s) {
+    if (K % 8) return Q3XK_EINVAL;  // TMA row stride of X16 must be a multiple of 16 bytes
+    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, tok_scale, K) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int gemm_f16(const q3xk_matrix* w, const __half* x16, const float* tok_scale, int T, float* y, int accumulate,
+             const GemmGroups* groups, int bn_hint, cudaStream_t s) {
+    const int K = w->cols;
+    if (K % 8 || ((uintptr_t)x16 & 15) || ((uintptr_t)w->data & 15)) return Q3XK_EALIGN;
+    // Token tile = MMA N: the smallest of 64/128/256 that covers T, else 256 (grouped: 64).
+    const int bn = groups ? 64 : bn_hint ? bn_hint : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    EncodeTiled enc = encode_fn();
+    if (!enc) return Q3XK_ECUDA;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {BK, (cuuint32_t)bn};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return Q3XK_ECUDA;
+
+    // Raw weights: the quant bytes of every row record (uint8, [rows][qbytes])
+    // and the scales ([rows][cols/32] FP16), both with the record stride; a
+    // pool is one tensor of experts * rows rows.
+    const int64_t qbytes = quant_bytes(w->type, K);
+    const int64_t all_rows = (int64_t)w->rows * (groups ? w->experts : 1);
+    CUtensorMap qmap, smap;
+    {
+        const cuuint64_t qd[2] = {(cuuint64_t)qbytes, (cuuint64_t)all_rows};
+        const cuuint64_t qs[1] = {(cuuint64_t)w->row_stride};
+        const cuuint32_t qb[2] = {(cuuint32_t)(w->type == Q3XK_Q4_0 ? RAWK / 2 : RAWK), BM};
+        if (enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->data, qd, qs, qb, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return Q3XK_ECUDA;
+        const cuuint64_t sd[2] = {(cuuint64_t)(K / kBlock), (cuuint64_t)all_rows};
+        const cuuint32_t sb[2] = {8, BM};
+        if (enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, static_cast<uint8_t*>(w->data) + qbytes, sd, qs, sb, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return Q3XK_ECUDA;
+    }
+
+    GemmParams p{};
+    p.w = static_cast<const uint8_t*>(w->data);
+    p.row_stride = w->row_stride;
+    p.qbytes = qbytes;
+    p.N = w->rows;
+    p.K = K;
+    p.T = T;
+    p.tok_scale = tok_scale;
+    p.y = y;
+    p.accumulate = accumulate ? 1 : 0;
+    p.tiles_w = (w->rows + BM - 1) / BM;
+    p.tiles_t = (T + bn - 1) / bn;
+    p.ksteps = (K + BK - 1) / BK;
+    if (groups) {
+        p.groups = groups->groups;
+        p.xoff = groups->xoff;
+        p.tile_off = groups->tile_off;
+    }
+    const size_t smem = gemm_smem_bytes();
+    using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+    const int q8 = w->type == Q3XK_Q8_0;
+    const int slot = (q8 ? 0 : 3) + (bn == 64 ? 0 : bn == 128 ? 1 : 2);
+    static const Kern kernels[6] = {gemm_kernel<Q3XK_Q8_0, 64>, gemm_kernel<Q3XK_Q8_0, 128>,
+                                    gemm_kernel<Q3XK_Q8_0, 256>, gemm_kernel<Q3XK_Q4_0, 64>,
+                                    gemm_kernel<Q3XK_Q4_0, 128>, gemm_kernel<Q3XK_Q4_0, 256>};
+    static bool configured[6] = {false, false, false, false, false, false};
+    const Kern kern = kernels[slot];
+    if (!configured[slot]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return Q3XK_ECUDA;
+        configured[slot] = true;
+    }
+    // grouped: the tile count is only known on the device -> one CTA per SM
+    const int tiles = groups ? sm_count() : p.tiles_w * p.tiles_t;
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    const cudaError_t e1 = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, qmap, smap, p);
+    if (e1 != cudaSuccess) return Q3XK_ECUDA;
+    count_launch();
+    return last_launch_status();
+}
+
+size_t gemm_grouped_tile_width() { return 64; }
+
 }  // namespace q3xk
 
 using namespace q3xk;
@@ -455,7 +580,6 @@ int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumul
     if (!w || !w->data || !x || !y || T <= 0 || w->rows <= 0 || w->cols <= 0) return Q3XK_EINVAL;
     if (w->type != Q3XK_Q8_0 && w->type != Q3XK_Q4_0) return Q3XK_EUNSUPPORTED;
     if (w->cols % kBlock || w->row_stride != row_record_bytes(w->type, w->cols)) return Q3XK_EINVAL;
-    if (w->cols % 8) return Q3XK_EINVAL;  // TMA row stride of X16 must be a multiple of 16 bytes
     size_t need = 0;
     q3xk_gemm_workspace_bytes(T, w->cols, &need);
     if (!workspace || workspace_bytes < need) return Q3XK_EWORKSPACE;
@@ -465,78 +589,9 @@ int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumul
     const int K = w->cols;
     __half* x16 = static_cast<__half*>(workspace);
     float* tok_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (((size_t)T * K * 2 + 255) & ~(size_t)255));
-
-    // Token tile = MMA N: the smallest of 64/128/256 that covers T, else 256.
-    const int bn = T <= 64 ? 64 : T <= 128 ? 128 : 256;
-    EncodeTiled enc = encode_fn();
-    if (!enc) return Q3XK_ECUDA;
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
-    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {BK, (cuuint32_t)bn};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return Q3XK_ECUDA;
-
-    // Raw weights: the quant bytes of every row record (uint8, [rows][qbytes])
-    // and the scales ([rows][cols/32] FP16), both with the record stride.
-    const int64_t qbytes = quant_bytes(w->type, K);
-    CUtensorMap qmap, smap;
-    {
-        const cuuint64_t qd[2] = {(cuuint64_t)qbytes, (cuuint64_t)w->rows};
-        const cuuint64_t qs[1] = {(cuuint64_t)w->row_stride};
-        const cuuint32_t qb[2] = {(cuuint32_t)(w->type == Q3XK_Q4_0 ? RAWK / 2 : RAWK), BM};
-        if (enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->data, qd, qs, qb, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return Q3XK_ECUDA;
-        const cuuint64_t sd[2] = {(cuuint64_t)(K / kBlock), (cuuint64_t)w->rows};
-        const cuuint32_t sb[2] = {8, BM};
-        if (enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, static_cast<uint8_t*>(w->data) + qbytes, sd, qs, sb, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return Q3XK_ECUDA;
-    }
-
-    const cudaError_t e0 = launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, tok_scale, K);
-    if (e0 != cudaSuccess) return Q3XK_ECUDA;
-    count_launch();
-
-    GemmParams p{};
-    p.w = static_cast<const uint8_t*>(w->data);
-    p.row_stride = w->row_stride;
-    p.qbytes = qbytes;
-    p.N = w->rows;
-    p.K = K;
-    p.T = T;
-    p.tok_scale = tok_scale;
-    p.y = y;
-    p.accumulate = accumulate ? 1 : 0;
-    p.tiles_w = (w->rows + BM - 1) / BM;
-    p.tiles_t = (T + bn - 1) / bn;
-    p.ksteps = (K + BK - 1) / BK;
-    const size_t smem = gemm_smem_bytes();
-    using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
-    const int q8 = w->type == Q3XK_Q8_0;
-    const int slot = (q8 ? 0 : 3) + (bn == 64 ? 0 : bn == 128 ? 1 : 2);
-    static const Kern kernels[6] = {gemm_kernel<Q3XK_Q8_0, 64>, gemm_kernel<Q3XK_Q8_0, 128>,
-                                    gemm_kernel<Q3XK_Q8_0, 256>, gemm_kernel<Q3XK_Q4_0, 64>,
-                                    gemm_kernel<Q3XK_Q4_0, 128>, gemm_kernel<Q3XK_Q4_0, 256>};
-    static bool configured[6] = {false, false, false, false, false, false};
-    const Kern kern = kernels[slot];
-    if (!configured[slot]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return Q3XK_ECUDA;
-        configured[slot] = true;
-    }
-    const int tiles = p.tiles_w * p.tiles_t;
-    const int grid = tiles < sm_count() ? tiles : sm_count();
-    const cudaError_t e1 = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, qmap, smap, p);
-    if (e1 != cudaSuccess) return Q3XK_ECUDA;
-    count_launch();
-    return last_launch_status();
+    const int st = launch_x_to_f16(x, T, K, x16, tok_scale, s);
+    if (st != Q3XK_OK) return st;
+    return gemm_f16(w, x16, tok_scale, T, y, accumulate, nullptr, 0, s);
 }
 
 int q3xk_gemm_device_error(int* flags) {

@@ -28,6 +28,52 @@ int repack_swiglu(const q3xk_matrix* m, const void* packed, int64_t src_rows, in
 int gemv_swiglu(const q3xk_matrix* w, const float* x, float* y, const int* ids, int slots, const float* slot_w,
                 const q3xk_xform* xf, cudaStream_t s);
 
+// ---- dequant-GEMM internals (gemm.cu) --------------------------------------------
+// Expert-grouped tiles: X rows [xoff[e], xoff[e+1]) multiply expert e of a
+// pool; tile_off[e] = first tile of expert e (tiles_w * ceil(count/64) each),
+// tile_off[groups] = total.  Device arrays.
+struct GemmGroups {
+    int groups;
+    const int* xoff;
+    const int* tile_off;
+};
+// X (FP32 [T][K]) -> FP16 with a per-row power-of-two scale (tok_scale = 2^-s).
+int launch_x_to_f16(const float* x, int T, int K, __half* x16, float* tok_scale, cudaStream_t s);
+// Y[T][N] (+)= X16 W^T * tok_scale on tcgen05; `groups` selects the expert-grouped tiles
+// (then W is a pool of groups experts and T the packed row count).
+int gemm_f16(const q3xk_matrix* w, const __half* x16, const float* tok_scale, int T, float* y, int accumulate,
+             const GemmGroups* groups, int bn_hint, cudaStream_t s);
+size_t gemm_grouped_tile_width();
+
+// MoE FFN over T prompt tokens on tcgen05 (moe.cu): router for all tokens,
+// device top-k, pairs grouped by expert, grouped gate|up GEMM, weighted
+// SwiGLU, grouped down GEMM, per-token sum of the slots added to hidden.
+struct MoePrefillArgs {
+    const q3xk_matrix* router;   // BF16 [E+1][H] (router rows + shared gate)
+    const q3xk_matrix* gate_up;  // pool [E+1][2I][H], SwiGLU-interleaved rows
+    const q3xk_matrix* down;     // pool [E+1][H][I]
+    int experts, top_k, T;
+    const float* x;  // RMSNorm(hidden) [T][H]
+    float* hidden;   // [T][H], += MoE output
+    // work (device): sizes for P = T * (top_k + 1) pairs
+    float* logits;       // [T][E+1]
+    int* ids;            // [T][S]
+    float* weights;      // [T][S]
+    int *xoff, *tile_gu, *tile_dn;  // [E+2]
+    int* pos;            // [P]
+    int* pair_token;     // [P]
+    float* pair_weight;  // [P]
+    __half* x16;         // [T][H]
+    float* scale;        // [T]
+    __half* x16g;        // [P][H]
+    float* scale_g;      // [P]
+    float* gu;           // [P][2I]
+    __half* h16;         // [P][I]
+    float* scale_h;      // [P]
+    float* out;          // [P][H]
+};
+int moe_prefill(const MoePrefillArgs& a, cudaStream_t s);
+
 int launch_embed(const q3xk_matrix& m, const int* tokens, int T, float* out, cudaStream_t s);
 int launch_rms(const float* x, const float* w1, int n, int T, float* out, cudaStream_t s);
 int launch_conv(float* proj, int64_t proj_stride, int T, int channels, const float* w, int CK, float* hist,

@@ -14,6 +14,7 @@
 #include <float.h>
 
 #include "common.cuh"
+#include "layers.cuh"
 
 namespace q3xk {
 namespace {
@@ -26,6 +27,10 @@ __global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict
                                                          float* __restrict__ weights) {
     griddep_wait();
     griddep_launch_dependents();
+    // one token per block: block b reads row b of [T][experts + with_shared] logits
+    logits += (int64_t)blockIdx.x * (experts + with_shared);
+    ids += (int64_t)blockIdx.x * (top_k + with_shared);
+    weights += (int64_t)blockIdx.x * (top_k + with_shared);
     const int lane = threadIdx.x;
     float p[kMaxPerLane];
     float mx = -INFINITY;
@@ -156,7 +161,199 @@ __global__ void __launch_bounds__(512) argmax_final_kernel(const ArgBest* __rest
 
 constexpr int kArgmaxParts = 148;
 
+// ---- MoE over a prompt: routing for all tokens, grouping by expert ------------
+
+// logits[t][e] = router row e . x_t for T tokens (BF16 row records, FP32 sums);
+// CTA = 8 tokens (one per warp) x 32 router rows.
+__global__ void __launch_bounds__(256) router_batch_kernel(const uint8_t* __restrict__ w, int64_t row_stride,
+                                                           int rows, int H, const float* __restrict__ x, int T,
+                                                           float* __restrict__ logits) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    const float* xt = x + (int64_t)t * H;
+    for (int j = 0; j < 32; ++j) {
+        const int e = blockIdx.y * 32 + j;
+        if (e >= rows) break;
+        const uint16_t* wr = reinterpret_cast<const uint16_t*>(w + (int64_t)e * row_stride);
+        float acc = 0.f;
+        for (int k = lane * 8; k < H; k += 256) {
+            const uint4 q = *reinterpret_cast<const uint4*>(wr + k);
+            const float4 x0 = *reinterpret_cast<const float4*>(xt + k);
+            const float4 x1 = *reinterpret_cast<const float4*>(xt + k + 4);
+            acc += __uint_as_float(q.x << 16) * x0.x + __uint_as_float(q.x & 0xFFFF0000u) * x0.y +
+                   __uint_as_float(q.y << 16) * x0.z + __uint_as_float(q.y & 0xFFFF0000u) * x0.w +
+                   __uint_as_float(q.z << 16) * x1.x + __uint_as_float(q.z & 0xFFFF0000u) * x1.y +
+                   __uint_as_float(q.w << 16) * x1.z + __uint_as_float(q.w & 0xFFFF0000u) * x1.w;
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) logits[(int64_t)t * rows + e] = acc;
+    }
+}
+
+// Groups the (token, slot) pairs by expert.  One CTA.  Outputs: xoff[E+1]
+// (first packed row of each expert), tile_off_a/b[E+1] (first GEMM tile of each
+// expert for two GEMMs with tiles_a / tiles_b weight-row tiles), pos[T*S]
+// (packed row of each pair), pair_token[P], pair_weight[P].  Positions inside
+// an expert depend on arrival order; every packed row is computed
+// independently, so results do not.
+__global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__ ids, const float* __restrict__ wts,
+                                                         int pairs, int S, int experts, int tiles_a, int tiles_b,
+                                                         int bn, int* __restrict__ xoff, int* __restrict__ tile_a,
+                                                         int* __restrict__ tile_b, int* __restrict__ pos,
+                                                         int* __restrict__ pair_token, float* __restrict__ pair_weight) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ int gsm[];
+    int* count = gsm;             // [experts]
+    int* cursor = gsm + experts;  // [experts]
+    for (int e = threadIdx.x; e < experts; e += blockDim.x) count[e] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < pairs; i += blockDim.x) atomicAdd(&count[ids[i]], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int x = 0, ta = 0, tb = 0;
+        for (int e = 0; e < experts; ++e) {
+            xoff[e] = x;
+            tile_a[e] = ta;
+            tile_b[e] = tb;
+            cursor[e] = x;
+            const int tt = (count[e] + bn - 1) / bn;
+            x += count[e];
+            ta += tiles_a * tt;
+            tb += tiles_b * tt;
+        }
+        xoff[experts] = x;
+        tile_a[experts] = ta;
+        tile_b[experts] = tb;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+        const int p = atomicAdd(&cursor[ids[i]], 1);
+        pos[i] = p;
+        pair_token[p] = i / S;
+        pair_weight[p] = wts[i];
+    }
+}
+
+// x16g[p] = x16[pair_token[p]], scale_g[p] = scale[pair_token[p]] (K halves per row).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ x16,
+                                                          const float* __restrict__ scale,
+                                                          const int* __restrict__ pair_token, int pairs, int K,
+                                                          __half* __restrict__ x16g, float* __restrict__ scale_g) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int p = blockIdx.x;
+    if (p >= pairs) return;
+    const int t = pair_token[p];
+    const uint4* src = reinterpret_cast<const uint4*>(x16 + (int64_t)t * K);
+    uint4* dst = reinterpret_cast<uint4*>(x16g + (int64_t)p * K);
+    for (int i = threadIdx.x; i < K / 8; i += blockDim.x) dst[i] = src[i];
+    if (threadIdx.x == 0) scale_g[p] = scale[t];
+}
+
+// Per packed row p: h = w_p * silu(g) * u over the interleaved gate|up row
+// (g(2j) g(2j+1) u(2j) u(2j+1)), then FP16 with a per-row power-of-two scale
+// (as x_to_f16_kernel) for the down GEMM.  I <= 1024.
+__global__ void __launch_bounds__(256) swiglu_f16_kernel(const float* __restrict__ gu, const float* __restrict__ pw,
+                                                         int pairs, int I, __half* __restrict__ h16,
+                                                         float* __restrict__ scale) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int p = blockIdx.x;
+    if (p >= pairs) return;
+    const float* row = gu + (int64_t)p * 2 * I;
+    const float wt = pw[p];
+    float h[4];
+    uint32_t emax = 0;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int i = threadIdx.x + 256 * a;
+        h[a] = 0.f;
+        if (i < I) {
+            const int c = (i >> 1) * 4 + (i & 1);
+            const float g = row[c], u = row[c + 2];
+            h[a] = wt * (g * sigmoid_ref(g) * u);
+            emax = max(emax, (__float_as_uint(h[a]) >> 23) & 0xFFu);
+        }
+    }
+    __shared__ uint32_t red[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = emax;
+    __syncthreads();
+    emax = 0;
+    for (int i = 0; i < 8; ++i) emax = max(emax, red[i]);
+    const int E = emax == 0xFFu ? 0 : (int)emax - 127;
+    const int sh = min(100, max(-100, 14 - E));
+    const float up = __uint_as_float((uint32_t)(sh + 127) << 23);
+    if (threadIdx.x == 0) scale[p] = __uint_as_float((uint32_t)(127 - sh) << 23);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int i = threadIdx.x + 256 * a;
+        if (i < I) h16[(int64_t)p * I + i] = __float2half_rn(h[a] * up);
+    }
+}
+
+// hidden[t] += sum over slots s (in slot order) of out[pos[t*S + s]].
+__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ out, const int* __restrict__ pos,
+                                                          int S, int H, float* __restrict__ hidden) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int t = blockIdx.x;
+    const int* pt = pos + (int64_t)t * S;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+        float acc = 0.f;
+        for (int sl = 0; sl < S; ++sl) acc += out[(int64_t)pt[sl] * H + j];
+        hidden[(int64_t)t * H + j] += acc;
+    }
+}
+
 }  // namespace
+
+int moe_prefill(const MoePrefillArgs& a, cudaStream_t s) {
+    const int T = a.T, S = a.top_k + 1, E1 = a.experts + 1, P = T * S;
+    const int H = a.gate_up->cols, I = a.down->cols;
+    if (I > 1024 || a.gate_up->rows != 2 * I || a.down->rows != H) return Q3XK_EUNSUPPORTED;
+    // 1. router logits (+ shared gate) for every token, then top-k per token
+    if (launch_pdl(router_batch_kernel, dim3((T + 7) / 8, (E1 + 31) / 32), dim3(256), 0, s,
+                   (const uint8_t*)a.router->data, a.router->row_stride, E1, H, a.x, T, a.logits) != cudaSuccess)
+        return Q3XK_ECUDA;
+    if (launch_pdl(router_topk_kernel, dim3(T), dim3(32), 0, s, (const float*)a.logits, a.experts, a.top_k, 1,
+                   a.ids, a.weights) != cudaSuccess)
+        return Q3XK_ECUDA;
+    // 2. group the pairs by expert
+    const int bn = (int)gemm_grouped_tile_width();
+    const int tiles_a = (a.gate_up->rows + 127) / 128, tiles_b = (a.down->rows + 127) / 128;
+    if (launch_pdl(moe_group_kernel, dim3(1), dim3(1024), (size_t)2 * E1 * sizeof(int), s, (const int*)a.ids,
+                   (const float*)a.weights, P, S, E1, tiles_a, tiles_b, bn, a.xoff, a.tile_gu, a.tile_dn, a.pos,
+                   a.pair_token, a.pair_weight) != cudaSuccess)
+        return Q3XK_ECUDA;
+    // 3. FP16 rows per token, gathered per pair
+    int st = launch_x_to_f16(a.x, T, H, a.x16, a.scale, s);
+    if (st != Q3XK_OK) return st;
+    if (launch_pdl(gather_rows_kernel, dim3(P), dim3(256), 0, s, (const __half*)a.x16, (const float*)a.scale,
+                   (const int*)a.pair_token, P, H, a.x16g, a.scale_g) != cudaSuccess)
+        return Q3XK_ECUDA;
+    // 4. gate|up of every pair on its expert, weighted SwiGLU -> FP16, down
+    const GemmGroups ggu{E1, a.xoff, a.tile_gu}, gdn{E1, a.xoff, a.tile_dn};
+    st = gemm_f16(a.gate_up, a.x16g, a.scale_g, P, a.gu, 0, &ggu, 0, s);
+    if (st != Q3XK_OK) return st;
+    if (launch_pdl(swiglu_f16_kernel, dim3(P), dim3(256), 0, s, (const float*)a.gu, (const float*)a.pair_weight, P,
+                   I, a.h16, a.scale_h) != cudaSuccess)
+        return Q3XK_ECUDA;
+    st = gemm_f16(a.down, a.h16, a.scale_h, P, a.out, 0, &gdn, 0, s);
+    if (st != Q3XK_OK) return st;
+    // 5. add each token's slots into its hidden row, in slot order
+    if (launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, s, (const float*)a.out, (const int*)a.pos, S, H,
+                   a.hidden) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch(7);
+    return Q3XK_OK;
+}
+
 }  // namespace q3xk
 
 using namespace q3xk;
