@@ -358,32 +358,47 @@ def model_file_dir(size: int) -> str:
     return tempfile.gettempdir()
 
 
-def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sample: bool):
+def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sample: bool,
+                rank: int = 0, world: int = 1):
     """The backend end to end (q3x_backend.h via qwen3x_b200.backend) on a
     seeded synthetic model.bin of config `cfg_id`: prefill `prompt_len`
     uniform-random tokens in one state_forward call, then `decode_steps`
     greedy steps (state_argmax + state_forward of that token), as the
     reference's runtime drives the backend.  Times are CUDA events on the
-    state's stream; weights (GBs) are far larger than L2."""
+    state's stream (max over ranks); weights (GBs) are far larger than L2.
+    world > 1: tensor parallelism, one rank per GPU (rank 0 writes the file)."""
     import numpy as np
     import torch
 
     from qwen3x_b200 import modelfile
-    from qwen3x_b200.backend import Model, State
+    from qwen3x_b200.backend import Model, State, tp_unique_id
 
     c = modelfile.CONFIGS[cfg_id]
     size = modelfile.file_size(c)
-    path = os.path.join(model_file_dir(size), f"q3x_bench_{cfg_id}_{os.getpid()}.bin")
-    out = {"config": f"{cfg_id} ({c.name})", "prompt_tokens": prompt_len, "decode_steps": decode_steps}
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    tag = os.environ.get("TORCHELASTIC_RUN_ID", str(os.getpid())) if world > 1 else str(os.getpid())
+    path = os.path.join(model_file_dir(size), f"q3x_bench_{cfg_id}_{tag}.bin")
+    out = {"config": f"{cfg_id} ({c.name})", "prompt_tokens": prompt_len, "decode_steps": decode_steps,
+           "parallelism": f"tp{world}" if world > 1 else "single GPU"}
     t0 = time.time()
     try:
-        modelfile.write_model(path, c, seed=7, device=device)
+        if rank == 0:
+            modelfile.write_model(path, c, seed=7, device=device)
+        if dist:
+            dist.barrier()
         out["model_write_s"] = round(time.time() - t0, 1)
         t1 = time.time()
-        model = Model(path)
+        model = Model(path, rank, world)
         out["model_load_s"] = round(time.time() - t1, 1)
         out["model_device_gb"] = round(model.device_bytes / 1e9, 2)
-        st = State(model, prompt_len + decode_steps + 72)
+        nccl_id = None
+        if dist:
+            ids = [tp_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(ids, src=0)
+            nccl_id = ids[0]
+        st = State(model, prompt_len + decode_steps + 72, nccl_id)
         stream = torch.cuda.ExternalStream(st.stream)
         prompt = np.random.default_rng(11).integers(0, c.V, prompt_len).astype(np.int32)
         for _ in range(3):  # warm-up: a short prompt and a few decode steps (captures the graph)
@@ -417,6 +432,10 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
         prefill_s = e0.elapsed_time(e1) / 1e3
         decode_s = e1.elapsed_time(e2) / 1e3
         dev_step_s = e3.elapsed_time(e4) / 1e3 / len(tokens[:64])
+        if dist:  # max over ranks
+            t = torch.tensor([prefill_s, decode_s, dev_step_s], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            prefill_s, decode_s, dev_step_s = (float(v) for v in t.tolist())
         mid = prompt_len + decode_steps // 2
         bpt = decode_bytes_per_token(c, mid)
         peak, peak_kind = measured_peaks()
@@ -435,10 +454,12 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
         })
         st.close()
         model.close()
-        if cpu_sample:
+        if cpu_sample and rank == 0:
             out["cpu_baseline"] = cpu_engine_tok_s(path, c)
+        if dist:
+            dist.barrier()
     finally:
-        if os.path.exists(path):
+        if rank == 0 and os.path.exists(path):
             os.unlink(path)
     return out
 
@@ -551,8 +572,15 @@ def main(argv=None):
     if args.engine_prompt is None:
         args.engine_prompt = prompts.get(args.engine_config, 4096)
     if args.only == "engine":
-        print(json.dumps(time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
-                                     rank == 0 and not args.no_cpu_baseline)), flush=True)
+        res = time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
+                          rank == 0 and world == 1 and not args.no_cpu_baseline, rank, world)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
         return 0
 
     secs, launches, clocks = time_gemv(1, args.steps, args.warmup, device, world, rank == 0)
@@ -588,7 +616,7 @@ def main(argv=None):
         gemm["peak_kind"] = peak_tf[1]
 
     engine = None
-    if args.only is None and not args.no_engine:
+    if args.only is None and not args.no_engine and world == 1:  # tensor-parallel runs: --only engine
         engine = time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
                              rank == 0 and world == 1 and not args.no_cpu_baseline)
 

@@ -96,6 +96,26 @@ Q3XK_API int q3xb_state_set_exact_prefill(q3xb_state* state, int enabled);
  * the maximum; the work buffers are sized for it at state creation). */
 Q3XK_API int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens);
 
+/*
+ * Tensor parallelism (one process per GPU, dense models): each rank loads its
+ * share of model.bin (column-parallel q/k/v/z/a/b, q+gate, gate/up and
+ * lm_head rows; row-parallel out/down columns, partial sums all-reduced with
+ * NCCL) and owns a State whose collectives run on the state's stream.  Rank 0
+ * makes a communicator id with q3xb_tp_unique_id and every rank passes the
+ * same 128 bytes to q3xb_state_create_tp.  state_forward, state_argmax and
+ * state_copy_logits are collective: every rank calls them in the same order.
+ * No counterpart in the reference (single-GPU backends only).
+ */
+Q3XK_API q3xb_model* q3xb_model_create_tp(const char* path, int rank, int world, char* err, size_t errlen);
+Q3XK_API int q3xb_tp_unique_id(char* id128);
+Q3XK_API q3xb_state* q3xb_state_create_tp(q3xb_model* model, int context_size, const char* id128, char* err,
+                                          size_t errlen);
+/* The rank's share: rank, world, first key/value/query/KV head, first
+ * intermediate row, first vocabulary row, then the local KH, VH, AH, KVH, I, V. */
+Q3XK_API int q3xb_model_shard(const q3xb_model* model, int* fields14);
+/* The same plan for a registered model ID without loading anything. */
+Q3XK_API int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields14, char* err, size_t errlen);
+
 #ifdef __cplusplus
 }  // extern "C"
 #endif

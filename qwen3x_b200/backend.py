@@ -19,18 +19,44 @@ from . import capi
 
 FIELDS = ("id", "V", "H", "I", "N", "AI", "AH", "KVH", "AD", "RD", "KH", "VH", "KD", "VD", "CK",
           "context", "experts", "top_k", "shared_I", "matrix_type", "tied")
+SHARD_FIELDS = ("rank", "world", "kh0", "vh0", "ah0", "kv0", "i0", "v0", "KH", "VH", "AH", "KVH", "I", "V")
+
+
+def tp_plan(model_id: int, rank: int, world: int) -> dict:
+    """This rank's tensor-parallel share of a registered model (no loading)."""
+    f = (ctypes.c_int * 14)()
+    err = ctypes.create_string_buffer(256)
+    st = capi.lib().q3xb_tp_plan(model_id, rank, world, f, err, 256)
+    if st != capi.OK:
+        raise ValueError(err.value.decode())
+    return dict(zip(SHARD_FIELDS, list(f)))
+
+
+def tp_unique_id() -> bytes:
+    """A new NCCL communicator id (rank 0 makes it; every rank passes it to State)."""
+    buf = ctypes.create_string_buffer(128)
+    capi.check(capi.lib().q3xb_tp_unique_id(buf), "q3xb_tp_unique_id")
+    return buf.raw
 
 
 class Model:
-    def __init__(self, path):
+    """q3x_backend::model_create; with world > 1 this rank's tensor-parallel share."""
+
+    def __init__(self, path, rank: int = 0, world: int = 1):
         self.lib = capi.lib()
         err = ctypes.create_string_buffer(256)
-        self.handle = self.lib.q3xb_model_create(str(path).encode(), err, 256)
+        if world == 1:
+            self.handle = self.lib.q3xb_model_create(str(path).encode(), err, 256)
+        else:
+            self.handle = self.lib.q3xb_model_create_tp(str(path).encode(), rank, world, err, 256)
         if not self.handle:
             raise RuntimeError(f"model_create: {err.value.decode()}")
         f = (ctypes.c_int * 21)()
         capi.check(self.lib.q3xb_model_config(self.handle, f), "q3xb_model_config")
         self.config = dict(zip(FIELDS, list(f)))
+        sf = (ctypes.c_int * 14)()
+        capi.check(self.lib.q3xb_model_shard(self.handle, sf), "q3xb_model_shard")
+        self.shard = dict(zip(SHARD_FIELDS, list(sf)))
 
     @property
     def id(self) -> int:
@@ -57,11 +83,19 @@ class Model:
 
 
 class State:
-    def __init__(self, model: Model, context: int):
+    """q3x_backend::state_create; tensor-parallel models need the communicator
+    id from tp_unique_id() (the same bytes on every rank)."""
+
+    def __init__(self, model: Model, context: int, nccl_id: bytes | None = None):
         self.model = model
         self.lib = model.lib
         err = ctypes.create_string_buffer(256)
-        self.handle = self.lib.q3xb_state_create(model.handle, int(context), err, 256)
+        if model.shard["world"] == 1:
+            self.handle = self.lib.q3xb_state_create(model.handle, int(context), err, 256)
+        else:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("a tensor-parallel state needs the 128-byte communicator id")
+            self.handle = self.lib.q3xb_state_create_tp(model.handle, int(context), nccl_id, err, 256)
         if not self.handle:
             raise RuntimeError(f"state_create: {err.value.decode()}")
 

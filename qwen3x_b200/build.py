@@ -25,9 +25,22 @@ INCLUDE = ROOT / "include"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+def _nccl_include():
+    """nccl.h for the types and prototypes of tp.cu (NCCL itself is loaded at run time)."""
+    try:
+        import nvidia.nccl  # the copy torch ships
+
+        inc = Path(list(nvidia.nccl.__path__)[0]) / "include"
+        if (inc / "nccl.h").exists():
+            return [f"-I{inc}"]
+    except ImportError:
+        pass
+    return []
+
+
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-         "-Xptxas", "-warn-spills", f"-I{INCLUDE}", f"-I{CSRC}"]
-LINK = ["-shared", "-lcuda"]
+         "-Xptxas", "-warn-spills", f"-I{INCLUDE}", f"-I{CSRC}", *_nccl_include()]
+LINK = ["-shared", "-lcuda", "-ldl"]
 
 
 def _sources():

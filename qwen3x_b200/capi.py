@@ -125,7 +125,30 @@ _SIGNATURES = {
     "q3xb_state_set_graphs": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "q3xb_state_set_exact_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "q3xb_state_set_prefill_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "q3xb_model_create_tp": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
+                                               ctypes.c_size_t]),
+    "q3xb_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "q3xb_state_create_tp": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p,
+                                               ctypes.c_size_t]),
+    "q3xb_model_shard": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xb_tp_plan": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                    ctypes.c_char_p, ctypes.c_size_t]),
 }
+
+
+def _nccl_hint():
+    """Point the library's run-time NCCL loader at the copy torch ships
+    (used only by tensor-parallel states)."""
+    if os.environ.get("Q3XK_NCCL_LIBRARY"):
+        return
+    try:
+        import nvidia.nccl
+
+        cand = Path(list(nvidia.nccl.__path__)[0]) / "lib" / "libnccl.so.2"
+        if cand.exists():
+            os.environ["Q3XK_NCCL_LIBRARY"] = str(cand)
+    except ImportError:
+        pass
 
 
 def lib():
@@ -137,6 +160,7 @@ def lib():
             raise RuntimeError(
                 f"{path} is missing: build it with `python -m qwen3x_b200.build` "
                 "(the qwen3x_b200 kernels have no CPU fallback)")
+        _nccl_hint()
         handle = ctypes.CDLL(path)
         for name, (res, args) in _SIGNATURES.items():
             fn = getattr(handle, name, None)

@@ -32,6 +32,7 @@
 
 #include "layers.cuh"
 #include "q3x_backend.h"
+#include "tp.cuh"
 
 namespace q3xk {
 namespace {
@@ -116,6 +117,59 @@ struct Layer {
     q3xk_matrix router{};   // MoE: BF16 [experts + 1][H] = router rows + shared gate row
 };
 
+// Tensor-parallel share of one rank (world = 1: everything).  Column-parallel
+// (split output rows): DeltaNet q/k by key head, v/z/a/b by value head,
+// attention q+gate by query head, k/v by KV head (replicated when there are
+// fewer KV heads than ranks), FFN gate/up by intermediate row, lm_head by
+// vocabulary row.  Row-parallel (split input columns, partial sums
+// all-reduced): DeltaNet out, attention out, FFN down.  lc = the rank's dims.
+struct Shard {
+    int rank = 0, world = 1;
+    int kh0 = 0, vh0 = 0, ah0 = 0, kv0 = 0, i0 = 0, v0 = 0;
+    Config lc{};
+};
+
+const char* make_shard(const Config& c, int rank, int world, Shard& sh) {
+    sh = Shard{};
+    sh.rank = rank;
+    sh.world = world;
+    sh.lc = c;
+    if (world < 1 || rank < 0 || rank >= world) return "invalid tensor-parallel rank";
+    if (world == 1) return nullptr;
+    if (c.experts) return "tensor parallelism is not built for MoE models";
+    if (c.KH % world || c.VH % world || c.AH % world || c.V % world || c.I % world || (c.I / world) % 32)
+        return "model shape does not split over the tensor-parallel ranks";
+    const int ahn = c.AH / world, G = c.AH / c.KVH;
+    int kvn = 0;
+    if (c.KVH % world == 0) {
+        kvn = c.KVH / world;
+        sh.kv0 = rank * kvn;
+    } else if (world % c.KVH == 0 && G % ahn == 0) {
+        kvn = 1;  // the rank's query heads share one KV head, replicated on its group of ranks
+        sh.kv0 = rank * ahn / G;
+    } else {
+        return "model shape does not split over the tensor-parallel ranks";
+    }
+    sh.kh0 = rank * (c.KH / world);
+    sh.vh0 = rank * (c.VH / world);
+    sh.ah0 = rank * ahn;
+    sh.i0 = rank * (c.I / world);
+    sh.v0 = rank * (c.V / world);
+    sh.lc.KH = c.KH / world;
+    sh.lc.VH = c.VH / world;
+    sh.lc.AH = ahn;
+    sh.lc.KVH = kvn;
+    sh.lc.I = c.I / world;
+    sh.lc.V = c.V / world;
+    return nullptr;
+}
+
+// Bytes of `cols` packed columns of one model.bin row.
+size_t row_bytes(int type, int cols) {
+    return type == Q3XK_BF16 ? (size_t)cols * 2
+                             : (size_t)cols / kBlock * (type == Q3XK_Q8_0 ? kQ8PackedBytes : kQ4PackedBytes);
+}
+
 }  // namespace
 }  // namespace q3xk
 
@@ -137,6 +191,7 @@ struct Model {
     int P = 0;       // widest in_proj / gate_up (dense) row count
     int mix = 0;     // widest mixer output (DO, AS, I)
     int maxcols = 0; // widest matrix input
+    Shard shard;     // this rank's share (world = 1 unless created for tensor parallelism)
 
     ~Model() {
         if (arena) {
@@ -146,7 +201,7 @@ struct Model {
         if (file) munmap(const_cast<uint8_t*>(file), file_size);
         if (fd >= 0) close(fd);
     }
-    bool load(const char* path, const char** error);
+    bool load(const char* path, int rank, int world, const char** error);
 };
 
 struct State {
@@ -177,6 +232,11 @@ struct State {
     void* gemm_ws = nullptr;
     size_t gemm_ws_bytes = 0;
     int split_len = 0;
+    int rank = 0, world = 1;
+    void* comm = nullptr;          // NCCL communicator (world > 1)
+    float* partial = nullptr;      // row-parallel partial sums [chunk][H] (world > 1)
+    float* full_logits = nullptr;  // gathered logits [V] (world > 1)
+    float* best = nullptr;         // [world][2] (value, index) of each rank's argmax
     bool use_graphs = true;
     bool exact_prefill = false;  // T > 1 through per-token GEMVs instead of the FP16 GEMM
     int chunk = 0;               // tokens per forward pass (work buffers hold `chunk_capacity`)
@@ -191,6 +251,7 @@ struct State {
         if (graph_exec) cudaGraphExecDestroy(graph_exec);
         if (graph) cudaGraphDestroy(graph);
         for (void* p : allocations) cudaFree(p);
+        tp_comm_destroy(comm);
         if (stream) cudaStreamDestroy(stream);
     }
     template <typename T>
@@ -247,6 +308,7 @@ struct Loader {
     cudaStream_t stream = nullptr;
     int status = Q3XK_OK;
     std::vector<float> host;
+    std::vector<uint8_t> gather;
 
     uint8_t* carve(size_t bytes) {
         const size_t at = used;
@@ -341,10 +403,51 @@ struct Loader {
         return d;
     }
 
-    // One walk over the file (engine.cpp:488-557).  Returns the cursor error.
+    // Columns [c0, c0 + cn) of a packed rows x K matrix (row-parallel shard):
+    // gathered row by row on the host, then repacked into dst.
+    void upload_cols(const q3xk_matrix& dst, const uint8_t* src, int rows, int K, int c0, int cn) {
+        if (pass == 0 || status != Q3XK_OK || !src) return;
+        const size_t full = row_bytes(dst.type, K), rb = row_bytes(dst.type, cn), off = row_bytes(dst.type, c0);
+        if ((size_t)rows * rb > staging_bytes) {
+            status = Q3XK_EINVAL;
+            return;
+        }
+        gather.resize((size_t)rows * rb);
+        for (int r = 0; r < rows; ++r) std::memcpy(gather.data() + (size_t)r * rb, src + (size_t)r * full + off, rb);
+        if (cudaMemcpyAsync(staging, gather.data(), gather.size(), cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+            status = Q3XK_ECUDA;
+            return;
+        }
+        const int st = q3xk_repack(&dst, staging, stream);
+        if (st != Q3XK_OK) status = st;
+    }
+    // FP32 device vector of the listed row ranges (each `per` values wide) of
+    // a BF16 file tensor.
+    float* vec_rows(const uint8_t* src, const int (*ranges)[2], int nranges, int per) {
+        int n = 0;
+        for (int i = 0; i < nranges; ++i) n += ranges[i][1] * per;
+        float* d = reinterpret_cast<float*>(carve((size_t)n * 4));
+        if (pass == 0 || status != Q3XK_OK || !src) return d;
+        host.resize(n);
+        int k = 0;
+        for (int i = 0; i < nranges; ++i)
+            for (int r = 0; r < ranges[i][1] * per; ++r) {
+                uint16_t b;
+                std::memcpy(&b, src + 2 * ((size_t)ranges[i][0] * per + r), 2);
+                host[k++] = bf16_to_float(b);
+            }
+        if (cudaMemcpy(d, host.data(), (size_t)n * 4, cudaMemcpyHostToDevice) != cudaSuccess) status = Q3XK_ECUDA;
+        return d;
+    }
+
+    // One walk over the file (engine.cpp:488-557), keeping this rank's share.
+    // Returns the cursor error.
     const char* walk() {
+        const Shard& sh = m.shard;
+        const Config& L = sh.lc;
         const int type = c.matrix_type;
         const int AS = c.AH * c.AD, KVW = c.KVH * c.AD, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO;
+        const int ASl = L.AH * L.AD, KVWl = L.KVH * L.AD, DOl = L.VH * L.VD, DQKVl = 2 * L.KH * L.KD + DOl;
         const int E = c.experts;
         Cursor cur{m.file, m.file_size, kHeaderSize};
         auto packed = [&](int t, int rows, int cols) -> const uint8_t* {
@@ -356,13 +459,17 @@ struct Loader {
             if (pass == 0) need_staging(t, rows, cols);
             return cur.take(b);
         };
+        // row r0 of a packed matrix with `cols` columns (nullptr stays nullptr)
+        auto at_row = [&](const uint8_t* p, int cols, int r0) -> const uint8_t* {
+            return p ? p + (size_t)r0 * row_bytes(type, cols) : nullptr;
+        };
         m.embedding = matrix(type, c.V, c.H, 1);
         upload(m.embedding, packed(type, c.V, c.H), 1);
         if (c.tied) {
-            m.lm_head = m.embedding;
+            m.lm_head = view(m.embedding, 0, sh.v0, L.V);
         } else {
-            m.lm_head = matrix(type, c.V, c.H, 1);
-            upload(m.lm_head, packed(type, c.V, c.H), 1);
+            m.lm_head = matrix(type, L.V, c.H, 1);
+            upload(m.lm_head, at_row(packed(type, c.V, c.H), c.H, sh.v0), 1);
         }
         m.final_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
         m.layer.assign(c.N, Layer{});
@@ -371,26 +478,36 @@ struct Loader {
             l.delta = is_delta(c, i);
             l.in_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
             if (l.delta) {
-                l.in_proj = matrix(type, DQKV + DO + 2 * c.VH, c.H, 1);
-                upload(view(l.in_proj, 0, 0, DQKV), packed(type, DQKV, c.H), 1);
-                upload(view(l.in_proj, 0, DQKV, DO), packed(type, DO, c.H), 1);
-                upload(view(l.in_proj, 0, DQKV + DO, c.VH), packed(type, c.VH, c.H), 1);
-                upload(view(l.in_proj, 0, DQKV + DO + c.VH, c.VH), packed(type, c.VH, c.H), 1);
-                l.conv = vec(cur.take((size_t)DQKV * c.CK * 2), DQKV * c.CK, true, 0.0f);
-                l.alog = vec(cur.take((size_t)c.VH * 4), c.VH, false, 0.0f);
-                l.dt = vec(cur.take((size_t)c.VH * 2), c.VH, true, 0.0f);
+                l.in_proj = matrix(type, DQKVl + DOl + 2 * L.VH, c.H, 1);
+                const uint8_t* qkv = packed(type, DQKV, c.H);
+                upload(view(l.in_proj, 0, 0, L.KH * c.KD), at_row(qkv, c.H, sh.kh0 * c.KD), 1);
+                upload(view(l.in_proj, 0, L.KH * c.KD, L.KH * c.KD), at_row(qkv, c.H, c.KH * c.KD + sh.kh0 * c.KD), 1);
+                upload(view(l.in_proj, 0, 2 * L.KH * c.KD, DOl), at_row(qkv, c.H, 2 * c.KH * c.KD + sh.vh0 * c.VD), 1);
+                upload(view(l.in_proj, 0, DQKVl, DOl), at_row(packed(type, DO, c.H), c.H, sh.vh0 * c.VD), 1);
+                upload(view(l.in_proj, 0, DQKVl + DOl, L.VH), at_row(packed(type, c.VH, c.H), c.H, sh.vh0), 1);
+                upload(view(l.in_proj, 0, DQKVl + DOl + L.VH, L.VH), at_row(packed(type, c.VH, c.H), c.H, sh.vh0),
+                       1);
+                const int ranges[3][2] = {{sh.kh0 * c.KD, L.KH * c.KD},
+                                          {c.KH * c.KD + sh.kh0 * c.KD, L.KH * c.KD},
+                                          {2 * c.KH * c.KD + sh.vh0 * c.VD, DOl}};
+                l.conv = vec_rows(cur.take((size_t)DQKV * c.CK * 2), ranges, 3, c.CK);
+                const uint8_t* alog = cur.take((size_t)c.VH * 4);
+                l.alog = vec(alog ? alog + (size_t)sh.vh0 * 4 : nullptr, L.VH, false, 0.0f);
+                const uint8_t* dt = cur.take((size_t)c.VH * 2);
+                l.dt = vec(dt ? dt + (size_t)sh.vh0 * 2 : nullptr, L.VH, true, 0.0f);
                 l.dnorm = vec(cur.take((size_t)c.VD * 4), c.VD, false, 0.0f);
-                l.out = matrix(type, c.H, DO, 1);
-                upload(l.out, packed(type, c.H, DO), 1);
+                l.out = matrix(type, c.H, DOl, 1);
+                upload_cols(l.out, packed(type, c.H, DO), c.H, DO, sh.vh0 * c.VD, DOl);
             } else {
-                l.in_proj = matrix(type, 2 * AS + 2 * KVW, c.H, 1);
-                upload(view(l.in_proj, 0, 0, 2 * AS), packed(type, 2 * AS, c.H), 1);
-                upload(view(l.in_proj, 0, 2 * AS, KVW), packed(type, KVW, c.H), 1);
-                upload(view(l.in_proj, 0, 2 * AS + KVW, KVW), packed(type, KVW, c.H), 1);
+                l.in_proj = matrix(type, 2 * ASl + 2 * KVWl, c.H, 1);
+                upload(view(l.in_proj, 0, 0, 2 * ASl), at_row(packed(type, 2 * AS, c.H), c.H, sh.ah0 * 2 * c.AD), 1);
+                upload(view(l.in_proj, 0, 2 * ASl, KVWl), at_row(packed(type, KVW, c.H), c.H, sh.kv0 * c.AD), 1);
+                upload(view(l.in_proj, 0, 2 * ASl + KVWl, KVWl), at_row(packed(type, KVW, c.H), c.H, sh.kv0 * c.AD),
+                       1);
                 l.qn1 = vec(cur.take((size_t)c.AD * 2), c.AD, true, 1.0f);
                 l.kn1 = vec(cur.take((size_t)c.AD * 2), c.AD, true, 1.0f);
-                l.out = matrix(type, c.H, AS, 1);
-                upload(l.out, packed(type, c.H, AS), 1);
+                l.out = matrix(type, c.H, ASl, 1);
+                upload_cols(l.out, packed(type, c.H, AS), c.H, AS, sh.ah0 * c.AD, ASl);
             }
             l.post_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
             if (E) {
@@ -405,11 +522,11 @@ struct Loader {
                 upload(view(l.down, E, 0, c.H), packed(type, c.H, c.shared_I), 1);
                 upload(view(l.router, 0, E, 1), packed(Q3XK_BF16, 1, c.H), 1);
             } else {
-                l.gate_up = matrix(type, 2 * c.I, c.H, 1);
-                upload_swiglu(l.gate_up, packed(type, c.I, c.H), c.I, c.I, 0);
-                upload_swiglu(l.gate_up, packed(type, c.I, c.H), c.I, c.I, c.I);
-                l.down = matrix(type, c.H, c.I, 1);
-                upload(l.down, packed(type, c.H, c.I), 1);
+                l.gate_up = matrix(type, 2 * L.I, c.H, 1);
+                upload_swiglu(l.gate_up, at_row(packed(type, c.I, c.H), c.H, sh.i0), L.I, L.I, 0);
+                upload_swiglu(l.gate_up, at_row(packed(type, c.I, c.H), c.H, sh.i0), L.I, L.I, L.I);
+                l.down = matrix(type, c.H, L.I, 1);
+                upload_cols(l.down, packed(type, c.H, c.I), c.H, c.I, sh.i0, L.I);
             }
         }
         if (!cur.error && cur.pos != m.file_size) cur.error = "model.bin size does not match schema";
@@ -423,7 +540,7 @@ struct Loader {
 namespace q3x_backend {
 
 // engine.cpp:480-559: same checks and error strings, then the device upload.
-bool Model::load(const char* path, const char** error) {
+bool Model::load(const char* path, int rank, int world, const char** error) {
     auto fail = [&](const char* message) {
         *error = message;
         return false;
@@ -441,6 +558,7 @@ bool Model::load(const char* path, const char** error) {
     if (!config) return fail("unsupported Qwen model ID");
     if (!header_matches(file, *config)) return fail("Qwen model.bin header mismatch");
     const Config& c = *config;
+    if (const char* e = make_shard(c, rank, world, shard)) return fail(e);
     if (c.experts && c.shared_I != c.I) return fail("unsupported MoE shape (shared_I != I)");
     if (c.experts && (c.experts > 512 || c.top_k > 8)) return fail("unsupported MoE shape");
 
@@ -467,13 +585,14 @@ bool Model::load(const char* path, const char** error) {
     if (e) return fail(e);
     if (ld.status != Q3XK_OK || se != cudaSuccess) return fail("model upload to the device failed");
 
-    const int AS = c.AH * c.AD, KVW = c.KVH * c.AD, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO;
-    P = DQKV + DO + 2 * c.VH;
+    const Config& L = shard.lc;
+    const int AS = L.AH * L.AD, KVW = L.KVH * L.AD, DO = L.VH * L.VD, DQKV = 2 * L.KH * L.KD + DO;
+    P = DQKV + DO + 2 * L.VH;
     if (2 * AS + 2 * KVW > P) P = 2 * AS + 2 * KVW;
-    if (!c.experts && 2 * c.I > P) P = 2 * c.I;
+    if (!L.experts && 2 * L.I > P) P = 2 * L.I;
     mix = DO > AS ? DO : AS;
-    if (c.I > mix) mix = c.I;
-    maxcols = c.H > mix ? c.H : mix;
+    if (L.I > mix) mix = L.I;
+    maxcols = L.H > mix ? L.H : mix;
     return true;
 }
 
@@ -549,8 +668,16 @@ int moe_token(State& s, const Config& c, const Layer& l, int t) {
 // One decode token (T = 1): every elementwise step that feeds a GEMV is
 // fused into that GEMV's staging of x (RMSNorm, DeltaNet gated RMS, SwiGLU);
 // residual adds are the GEMVs' accumulate.
+// out = W x for a row-parallel projection: y += W x on one GPU; with
+// tensor parallelism the rank's partial sum is all-reduced into y.
+int row_parallel(State& s, const q3xk_matrix& w, const float* x, int T, float* y) {
+    if (s.world == 1) return mm(s, w, x, T, y, 1);
+    Q3XB_TRY(mm(s, w, x, T, s.partial, 0));
+    return tp_allreduce_add(s.comm, s.partial, y, (int64_t)T * w.rows, s.stream);
+}
+
 int forward_token(Model& m, State& s, bool logits) {
-    const Config& c = *m.config;
+    const Config& c = m.shard.lc;
     const cudaStream_t st = s.stream;
     const int DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO, AS = c.AH * c.AD;
     Q3XB_TRY(launch_embed(m.embedding, s.tokens, 1, s.hidden, st));
@@ -578,13 +705,16 @@ int forward_token(Model& m, State& s, bool logits) {
                 xg.w = l.dnorm;
                 xg.z = s.proj + DQKV;
             }
-            Q3XB_TRY(q3xk_gemv_ex(&l.out, s.mix, s.hidden, 1, &xg, st));
+            if (s.world == 1 || xg.kind != Q3XK_XFORM_NONE)
+                Q3XB_TRY(q3xk_gemv_ex(&l.out, s.mix, s.hidden, 1, &xg, st));
+            else
+                Q3XB_TRY(row_parallel(s, l.out, s.mix, 1, s.hidden));
             ++di;
         } else {
             const AttnDims ad{c.AH, c.KVH, c.AD, c.RD};
             Q3XB_TRY(launch_attention(s.proj, P, 1, ad, l.qn1, l.kn1, s.pos, s.kcache[ai], s.vcache[ai], s.capacity,
                                       s.part, s.split_len, s.mix, AS, st));
-            Q3XB_TRY(q3xk_gemv(&l.out, s.mix, s.hidden, 1, st));
+            Q3XB_TRY(row_parallel(s, l.out, s.mix, 1, s.hidden));
             ++ai;
         }
         if (c.experts) {
@@ -594,7 +724,7 @@ int forward_token(Model& m, State& s, bool logits) {
             const float* pin = nullptr;
             Q3XB_TRY(rms_input(s, s.hidden, l.post_norm, c.H, &xpost, &pin));
             Q3XB_TRY(gemv_swiglu(&l.gate_up, pin, s.mix, nullptr, 0, nullptr, &xpost, st));
-            Q3XB_TRY(q3xk_gemv(&l.down, s.mix, s.hidden, 1, st));
+            Q3XB_TRY(row_parallel(s, l.down, s.mix, 1, s.hidden));
         }
     }
     if (logits) {
@@ -613,7 +743,7 @@ int forward_token(Model& m, State& s, bool logits) {
 
 int forward_chunk(Model& m, State& s, int T, bool logits) {
     if (Q3XB_FUSED_DECODE && T == 1 && !s.exact_prefill) return forward_token(m, s, logits);
-    const Config& c = *m.config;
+    const Config& c = m.shard.lc;
     const cudaStream_t st = s.stream;
     const int H = c.H, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO, AS = c.AH * c.AD;
     Q3XB_TRY(launch_embed(m.embedding, s.tokens, T, s.hidden, st));
@@ -634,13 +764,13 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
                 Q3XB_TRY(launch_delta_chunked(s.proj, P, s.proj, P, T, dd, l.alog, l.dt, l.dnorm, s.memory[di],
                                               s.mix, DO, s.delta_work, st));
             }
-            Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
+            Q3XB_TRY(row_parallel(s, l.out, s.mix, T, s.hidden));
             ++di;
         } else {
             const AttnDims ad{c.AH, c.KVH, c.AD, c.RD};
             Q3XB_TRY(launch_attention(s.proj, P, T, ad, l.qn1, l.kn1, s.pos, s.kcache[ai], s.vcache[ai], s.capacity,
                                       s.part, s.split_len, s.mix, AS, st));
-            Q3XB_TRY(mm(s, l.out, s.mix, T, s.hidden, 1));
+            Q3XB_TRY(row_parallel(s, l.out, s.mix, T, s.hidden));
             ++ai;
         }
         if (c.experts && !s.exact_prefill) {
@@ -662,7 +792,7 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
             Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
             Q3XB_TRY(mm(s, l.gate_up, s.normed, T, s.proj, 0));
             Q3XB_TRY(launch_ffn_swiglu(s.proj, 2 * c.I, T, c.I, s.mix, st));
-            Q3XB_TRY(mm(s, l.down, s.mix, T, s.hidden, 1));
+            Q3XB_TRY(row_parallel(s, l.down, s.mix, T, s.hidden));
         }
     }
     if (logits) {
@@ -699,7 +829,7 @@ void set_error(char* err, size_t errlen, const char* fmt, ...) {
     va_end(ap);
 }
 
-State* create_state(Model* model, int context, char* err, size_t errlen) {
+State* create_state(Model* model, int context, const char* nccl_id, char* err, size_t errlen) {
     if (!model || !model->config || context <= 0 || context > kMaxContext) {
         set_error(err, errlen, "state_create model=%p context=%d", static_cast<void*>(model), context);
         return nullptr;
@@ -710,11 +840,13 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
     }
     std::unique_ptr<State> s(new (std::nothrow) State());
     if (!s) return nullptr;
-    const Config& c = *model->config;
+    const Config& c = model->shard.lc;  // this rank's dims
     s->model = model;
     s->c = &c;
     s->device = model->device;
     s->capacity = context;
+    s->rank = model->shard.rank;
+    s->world = model->shard.world;
     if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
         set_error(err, errlen, "cannot create a CUDA stream");
         return nullptr;
@@ -752,6 +884,9 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
              s->alloc(&a.scale_g, P) && s->alloc(&a.gu, P * 2 * c.I) && s->alloc(&a.h16, P * c.I) &&
              s->alloc(&a.scale_h, P) && s->alloc(&a.out, P * c.H);
     }
+    if (ok && s->world > 1)
+        ok = s->alloc(&s->partial, (size_t)chunk * c.H) && s->alloc(&s->full_logits, model->config->V) &&
+             s->alloc(&s->best, 2 * (size_t)s->world + 2);
     if (ok && chunk > 1 && delta_layers > 0)
         ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4) &&
              s->alloc(&s->qkv, (size_t)chunk * DQKV);
@@ -770,6 +905,20 @@ State* create_state(Model* model, int context, char* err, size_t errlen) {
     if (!ok) {
         set_error(err, errlen, "State allocation failed model=%s context=%d", c.name, context);
         return nullptr;
+    }
+    if (s->world > 1) {
+        if (!nccl_id) {
+            set_error(err, errlen, "tensor-parallel state needs a communicator id");
+            return nullptr;
+        }
+        if (const char* why = nccl_load()) {
+            set_error(err, errlen, "%s", why);
+            return nullptr;
+        }
+        if (tp_comm_create(nccl_id, s->rank, s->world, &s->comm) != Q3XK_OK) {
+            set_error(err, errlen, "NCCL communicator creation failed");
+            return nullptr;
+        }
     }
     float* r = s->recurrent;
     float* kv = s->kv;
@@ -862,6 +1011,21 @@ int argmax_impl(const State* s, int* token) {
     if (!s || !token) return Q3XK_EINVAL;
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
     Q3XB_TRY(q3xk_argmax(s->logits, s->c->V, s->argmax_out, s->argmax_ws, s->argmax_ws_bytes, s->stream));
+    if (s->world > 1) {
+        // every rank's (value, global index), gathered; the first maximum wins
+        float* mine = s->best + 2 * s->world;
+        Q3XB_TRY(tp_pack_best(s->logits, s->argmax_out, s->model->shard.v0, mine, s->stream));
+        Q3XB_TRY(tp_allgather(s->comm, mine, s->best, 2, s->stream));
+        std::vector<float> all(2 * (size_t)s->world);
+        if (cudaMemcpyAsync(all.data(), s->best, all.size() * 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
+            cudaStreamSynchronize(s->stream) != cudaSuccess)
+            return Q3XK_ECUDA;
+        int bi = 0;
+        for (int r = 1; r < s->world; ++r)
+            if (all[2 * r] > all[2 * bi] || (all[2 * r] == all[2 * bi] && all[2 * r + 1] < all[2 * bi + 1])) bi = r;
+        *token = (int)all[2 * bi + 1];
+        return Q3XK_OK;
+    }
     if (cudaMemcpyAsync(token, s->argmax_out, 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess)
         return Q3XK_ECUDA;
@@ -871,6 +1035,14 @@ int argmax_impl(const State* s, int* token) {
 int copy_logits_impl(const State* s, float* out) {
     if (!s || !out) return Q3XK_EINVAL;
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    if (s->world > 1) {  // vocabulary shards in rank order
+        Q3XB_TRY(tp_allgather(s->comm, s->logits, s->full_logits, s->c->V, s->stream));
+        if (cudaMemcpyAsync(out, s->full_logits, (size_t)s->c->V * s->world * 4, cudaMemcpyDeviceToHost,
+                            s->stream) != cudaSuccess ||
+            cudaStreamSynchronize(s->stream) != cudaSuccess)
+            return Q3XK_ECUDA;
+        return Q3XK_OK;
+    }
     if (cudaMemcpyAsync(out, s->logits, (size_t)s->c->V * 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess)
         return Q3XK_ECUDA;
@@ -890,21 +1062,22 @@ int copy_logits_impl(const State* s, float* out) {
 
 namespace q3x_backend {
 
-Model* model_create(const char* path, char* err, size_t errlen) {
+Model* model_create_shard(const char* path, int rank, int world, char* err, size_t errlen) {
     std::unique_ptr<Model> model(new (std::nothrow) Model());
     const char* message = nullptr;
-    if (!model || !path || !model->load(path, &message)) {
+    if (!model || !path || !model->load(path, rank, world, &message)) {
         if (err && errlen) std::snprintf(err, errlen, "%s", message ? message : "allocation failed");
         return nullptr;
     }
     if (err && errlen) err[0] = '\0';
     return model.release();
 }
+Model* model_create(const char* path, char* err, size_t errlen) { return model_create_shard(path, 0, 1, err, errlen); }
 void model_destroy(Model* model) { delete model; }
 
 State* state_create(Model* model, int context_size) {
     char err[256];
-    State* s = create_state(model, context_size, err, sizeof err);
+    State* s = create_state(model, context_size, nullptr, err, sizeof err);
     if (!s) {
         std::fprintf(stderr, "q3x_backend: %s\n", err);
         std::abort();
@@ -970,7 +1143,41 @@ size_t q3xb_model_device_bytes(const q3xb_model* model) {
     return model ? reinterpret_cast<const Model*>(model)->arena_bytes : 0;
 }
 q3xb_state* q3xb_state_create(q3xb_model* model, int context_size, char* err, size_t errlen) {
-    return reinterpret_cast<q3xb_state*>(create_state(reinterpret_cast<Model*>(model), context_size, err, errlen));
+    return reinterpret_cast<q3xb_state*>(
+        create_state(reinterpret_cast<Model*>(model), context_size, nullptr, err, errlen));
+}
+q3xb_model* q3xb_model_create_tp(const char* path, int rank, int world, char* err, size_t errlen) {
+    return reinterpret_cast<q3xb_model*>(q3x_backend::model_create_shard(path, rank, world, err, errlen));
+}
+int q3xb_tp_unique_id(char* id) { return tp_unique_id(id); }
+q3xb_state* q3xb_state_create_tp(q3xb_model* model, int context_size, const char* nccl_id, char* err,
+                                 size_t errlen) {
+    return reinterpret_cast<q3xb_state*>(
+        create_state(reinterpret_cast<Model*>(model), context_size, nccl_id, err, errlen));
+}
+static void shard_fields(const Shard& sh, int* f) {
+    const int v[14] = {sh.rank, sh.world, sh.kh0,     sh.vh0,    sh.ah0,    sh.kv0,   sh.i0,
+                       sh.v0,   sh.lc.KH, sh.lc.VH, sh.lc.AH, sh.lc.KVH, sh.lc.I, sh.lc.V};
+    std::memcpy(f, v, sizeof v);
+}
+int q3xb_model_shard(const q3xb_model* model, int* fields14) {
+    if (!model || !fields14) return Q3XK_EINVAL;
+    shard_fields(reinterpret_cast<const Model*>(model)->shard, fields14);
+    return Q3XK_OK;
+}
+int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields14, char* err, size_t errlen) {
+    const Config* c = config_for_id(model_id);
+    if (!c || !fields14) {
+        set_error(err, errlen, "unsupported Qwen model ID");
+        return Q3XK_EINVAL;
+    }
+    Shard sh;
+    if (const char* e = make_shard(*c, rank, world, sh)) {
+        set_error(err, errlen, "%s", e);
+        return Q3XK_EUNSUPPORTED;
+    }
+    shard_fields(sh, fields14);
+    return Q3XK_OK;
 }
 void q3xb_state_destroy(q3xb_state* state) { delete reinterpret_cast<State*>(state); }
 int q3xb_state_reset(q3xb_state* state) { return reset_impl(reinterpret_cast<State*>(state)); }

@@ -1,0 +1,119 @@
+// tp.cu -- NCCL, loaded at run time, for the tensor-parallel backend.
+//
+// Row-parallel projections (attention/DeltaNet out, FFN down) leave a partial
+// [T][H] sum on every rank; tp_allreduce_add sums the partials with one
+// ncclAllReduce on the state's stream (capturable in the decode graph) and
+// adds the result into the replicated residual stream.
+#include <dlfcn.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include <nccl.h>
+
+#include "tp.cuh"
+
+namespace q3xk {
+namespace {
+
+struct NcclApi {
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+};
+
+NcclApi g_nccl;
+std::mutex g_nccl_mutex;
+const char* g_nccl_error = nullptr;
+bool g_nccl_tried = false;
+
+__global__ void add_kernel(float* __restrict__ hidden, const float* __restrict__ partial, int64_t n) {
+    griddep_wait();
+    griddep_launch_dependents();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        hidden[i] += partial[i];
+}
+
+__global__ void pack_best_kernel(const float* __restrict__ logits, const int* __restrict__ idx, int v0,
+                                 float* __restrict__ out) {
+    griddep_wait();
+    const int i = *idx;
+    out[0] = logits[i];
+    out[1] = (float)(i + v0);  // exact: vocabulary indices < 2^24
+}
+
+}  // namespace
+
+int tp_pack_best(const float* logits, const int* idx, int v0, float* out2, cudaStream_t s) {
+    if (launch_pdl(pack_best_kernel, dim3(1), dim3(1), 0, s, logits, idx, v0, out2) != cudaSuccess) return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+const char* nccl_load() {
+    std::lock_guard<std::mutex> lock(g_nccl_mutex);
+    if (g_nccl_tried) return g_nccl_error;
+    g_nccl_tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the copy torch loaded, if any
+    if (!h) {
+        const char* path = std::getenv("Q3XK_NCCL_LIBRARY");
+        h = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    }
+    if (!h) return g_nccl_error = "libnccl.so.2 not found (set Q3XK_NCCL_LIBRARY)";
+    g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
+    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.comm_destroy || !g_nccl.all_reduce ||
+        !g_nccl.all_gather)
+        return g_nccl_error = "libnccl.so.2 lacks a needed symbol";
+    return nullptr;
+}
+
+int tp_unique_id(char id[kNcclIdBytes]) {
+    static_assert(sizeof(ncclUniqueId) == kNcclIdBytes, "NCCL id size");
+    if (!id) return Q3XK_EINVAL;
+    if (nccl_load()) return Q3XK_EUNSUPPORTED;
+    ncclUniqueId u;
+    if (g_nccl.get_unique_id(&u) != ncclSuccess) return Q3XK_ECUDA;
+    std::memcpy(id, &u, sizeof u);
+    return Q3XK_OK;
+}
+
+int tp_comm_create(const char id[kNcclIdBytes], int rank, int world, void** comm) {
+    if (!id || !comm || world < 1 || rank < 0 || rank >= world) return Q3XK_EINVAL;
+    if (nccl_load()) return Q3XK_EUNSUPPORTED;
+    ncclUniqueId u;
+    std::memcpy(&u, id, sizeof u);
+    ncclComm_t c = nullptr;
+    if (g_nccl.comm_init_rank(&c, world, u, rank) != ncclSuccess) return Q3XK_ECUDA;
+    *comm = c;
+    return Q3XK_OK;
+}
+
+void tp_comm_destroy(void* comm) {
+    if (comm && !nccl_load()) g_nccl.comm_destroy(static_cast<ncclComm_t>(comm));
+}
+
+int tp_allreduce_add(void* comm, float* partial, float* hidden, int64_t n, cudaStream_t s) {
+    if (g_nccl.all_reduce(partial, partial, (size_t)n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(comm), s) !=
+        ncclSuccess)
+        return Q3XK_ECUDA;
+    const int blocks = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+    if (launch_pdl(add_kernel, dim3(blocks), dim3(256), 0, s, hidden, (const float*)partial, n) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
+int tp_allgather(void* comm, const float* in, float* out, int64_t n, cudaStream_t s) {
+    if (g_nccl.all_gather(in, out, (size_t)n, ncclFloat32, static_cast<ncclComm_t>(comm), s) != ncclSuccess)
+        return Q3XK_ECUDA;
+    return Q3XK_OK;
+}
+
+}  // namespace q3xk

@@ -1,0 +1,28 @@
+// tp.cuh -- tensor parallelism across GPUs: the NCCL calls the backend makes.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2: the copy torch already
+// loaded, or the path in Q3XK_NCCL_LIBRARY), so libq3xk.so itself does not
+// depend on it and single-GPU use never touches it.
+#pragma once
+
+#include "common.cuh"
+
+namespace q3xk {
+
+constexpr int kNcclIdBytes = 128;
+
+// The NCCL library (nullptr with a reason if it cannot be loaded).
+const char* nccl_load();
+// A new communicator id (rank 0 creates it, every rank receives the bytes).
+int tp_unique_id(char id[kNcclIdBytes]);
+// Communicator of `world` ranks (collective: every rank calls it).
+int tp_comm_create(const char id[kNcclIdBytes], int rank, int world, void** comm);
+void tp_comm_destroy(void* comm);
+// hidden[0..n) += allreduce_sum(partial[0..n)) (partial is overwritten).
+int tp_allreduce_add(void* comm, float* partial, float* hidden, int64_t n, cudaStream_t s);
+// out2 = {logits[*idx], *idx + v0} (a rank's argmax in global numbering).
+int tp_pack_best(const float* logits, const int* idx, int v0, float* out2, cudaStream_t s);
+// out[world * n] = concatenation of every rank's in[n] (floats).
+int tp_allgather(void* comm, const float* in, float* out, int64_t n, cudaStream_t s);
+
+}  // namespace q3xk

@@ -1,0 +1,97 @@
+"""Tensor-parallel backend on 2 GPUs (one process per GPU, NCCL): the same
+logits and greedy tokens as the single-GPU backend on a seeded test model.
+Needs 2 GPUs; on a 1-GPU box it is skipped (the host-side logic is covered by
+tests/test_tp.py on CPU)."""
+import os
+
+import numpy as np
+import pytest
+
+from qwen3x_b200 import modelfile
+
+pytestmark = pytest.mark.gpu
+
+MID = 9091
+TOL = 1e-4  # partial sums of the row-parallel projections are added in another order
+
+
+def _tp_rank(rank, world, port, path, out, prompt, steps):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from qwen3x_b200.backend import Model, State, tp_unique_id
+
+    ids = [tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    model = Model(path, rank, world)
+    res = {}
+    for mode in ("decode", "prefill"):
+        st = State(model, 256, ids[0])
+        if mode == "decode":
+            for t in prompt:
+                st.forward([int(t)])
+        else:
+            st.forward(prompt)
+        res[mode + "_logits"] = st.logits()
+        toks = []
+        for _ in range(steps):
+            toks.append(st.argmax())
+            st.forward([toks[-1]])
+        res[mode + "_tokens"] = np.array(toks)
+        res[mode + "_final"] = st.logits()
+        st.close()
+    model.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        np.savez(out, **res)
+
+
+def test_tp2_matches_single_gpu(cuda, tmp_path):
+    import multiprocessing as mp
+    import socket
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs 2 GPUs (host-side logic: tests/test_tp.py)")
+    path = modelfile.write_model(tmp_path / "m.bin", modelfile.CONFIGS[MID], seed=5)
+    prompt = np.random.default_rng(8).integers(0, modelfile.CONFIGS[MID].V, 40).astype(np.int32)
+    steps = 24
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    out = tmp_path / "tp.npz"
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, port, str(path), str(out), prompt, steps)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    tp = np.load(out)
+
+    from qwen3x_b200.backend import Model, State
+
+    model = Model(path)
+    for mode in ("decode", "prefill"):
+        st = State(model, 256)
+        if mode == "decode":
+            for t in prompt:
+                st.forward([int(t)])
+        else:
+            st.forward(prompt)
+        ref = st.logits()
+        scale = max(1.0, float(np.abs(ref).max()))
+        assert float(np.abs(tp[mode + "_logits"] - ref).max()) <= TOL * scale, mode
+        toks = []
+        for _ in range(steps):
+            toks.append(st.argmax())
+            st.forward([toks[-1]])
+        assert toks == list(tp[mode + "_tokens"]), mode
+        ref = st.logits()
+        assert float(np.abs(tp[mode + "_final"] - ref).max()) <= TOL * max(1.0, float(np.abs(ref).max())), mode
+        st.close()
