@@ -149,6 +149,7 @@ def dist_setup(n_gpus: int):
     if world > 1:
         import datetime
 
+        os.environ.setdefault("NCCL_SOCKET_IFNAME", "lo")  # one node: bootstrap over loopback
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))

@@ -102,7 +102,8 @@ Q3XK_API int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens);
  * lm_head rows; row-parallel out/down columns, partial sums all-reduced with
  * NCCL) and owns a State whose collectives run on the state's stream.  Rank 0
  * makes a communicator id with q3xb_tp_unique_id and every rank passes the
- * same 128 bytes to q3xb_state_create_tp.  state_forward, state_argmax and
+ * same 128 bytes to q3xb_state_create_tp; an id bootstraps one communicator,
+ * so every State needs a fresh one.  state_forward, state_argmax and
  * state_copy_logits are collective: every rank calls them in the same order.
  * No counterpart in the reference (single-GPU backends only).
  */

@@ -916,7 +916,7 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
             return nullptr;
         }
         if (tp_comm_create(nccl_id, s->rank, s->world, &s->comm) != Q3XK_OK) {
-            set_error(err, errlen, "NCCL communicator creation failed");
+            set_error(err, errlen, "NCCL communicator creation failed (%s)", tp_last_error());
             return nullptr;
         }
     }

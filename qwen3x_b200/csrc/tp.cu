@@ -6,6 +6,7 @@
 // adds the result into the replicated residual stream.
 #include <dlfcn.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -23,7 +24,9 @@ struct NcclApi {
     decltype(&ncclCommDestroy) comm_destroy = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
     decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
 };
+char g_last_error[160] = "";
 
 NcclApi g_nccl;
 std::mutex g_nccl_mutex;
@@ -68,6 +71,7 @@ const char* nccl_load() {
     g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(h, "ncclAllReduce"));
     g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
+    g_nccl.error_string = reinterpret_cast<decltype(g_nccl.error_string)>(dlsym(h, "ncclGetErrorString"));
     if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.comm_destroy || !g_nccl.all_reduce ||
         !g_nccl.all_gather)
         return g_nccl_error = "libnccl.so.2 lacks a needed symbol";
@@ -90,10 +94,17 @@ int tp_comm_create(const char id[kNcclIdBytes], int rank, int world, void** comm
     ncclUniqueId u;
     std::memcpy(&u, id, sizeof u);
     ncclComm_t c = nullptr;
-    if (g_nccl.comm_init_rank(&c, world, u, rank) != ncclSuccess) return Q3XK_ECUDA;
+    const ncclResult_t r = g_nccl.comm_init_rank(&c, world, u, rank);
+    if (r != ncclSuccess) {
+        std::snprintf(g_last_error, sizeof g_last_error, "ncclCommInitRank: %s",
+                      g_nccl.error_string ? g_nccl.error_string(r) : "error");
+        return Q3XK_ECUDA;
+    }
     *comm = c;
     return Q3XK_OK;
 }
+
+const char* tp_last_error() { return g_last_error; }
 
 void tp_comm_destroy(void* comm) {
     if (comm && !nccl_load()) g_nccl.comm_destroy(static_cast<ncclComm_t>(comm));

@@ -18,6 +18,8 @@ int tp_unique_id(char id[kNcclIdBytes]);
 // Communicator of `world` ranks (collective: every rank calls it).
 int tp_comm_create(const char id[kNcclIdBytes], int rank, int world, void** comm);
 void tp_comm_destroy(void* comm);
+// Message of the last failed NCCL call.
+const char* tp_last_error();
 // hidden[0..n) += allreduce_sum(partial[0..n)) (partial is overwritten).
 int tp_allreduce_add(void* comm, float* partial, float* hidden, int64_t n, cudaStream_t s);
 // out2 = {logits[*idx], *idx + v0} (a rank's argmax in global numbering).

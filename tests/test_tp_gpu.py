@@ -12,11 +12,15 @@ from qwen3x_b200 import modelfile
 pytestmark = pytest.mark.gpu
 
 MID = 9091
-TOL = 1e-4  # partial sums of the row-parallel projections are added in another order
+# decode (GEMV path): partial sums of the row-parallel projections are added in
+# another order; prompt (FP16 dequant-GEMM): a rank's K slice gets its own
+# per-token FP16 scale, so rounding differs within the GEMM bar
+TOL = {"decode": 1e-4, "prefill": 5e-3}
 
 
 def _tp_rank(rank, world, port, path, out, prompt, steps):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    # one node: NCCL's bootstrap over loopback
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", NCCL_SOCKET_IFNAME="lo")
     import torch
     import torch.distributed as dist
 
@@ -24,12 +28,13 @@ def _tp_rank(rank, world, port, path, out, prompt, steps):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from qwen3x_b200.backend import Model, State, tp_unique_id
 
-    ids = [tp_unique_id() if rank == 0 else None]
+    # one communicator per state: a fresh id for each (an id bootstraps one communicator)
+    ids = [(tp_unique_id(), tp_unique_id()) if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0)
     model = Model(path, rank, world)
     res = {}
-    for mode in ("decode", "prefill"):
-        st = State(model, 256, ids[0])
+    for k, mode in enumerate(("decode", "prefill")):
+        st = State(model, 256, ids[0][k])
         if mode == "decode":
             for t in prompt:
                 st.forward([int(t)])
@@ -86,12 +91,12 @@ def test_tp2_matches_single_gpu(cuda, tmp_path):
             st.forward(prompt)
         ref = st.logits()
         scale = max(1.0, float(np.abs(ref).max()))
-        assert float(np.abs(tp[mode + "_logits"] - ref).max()) <= TOL * scale, mode
+        assert float(np.abs(tp[mode + "_logits"] - ref).max()) <= TOL[mode] * scale, mode
         toks = []
         for _ in range(steps):
             toks.append(st.argmax())
             st.forward([toks[-1]])
         assert toks == list(tp[mode + "_tokens"]), mode
         ref = st.logits()
-        assert float(np.abs(tp[mode + "_final"] - ref).max()) <= TOL * max(1.0, float(np.abs(ref).max())), mode
+        assert float(np.abs(tp[mode + "_final"] - ref).max()) <= TOL[mode] * max(1.0, float(np.abs(ref).max())), mode
         st.close()
