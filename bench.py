@@ -399,7 +399,13 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
             ids = [tp_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(ids, src=0)
             nccl_id = ids[0]
-        st = State(model, prompt_len + decode_steps + 72, nccl_id)
+        exchange = None
+        if dist:
+            def exchange(handle):  # IPC handles of the peer all-reduce buffers, in rank order
+                out_h = [None] * world
+                dist.all_gather_object(out_h, handle)
+                return out_h
+        st = State(model, prompt_len + decode_steps + 72, nccl_id, exchange=exchange)
         stream = torch.cuda.ExternalStream(st.stream)
         prompt = np.random.default_rng(11).integers(0, c.V, prompt_len).astype(np.int32)
         for _ in range(3):  # warm-up: a short prompt and a few decode steps (captures the graph)
@@ -453,6 +459,9 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
             "clocks": clk.summary(),
             "first_tokens": tokens[:8],
         })
+        if dist:
+            out["tp_error"] = st.tp_error()
+            dist.barrier()
         st.close()
         model.close()
         if cpu_sample and rank == 0:

@@ -111,6 +111,14 @@ Q3XK_API q3xb_model* q3xb_model_create_tp(const char* path, int rank, int world,
 Q3XK_API int q3xb_tp_unique_id(char* id128);
 Q3XK_API q3xb_state* q3xb_state_create_tp(q3xb_model* model, int context_size, const char* id128, char* err,
                                           size_t errlen);
+/* Decode all-reduces over NVLink peer memory instead of NCCL (one kernel, one
+ * round of flags): every rank exports its buffer (64-byte CUDA IPC handle),
+ * the handles are exchanged in rank order, and every rank opens the others'.
+ * Without this step the state uses NCCL for every all-reduce. */
+Q3XK_API int q3xb_state_ipc_handle(const q3xb_state* state, char* handle64);
+Q3XK_API int q3xb_state_ipc_open(q3xb_state* state, const char* handles_world_x_64);
+/* 1 if a peer all-reduce gave up waiting for a peer (~1 s), else 0. */
+Q3XK_API int q3xb_state_tp_error(const q3xb_state* state, int* flags);
 /* The rank's share: rank, world, first key/value/query/KV head, first
  * intermediate row, first vocabulary row, then the local KH, VH, AH, KVH, I, V. */
 Q3XK_API int q3xb_model_shard(const q3xb_model* model, int* fields14);

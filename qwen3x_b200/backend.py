@@ -86,7 +86,7 @@ class State:
     """q3x_backend::state_create; tensor-parallel models need the communicator
     id from tp_unique_id() (the same bytes on every rank)."""
 
-    def __init__(self, model: Model, context: int, nccl_id: bytes | None = None):
+    def __init__(self, model: Model, context: int, nccl_id: bytes | None = None, exchange=None):
         self.model = model
         self.lib = model.lib
         err = ctypes.create_string_buffer(256)
@@ -98,6 +98,17 @@ class State:
             self.handle = self.lib.q3xb_state_create_tp(model.handle, int(context), nccl_id, err, 256)
         if not self.handle:
             raise RuntimeError(f"state_create: {err.value.decode()}")
+        if model.shard["world"] > 1 and exchange is not None:
+            # decode all-reduces over peer memory: exchange the IPC handles in rank order
+            h = ctypes.create_string_buffer(64)
+            capi.check(self.lib.q3xb_state_ipc_handle(self.handle, h), "q3xb_state_ipc_handle")
+            handles = exchange(h.raw)
+            capi.check(self.lib.q3xb_state_ipc_open(self.handle, b"".join(handles)), "q3xb_state_ipc_open")
+
+    def tp_error(self) -> int:
+        out = ctypes.c_int(0)
+        capi.check(self.lib.q3xb_state_tp_error(self.handle, ctypes.byref(out)), "q3xb_state_tp_error")
+        return out.value
 
     def forward(self, tokens, compute_logits: bool = True):
         t = np.ascontiguousarray(np.atleast_1d(tokens), dtype=np.int32)

@@ -131,6 +131,9 @@ _SIGNATURES = {
     "q3xb_state_create_tp": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_char_p,
                                                ctypes.c_size_t]),
     "q3xb_model_shard": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "q3xb_state_ipc_handle": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
+    "q3xb_state_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
+    "q3xb_state_tp_error": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "q3xb_tp_plan": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                     ctypes.c_char_p, ctypes.c_size_t]),
 }

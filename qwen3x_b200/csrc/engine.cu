@@ -237,6 +237,11 @@ struct State {
     float* partial = nullptr;      // row-parallel partial sums [chunk][H] (world > 1)
     float* full_logits = nullptr;  // gathered logits [V] (world > 1)
     float* best = nullptr;         // [world][2] (value, index) of each rank's argmax
+    void* peer_buf = nullptr;      // own one-shot all-reduce buffer (CUDA IPC exported)
+    void* peer_bases[8] = {};      // every rank's buffer, mapped (own one included)
+    bool peer_ready = false;       // decode all-reduces go over peer memory
+    int* peer_seq = nullptr;       // call counter of the peer all-reduce
+    int* tp_err = nullptr;         // set by a peer all-reduce that gave up waiting
     bool use_graphs = true;
     bool exact_prefill = false;  // T > 1 through per-token GEMVs instead of the FP16 GEMM
     int chunk = 0;               // tokens per forward pass (work buffers hold `chunk_capacity`)
@@ -250,6 +255,8 @@ struct State {
         if (stream) cudaStreamSynchronize(stream);
         if (graph_exec) cudaGraphExecDestroy(graph_exec);
         if (graph) cudaGraphDestroy(graph);
+        for (int r = 0; r < world && r < 8; ++r)
+            if (peer_ready && r != rank && peer_bases[r]) cudaIpcCloseMemHandle(peer_bases[r]);
         for (void* p : allocations) cudaFree(p);
         tp_comm_destroy(comm);
         if (stream) cudaStreamDestroy(stream);
@@ -673,6 +680,9 @@ int moe_token(State& s, const Config& c, const Layer& l, int t) {
 int row_parallel(State& s, const q3xk_matrix& w, const float* x, int T, float* y) {
     if (s.world == 1) return mm(s, w, x, T, y, 1);
     Q3XB_TRY(mm(s, w, x, T, s.partial, 0));
+    if (T == 1 && s.peer_ready)  // decode: one-shot all-reduce over NVLink peer memory
+        return tp_peer_allreduce_add(s.peer_bases, s.rank, s.world, s.c->H, s.peer_seq, s.partial, y, w.rows,
+                                     s.tp_err, s.stream);
     return tp_allreduce_add(s.comm, s.partial, y, (int64_t)T * w.rows, s.stream);
 }
 
@@ -884,9 +894,16 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
              s->alloc(&a.scale_g, P) && s->alloc(&a.gu, P * 2 * c.I) && s->alloc(&a.h16, P * c.I) &&
              s->alloc(&a.scale_h, P) && s->alloc(&a.out, P * c.H);
     }
-    if (ok && s->world > 1)
+    if (ok && s->world > 1) {
+        uint8_t* pb = nullptr;
         ok = s->alloc(&s->partial, (size_t)chunk * c.H) && s->alloc(&s->full_logits, model->config->V) &&
-             s->alloc(&s->best, 2 * (size_t)s->world + 2);
+             s->alloc(&s->best, 2 * (size_t)s->world + 2) && s->alloc(&pb, tp_peer_buffer_bytes(c.H)) &&
+             s->alloc(&s->peer_seq, 1) && s->alloc(&s->tp_err, 1);
+        s->peer_buf = pb;
+        if (ok)
+            ok = cudaMemset(pb, 0, tp_peer_buffer_bytes(c.H)) == cudaSuccess &&
+                 cudaMemset(s->peer_seq, 0, 4) == cudaSuccess && cudaMemset(s->tp_err, 0, 4) == cudaSuccess;
+    }
     if (ok && chunk > 1 && delta_layers > 0)
         ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4) &&
              s->alloc(&s->qkv, (size_t)chunk * DQKV);
@@ -1159,6 +1176,44 @@ static void shard_fields(const Shard& sh, int* f) {
     const int v[14] = {sh.rank, sh.world, sh.kh0,     sh.vh0,    sh.ah0,    sh.kv0,   sh.i0,
                        sh.v0,   sh.lc.KH, sh.lc.VH, sh.lc.AH, sh.lc.KVH, sh.lc.I, sh.lc.V};
     std::memcpy(f, v, sizeof v);
+}
+int q3xb_state_ipc_handle(const q3xb_state* state, char* handle64) {
+    const State* s = reinterpret_cast<const State*>(state);
+    if (!s || !handle64 || s->world < 2 || !s->peer_buf) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, s->peer_buf) != cudaSuccess) return Q3XK_ECUDA;
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    std::memcpy(handle64, &h, sizeof h);
+    return Q3XK_OK;
+}
+int q3xb_state_ipc_open(q3xb_state* state, const char* handles) {
+    State* s = reinterpret_cast<State*>(state);
+    if (!s || !handles || s->world < 2 || s->world > 8 || s->peer_ready) return Q3XK_EINVAL;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    for (int r = 0; r < s->world; ++r) {
+        if (r == s->rank) {
+            s->peer_bases[r] = s->peer_buf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handles + 64 * (size_t)r, sizeof h);
+        if (cudaIpcOpenMemHandle(&s->peer_bases[r], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (q != s->rank && s->peer_bases[q]) cudaIpcCloseMemHandle(s->peer_bases[q]);
+            return Q3XK_ECUDA;
+        }
+    }
+    s->peer_ready = true;
+    return Q3XK_OK;
+}
+int q3xb_state_tp_error(const q3xb_state* state, int* flags) {
+    const State* s = reinterpret_cast<const State*>(state);
+    if (!s || !flags) return Q3XK_EINVAL;
+    *flags = 0;
+    if (!s->tp_err) return Q3XK_OK;
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    return cudaMemcpy(flags, s->tp_err, 4, cudaMemcpyDeviceToHost) == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
 }
 int q3xb_model_shard(const q3xb_model* model, int* fields14) {
     if (!model || !fields14) return Q3XK_EINVAL;

@@ -48,7 +48,131 @@ __global__ void pack_best_kernel(const float* __restrict__ logits, const int* __
     out[1] = (float)(i + v0);  // exact: vocabulary indices < 2^24
 }
 
+// ---- one-shot all-reduce over NVLink peer memory (decode-sized vectors) ------
+//
+// Every rank owns a PeerBuf in its own HBM, mapped into the other ranks with
+// CUDA IPC:  data[2][n_max] (this rank's partial, by phase)  flags[2][kMaxRanks]
+// (flags[phase][r] = the sequence number rank r has published).  A call with
+// sequence s (phase s & 1):
+//   1. copy the local partial into data[phase] of the own buffer;
+//   2. fence (system scope), then store s into flags[phase][rank] of every
+//      peer's buffer;
+//   3. wait until the own flags[phase][r] == s for every rank r -- bounded:
+//      after ~1 s the kernel sets the error word and returns;
+//   4. y[j] += sum over r = 0..world-1, in rank order, of data_r[phase][j]
+//      (peer loads over NVLink), so every rank gets bit-identical sums.
+// Two phases make the reuse safe: a rank reaches call s + 2 only after every
+// peer has published s + 1, i.e. finished reading the phase of call s.
+constexpr int kMaxRanks = 8;
+constexpr int kPerThread = 5;  // vectors up to 5 x 1024 floats (H <= 5120)
+
+struct PeerArgs {
+    float* data[kMaxRanks];  // data[2][n_max] of every rank (own one included)
+    int* flags[kMaxRanks];   // flags[2][kMaxRanks] of every rank
+    int rank, world, n_max;
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(1024) peer_allreduce_kernel(PeerArgs a, int* __restrict__ seq_ptr,
+                                                              const float* __restrict__ partial,
+                                                              float* __restrict__ y, int n,
+                                                              int* __restrict__ err) {
+    griddep_wait();
+    __shared__ int s_ok;
+    const int seq = *seq_ptr + 1, phase = seq & 1;
+    float* mine = a.data[a.rank] + (int64_t)phase * a.n_max;
+    {
+        float v[kPerThread];
+#pragma unroll
+        for (int k = 0; k < kPerThread; ++k) {
+            const int j = threadIdx.x + k * 1024;
+            v[k] = j < n ? partial[j] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < kPerThread; ++k) {
+            const int j = threadIdx.x + k * 1024;
+            if (j < n) mine[j] = v[k];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < a.world; ++r) st_release_sys(a.flags[r] + phase * kMaxRanks + a.rank, seq);
+        s_ok = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x < a.world) {  // one thread per source rank
+        const int* f = a.flags[a.rank] + phase * kMaxRanks + threadIdx.x;
+        const long long start = clock64();
+        int n_try = 0;
+        while (ld_acquire_sys(f) != seq) {
+            if ((++n_try & 63) == 0 && clock64() - start > 2000000000LL) {
+                atomicExch(err, 1);
+                s_ok = 0;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    // every load of every rank is issued before the first use (peer loads
+    // cost ~1 us each over NVLink), then the sums are taken in rank order
+    float t[kMaxRanks][kPerThread];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+        if (r < a.world) {
+            const float* src = a.data[r] + (int64_t)phase * a.n_max;
+#pragma unroll
+            for (int k = 0; k < kPerThread; ++k) {
+                const int j = threadIdx.x + k * 1024;
+                t[r][k] = j < n ? src[j] : 0.f;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kPerThread; ++k) {
+        const int j = threadIdx.x + k * 1024;
+        float acc = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (r < a.world) acc += t[r][k];
+        if (j < n) y[j] += acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *seq_ptr = seq;
+}
+
 }  // namespace
+
+size_t tp_peer_buffer_bytes(int n_max) {
+    return ((size_t)2 * n_max * 4 + 255) / 256 * 256 + 2 * kMaxRanks * sizeof(int);
+}
+
+int tp_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, int* seq, const float* partial,
+                          float* y, int n, int* err, cudaStream_t s) {
+    if (world > kMaxRanks || n > n_max || n > kPerThread * 1024) return Q3XK_EUNSUPPORTED;
+    PeerArgs a{};
+    const size_t data_bytes = ((size_t)2 * n_max * 4 + 255) / 256 * 256;
+    for (int r = 0; r < world; ++r) {
+        a.data[r] = static_cast<float*>(bases[r]);
+        a.flags[r] = reinterpret_cast<int*>(static_cast<uint8_t*>(bases[r]) + data_bytes);
+    }
+    a.rank = rank;
+    a.world = world;
+    a.n_max = n_max;
+    if (launch_pdl(peer_allreduce_kernel, dim3(1), dim3(1024), 0, s, a, seq, partial, y, n, err) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
 
 int tp_pack_best(const float* logits, const int* idx, int v0, float* out2, cudaStream_t s) {
     if (launch_pdl(pack_best_kernel, dim3(1), dim3(1), 0, s, logits, idx, v0, out2) != cudaSuccess) return Q3XK_ECUDA;

@@ -22,6 +22,15 @@ void tp_comm_destroy(void* comm);
 const char* tp_last_error();
 // hidden[0..n) += allreduce_sum(partial[0..n)) (partial is overwritten).
 int tp_allreduce_add(void* comm, float* partial, float* hidden, int64_t n, cudaStream_t s);
+// One-shot all-reduce of decode-sized vectors over peer memory (tp.cu):
+// bases[r] = rank r's buffer of tp_peer_buffer_bytes(n_max) bytes (own one
+// included, the others mapped with CUDA IPC), flags zeroed at creation; `seq`
+// a device int (zero-initialised, identical call sequence on every rank);
+// `err` a device int set to 1 if a peer did not publish within ~1 s.
+// y[0..n) += sum over ranks of partial[0..n), bit-identical on every rank.
+size_t tp_peer_buffer_bytes(int n_max);
+int tp_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, int* seq, const float* partial,
+                          float* y, int n, int* err, cudaStream_t s);
 // out2 = {logits[*idx], *idx + v0} (a rank's argmax in global numbering).
 int tp_pack_best(const float* logits, const int* idx, int v0, float* out2, cudaStream_t s);
 // out[world * n] = concatenation of every rank's in[n] (floats).

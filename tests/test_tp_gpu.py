@@ -33,8 +33,14 @@ def _tp_rank(rank, world, port, path, out, prompt, steps):
     dist.broadcast_object_list(ids, src=0)
     model = Model(path, rank, world)
     res = {}
+    def exchange(handle):  # IPC handles of the peer all-reduce buffers, in rank order
+        out = [None] * world
+        dist.all_gather_object(out, handle)
+        return out
+
     for k, mode in enumerate(("decode", "prefill")):
-        st = State(model, 256, ids[0][k])
+        # the decode-mode state all-reduces over peer memory, the other one with NCCL
+        st = State(model, 256, ids[0][k], exchange=exchange if mode == "decode" else None)
         if mode == "decode":
             for t in prompt:
                 st.forward([int(t)])
@@ -47,6 +53,8 @@ def _tp_rank(rank, world, port, path, out, prompt, steps):
             st.forward([toks[-1]])
         res[mode + "_tokens"] = np.array(toks)
         res[mode + "_final"] = st.logits()
+        assert st.tp_error() == 0
+        dist.barrier()  # no rank unmaps a peer buffer that another still reads
         st.close()
     model.close()
     dist.barrier()
