@@ -635,12 +635,16 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict
 }
 
 // ---- causal attention for a prompt (T > 1): flash-style tiles on CUDA cores.
-// CTA = 64 query tokens of one query head; key/value tiles of 32 positions
-// stream through shared memory with an online softmax (engine.cpp:347-367
-// computes the same softmax(q.k / sqrt(AD)) V per token); the output is
-// already gated by sigmoid(gate) (engine.cpp:368).
-constexpr int kFBQ = 64, kFBK = 32, kFD = 256, kFLd = kFD + 4;
-constexpr size_t kFlashSmem = (size_t)(kFBQ * kFLd + kFBK * kFLd + kFBK * kFD + kFBQ * (kFBK + 1)) * 4;
+// CTA = 64 query tokens of one query head; 64-key tiles of K and V stream
+// through shared memory with an online softmax (engine.cpp:347-367 computes
+// the same softmax(q.k / sqrt(AD)) V per token); the output is already gated
+// by sigmoid(gate) (engine.cpp:368).  Thread (ty, tx) of 16 x 16 owns query
+// rows 4ty..4ty+3: scores for keys tx + 16i, output dims 4tx + 64j; products
+// accumulate with packed FFMA2.
+constexpr int kFBQ = 64, kFBK = 64, kFD = 256, kFLd = kFD + 4, kFPd = kFBK + 4;
+constexpr size_t kFlashSmem = (size_t)(2 * kFBQ * kFLd + kFBK * kFD + kFBQ * kFPd) * 4;
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restrict__ proj, int64_t proj_stride, int T,
                                                            AttnDims ad, const int* __restrict__ pos,
@@ -653,10 +657,10 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
     float* Qs = fsm;                 // [kFBQ][kFLd]
     float* Ks = Qs + kFBQ * kFLd;    // [kFBK][kFLd]
     float* Vs = Ks + kFBK * kFLd;    // [kFBK][kFD]
-    float* Ps = Vs + kFBK * kFD;     // [kFBQ][kFBK + 1]
+    float* Ps = Vs + kFBK * kFD;     // [kFBQ][kFPd]
     const int qt = blockIdx.x, h = blockIdx.y;
     const int G = ad.AH / ad.KVH, kvh = h / G;
-    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
     const int t0 = qt * kFBQ;
     const int pos0 = *pos;
     const int rows = min(kFBQ, T - t0);
@@ -666,17 +670,22 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
     for (int e = tid; e < kFBQ * kFD / 4; e += 256) {
         const int r = e / (kFD / 4), d4 = e % (kFD / 4);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (r < rows) v = reinterpret_cast<const float4*>(proj + (int64_t)(t0 + r) * proj_stride + (int64_t)h * 2 * kFD)[d4];
+        if (r < rows)
+            v = reinterpret_cast<const float4*>(proj + (int64_t)(t0 + r) * proj_stride + (int64_t)h * 2 * kFD)[d4];
         reinterpret_cast<float4*>(Qs + r * kFLd)[d4] = v;
     }
-    const int r0 = ty * 2;  // this thread's two query rows; S keys tx + 8i; O dims tx*4 + 32j
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    float o[2][32];
+    const int r0 = ty * 4;
+    float m[4], l[4];
+    float2 o[4][8];  // row a, dims 4tx + 64j (+0,1 | +2,3)
+    int qpos[4];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < 4; ++a) {
+        m[a] = -INFINITY;
+        l[a] = 0.f;
+        qpos[a] = pos0 + t0 + r0 + a;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[a][j] = 0.f;
-    const int qpos[2] = {pos0 + t0 + r0, pos0 + t0 + r0 + 1};
+        for (int j = 0; j < 8; ++j) o[a][j] = make_float2(0.f, 0.f);
+    }
     for (int k0 = 0; k0 <= last_key; k0 += kFBK) {
         __syncthreads();  // previous tile consumed
         for (int e = tid; e < kFBK * kFD / 4; e += 256) {
@@ -692,83 +701,102 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
             reinterpret_cast<float4*>(Vs + r * kFD)[d4] = vv;
         }
         __syncthreads();
-        // S = Q K^T for rows r0, r0+1 and keys tx + 8i
-        float sc[2][4];
+        // S = Q K^T: rows r0 + a, keys tx + 16 i; sc[a][i/2] packs keys (i, i+1)
+        float2 sc[4][2];
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sc[a][i] = 0.f;
-#pragma unroll 4
+        for (int a = 0; a < 4; ++a) sc[a][0] = sc[a][1] = make_float2(0.f, 0.f);
+#pragma unroll 2
         for (int d4 = 0; d4 < kFD / 4; ++d4) {
-            const float4 q0 = reinterpret_cast<const float4*>(Qs + r0 * kFLd)[d4];
-            const float4 q1 = reinterpret_cast<const float4*>(Qs + (r0 + 1) * kFLd)[d4];
+            float4 q[4], k[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float4 kk = reinterpret_cast<const float4*>(Ks + (tx + 8 * i) * kFLd)[d4];
-                sc[0][i] += q0.x * kk.x + q0.y * kk.y + q0.z * kk.z + q0.w * kk.w;
-                sc[1][i] += q1.x * kk.x + q1.y * kk.y + q1.z * kk.z + q1.w * kk.w;
-            }
+            for (int a = 0; a < 4; ++a) q[a] = reinterpret_cast<const float4*>(Qs + (r0 + a) * kFLd)[d4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) k[i] = reinterpret_cast<const float4*>(Ks + (tx + 16 * i) * kFLd)[d4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int ip = 0; ip < 2; ++ip) {
+                    const float4 ka = k[2 * ip], kb = k[2 * ip + 1];
+                    float2 acc = sc[a][ip];
+                    acc = ffma2(make_float2(q[a].x, q[a].x), make_float2(ka.x, kb.x), acc);
+                    acc = ffma2(make_float2(q[a].y, q[a].y), make_float2(ka.y, kb.y), acc);
+                    acc = ffma2(make_float2(q[a].z, q[a].z), make_float2(ka.z, kb.z), acc);
+                    acc = ffma2(make_float2(q[a].w, q[a].w), make_float2(ka.w, kb.w), acc);
+                    sc[a][ip] = acc;
+                }
         }
-        // online softmax per row over this tile (8 threads share a row pair)
+        // online softmax per row over this tile (16 threads share a row)
 #pragma unroll
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < 4; ++a) {
+            float s4[4] = {sc[a][0].x, sc[a][0].y, sc[a][1].x, sc[a][1].y};
             float tmax = -INFINITY;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int j = k0 + tx + 8 * i;
-                sc[a][i] = j <= qpos[a] ? sc[a][i] * inv : -INFINITY;
-                tmax = fmaxf(tmax, sc[a][i]);
+                const int j = k0 + tx + 16 * i;
+                s4[i] = j <= qpos[a] ? s4[i] * inv : -INFINITY;
+                tmax = fmaxf(tmax, s4[i]);
             }
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
             const float mn = fmaxf(m[a], tmax);
             const float corr = mn == -INFINITY ? 1.f : expf(m[a] - mn);
             float psum = 0.f;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float pv = sc[a][i] == -INFINITY ? 0.f : expf(sc[a][i] - mn);
+                const float pv = s4[i] == -INFINITY ? 0.f : expf(s4[i] - mn);
                 psum += pv;
-                Ps[(r0 + a) * (kFBK + 1) + tx + 8 * i] = pv;
+                Ps[(r0 + a) * kFPd + tx + 16 * i] = pv;
             }
-            psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-            psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-            psum += __shfl_xor_sync(0xffffffffu, psum, 4);
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
             l[a] = l[a] * corr + psum;
             m[a] = mn;
+            const float2 c2 = make_float2(corr, corr);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[a][j] *= corr;
+            for (int j = 0; j < 8; ++j) o[a][j] = __fmul2_rn(o[a][j], c2);
         }
-        __syncwarp();
-        // O += P V (rows r0, r0+1; dims tx*4 + 32 jj)
-        for (int j = 0; j < kFBK; ++j) {
-            const float p0 = Ps[r0 * (kFBK + 1) + j], p1 = Ps[(r0 + 1) * (kFBK + 1) + j];
+        __syncwarp();  // a row's probabilities come from the 16 threads of its half-warp
+        // O += P V
+#pragma unroll 2
+        for (int j4 = 0; j4 < kFBK / 4; ++j4) {
+            float4 p[4];
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                const float4 v = reinterpret_cast<const float4*>(Vs + j * kFD)[tx + 8 * jj];
-                o[0][4 * jj] += p0 * v.x; o[0][4 * jj + 1] += p0 * v.y;
-                o[0][4 * jj + 2] += p0 * v.z; o[0][4 * jj + 3] += p0 * v.w;
-                o[1][4 * jj] += p1 * v.x; o[1][4 * jj + 1] += p1 * v.y;
-                o[1][4 * jj + 2] += p1 * v.z; o[1][4 * jj + 3] += p1 * v.w;
+            for (int a = 0; a < 4; ++a) p[a] = reinterpret_cast<const float4*>(Ps + (r0 + a) * kFPd)[j4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int key = 4 * j4 + jj;
+                float4 v[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) v[c] = reinterpret_cast<const float4*>(Vs + key * kFD)[tx + 16 * c];
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    const float pa = jj == 0 ? p[a].x : jj == 1 ? p[a].y : jj == 2 ? p[a].z : p[a].w;
+                    const float2 p2 = make_float2(pa, pa);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        o[a][2 * c] = ffma2(p2, make_float2(v[c].x, v[c].y), o[a][2 * c]);
+                        o[a][2 * c + 1] = ffma2(p2, make_float2(v[c].z, v[c].w), o[a][2 * c + 1]);
+                    }
+                }
             }
         }
     }
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < 4; ++a) {
         const int r = r0 + a;
         if (r >= rows) continue;
         const float* gate = proj + (int64_t)(t0 + r) * proj_stride + (int64_t)h * 2 * kFD + kFD;
         float* dst = out + (int64_t)(t0 + r) * out_stride + (int64_t)h * kFD;
         const float invl = 1.0f / l[a];
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-            const int d = tx * 4 + 32 * jj;
+        for (int c = 0; c < 4; ++c) {
+            const int d = 4 * tx + 64 * c;
             const float4 g = *reinterpret_cast<const float4*>(gate + d);
             float4 res;
-            res.x = o[a][4 * jj] * invl * sigmoidf_ref(g.x);
-            res.y = o[a][4 * jj + 1] * invl * sigmoidf_ref(g.y);
-            res.z = o[a][4 * jj + 2] * invl * sigmoidf_ref(g.z);
-            res.w = o[a][4 * jj + 3] * invl * sigmoidf_ref(g.w);
+            res.x = o[a][2 * c].x * invl * sigmoidf_ref(g.x);
+            res.y = o[a][2 * c].y * invl * sigmoidf_ref(g.y);
+            res.z = o[a][2 * c + 1].x * invl * sigmoidf_ref(g.z);
+            res.w = o[a][2 * c + 1].y * invl * sigmoidf_ref(g.w);
             *reinterpret_cast<float4*>(dst + d) = res;
         }
     }
