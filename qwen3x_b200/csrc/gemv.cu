@@ -41,20 +41,9 @@ namespace {
 #ifndef Q3XK_GEMV_MIN_BLOCKS
 #define Q3XK_GEMV_MIN_BLOCKS 3
 #endif
-// 1: the first row group's weights are prefetched into L2 before the
-// prologue (no registers held across it) and loaded after it;
-// 0: they are loaded into registers before the prologue.
-#ifndef Q3XK_GEMV_PREFETCH
-#define Q3XK_GEMV_PREFETCH 0
-#endif
 // CTAs per SM of the double-buffered kernels (two register batches per warp),
 // used when a matrix has too few rows to fill the GPU without a K split.
 constexpr int kDbBlocks = 2;
-// Batches ahead of the one being loaded whose weights are prefetched into
-// L2 (no registers held), so DRAM keeps streaming while a warp computes.
-#ifndef Q3XK_GEMV_L2_AHEAD
-#define Q3XK_GEMV_L2_AHEAD 0
-#endif
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
@@ -268,31 +257,6 @@ __device__ __forceinline__ void load_batch(Batch<TYPE>& bt, const GemvParams& p,
     }
 }
 
-template <int TYPE, int KS, int MODE>
-__device__ __forceinline__ void prefetch_batch(const GemvParams& p, const uint8_t* const* rec, int lane, int ks,
-                                               const int64_t* seg_off, int b = 0) {
-    constexpr int kBatch = Codec<TYPE>::kBatch;
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-        int u = unit_of(lane, b, i, kBatch, ks, KS);
-        if (u < p.units) {
-            int64_t off = 0;
-            if (MODE == kSegGather) {
-                const int seg = u / p.units_per_seg;
-                off = seg_off[seg];
-                u -= seg * p.units_per_seg;
-            }
-#pragma unroll
-            for (int j = 0; j < kRows; ++j) {
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(rec[j] + off + (int64_t)u * 16));
-                if (TYPE != Q3XK_BF16 && (u % (8 * Codec<TYPE>::kUnitsPerBlock)) == 0)
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(rec[j] + off + p.qbytes +
-                                                                  2 * (u / Codec<TYPE>::kUnitsPerBlock)));
-            }
-        }
-    }
-}
-
 // Returns this warp's partial sum of row (b4 ? 2 : 0) + (b3 ? 1 : 0) in lanes
 // 0, 8, 16 and 24 (transposed butterfly over the 4 rows).
 template <int TYPE, bool FAST, int KS, int MODE, bool DB>
@@ -328,7 +292,6 @@ __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* c
     if (DB) {
         // two register batches: the next one is in flight while this one is used
         Batch<TYPE> B;
-        if (Q3XK_GEMV_PREFETCH) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
         for (int b = 0; b < nb; b += 2) {
             if (b + 1 < nb) load_batch<TYPE, KS, MODE>(B, p, rec, lane, b + 1, ks, seg_off);
             compute(A, b);
@@ -337,9 +300,7 @@ __device__ __forceinline__ float warp_rows(const GemvParams& p, const uint8_t* c
         }
     } else {
         for (int b = 0; b < nb; ++b) {
-            if (Q3XK_GEMV_L2_AHEAD && b + Q3XK_GEMV_L2_AHEAD < nb)
-                prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off, b + Q3XK_GEMV_L2_AHEAD);
-            if (b > 0 || Q3XK_GEMV_PREFETCH) load_batch<TYPE, KS, MODE>(A, p, rec, lane, b, ks, seg_off);
+            if (b > 0) load_batch<TYPE, KS, MODE>(A, p, rec, lane, b, ks, seg_off);
             compute(A, b);
         }
     }
@@ -557,11 +518,7 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
     if (MODE == kPlain) {
         pass_rows<MODE>(p, gb, ge, 0, groups_per_cta, group, rec, row0, live);
         // The first batch of weights is requested before waiting on the previous kernel.
-#if Q3XK_GEMV_PREFETCH
-        if (live) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
-#else
         if (live) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
-#endif
         griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
     } else {
         griddep_wait();  // the expert ids come from the previous kernel
@@ -570,11 +527,7 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
             __syncthreads();
         }
         pass_rows<MODE>(p, gb, ge, 0, groups_per_cta, group, rec, row0, live);
-#if Q3XK_GEMV_PREFETCH
-        if (live) prefetch_batch<TYPE, KS, MODE>(p, rec, lane, ks, seg_off);
-#else
         if (live) load_batch<TYPE, KS, MODE>(A, p, rec, lane, 0, ks, seg_off);
-#endif
     }
 
     __shared__ float xstat[XF ? kMaxXGroups : 1], xred[kWarps];
@@ -649,11 +602,7 @@ int sm_count_cached() {
 // fill the GPU: the smallest split (1, 2, 4) whose grid keeps at least half
 // of the resident CTA slots busy.  Every CTA prescales all of x, so small
 // CTAs (large splits) pay that prologue over fewer rows.
-#ifndef Q3XK_GEMV_FORCE_KS
-#define Q3XK_GEMV_FORCE_KS 0  // tuning builds only: fixed K split (1, 2, 4, 8)
-#endif
 int choose_ksplit(int rows, int units, int slots) {
-    if (Q3XK_GEMV_FORCE_KS) return units >= 32 * Q3XK_GEMV_FORCE_KS ? Q3XK_GEMV_FORCE_KS : 1;
     for (int ks = 1; ks <= 4; ks *= 2) {
         if (ks > 1 && units < 32 * ks) return ks / 2;
         const int64_t per = (int64_t)(kWarps / ks) * kRows;
@@ -713,7 +662,7 @@ int launch(GemvParams p, cudaStream_t s) {
     const size_t smem = smem_bytes<TYPE>(p);
     if (smem > 200 * 1024) return Q3XK_EUNSUPPORTED;
     if (p.xform) return launch_xf<TYPE, MODE, true, false>(p, smem, s);
-    if (MODE != kRowGather && p.ksplit > 1 && !Q3XK_GEMV_FORCE_KS) {
+    if (MODE != kRowGather && p.ksplit > 1) {
         p.ksplit = choose_ksplit(p.rows, p.units, sm_count_cached() * kDbBlocks);
         return launch_xf<TYPE, MODE, false, true>(p, smem, s);
     }
