@@ -367,7 +367,8 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
     greedy steps (state_argmax + state_forward of that token), as the
     reference's runtime drives the backend.  Times are CUDA events on the
     state's stream (max over ranks); weights (GBs) are far larger than L2.
-    world > 1: tensor parallelism, one rank per GPU (rank 0 writes the file)."""
+    world > 1: one rank per GPU (rank 0 writes the file) -- tensor parallelism
+    for dense configs, expert parallelism for MoE configs."""
     import numpy as np
     import torch
 
@@ -382,7 +383,7 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
     tag = os.environ.get("TORCHELASTIC_RUN_ID", str(os.getpid())) if world > 1 else str(os.getpid())
     path = os.path.join(model_file_dir(size), f"q3x_bench_{cfg_id}_{tag}.bin")
     out = {"config": f"{cfg_id} ({c.name})", "prompt_tokens": prompt_len, "decode_steps": decode_steps,
-           "parallelism": f"tp{world}" if world > 1 else "single GPU"}
+           "parallelism": (f"ep{world}" if c.experts else f"tp{world}") if world > 1 else "single GPU"}
     t0 = time.time()
     try:
         if rank == 0:

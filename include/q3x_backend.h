@@ -100,7 +100,12 @@ Q3XK_API int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens);
  * Tensor parallelism (one process per GPU, dense models): each rank loads its
  * share of model.bin (column-parallel q/k/v/z/a/b, q+gate, gate/up and
  * lm_head rows; row-parallel out/down columns, partial sums all-reduced with
- * NCCL) and owns a State whose collectives run on the state's stream.  Rank 0
+ * NCCL) and owns a State whose collectives run on the state's stream.
+ * MoE models take expert parallelism through the same calls: each rank loads
+ * the routed experts [e0, e0 + experts/world) of every layer and replicates
+ * everything else; a token's MoE output is the all-reduced sum of the slots
+ * each rank runs (the shared expert of layer i runs on rank i % world), and
+ * logits/argmax are local (every rank holds the full lm_head).  Rank 0
  * makes a communicator id with q3xb_tp_unique_id and every rank passes the
  * same 128 bytes to q3xb_state_create_tp; an id bootstraps one communicator,
  * so every State needs a fresh one.  state_forward, state_argmax and
@@ -120,10 +125,11 @@ Q3XK_API int q3xb_state_ipc_open(q3xb_state* state, const char* handles_world_x_
 /* 1 if a peer all-reduce gave up waiting for a peer (~1 s), else 0. */
 Q3XK_API int q3xb_state_tp_error(const q3xb_state* state, int* flags);
 /* The rank's share: rank, world, first key/value/query/KV head, first
- * intermediate row, first vocabulary row, then the local KH, VH, AH, KVH, I, V. */
-Q3XK_API int q3xb_model_shard(const q3xb_model* model, int* fields14);
+ * intermediate row, first vocabulary row, the local KH, VH, AH, KVH, I, V,
+ * then the first routed expert and the local routed-expert count (MoE). */
+Q3XK_API int q3xb_model_shard(const q3xb_model* model, int* fields16);
 /* The same plan for a registered model ID without loading anything. */
-Q3XK_API int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields14, char* err, size_t errlen);
+Q3XK_API int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields16, char* err, size_t errlen);
 
 #ifdef __cplusplus
 }  // extern "C"

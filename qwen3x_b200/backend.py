@@ -19,12 +19,13 @@ from . import capi
 
 FIELDS = ("id", "V", "H", "I", "N", "AI", "AH", "KVH", "AD", "RD", "KH", "VH", "KD", "VD", "CK",
           "context", "experts", "top_k", "shared_I", "matrix_type", "tied")
-SHARD_FIELDS = ("rank", "world", "kh0", "vh0", "ah0", "kv0", "i0", "v0", "KH", "VH", "AH", "KVH", "I", "V")
+SHARD_FIELDS = ("rank", "world", "kh0", "vh0", "ah0", "kv0", "i0", "v0", "KH", "VH", "AH", "KVH", "I", "V",
+                "e0", "experts")
 
 
 def tp_plan(model_id: int, rank: int, world: int) -> dict:
     """This rank's tensor-parallel share of a registered model (no loading)."""
-    f = (ctypes.c_int * 14)()
+    f = (ctypes.c_int * 16)()
     err = ctypes.create_string_buffer(256)
     st = capi.lib().q3xb_tp_plan(model_id, rank, world, f, err, 256)
     if st != capi.OK:
@@ -54,7 +55,7 @@ class Model:
         f = (ctypes.c_int * 21)()
         capi.check(self.lib.q3xb_model_config(self.handle, f), "q3xb_model_config")
         self.config = dict(zip(FIELDS, list(f)))
-        sf = (ctypes.c_int * 14)()
+        sf = (ctypes.c_int * 16)()
         capi.check(self.lib.q3xb_model_shard(self.handle, sf), "q3xb_model_shard")
         self.shard = dict(zip(SHARD_FIELDS, list(sf)))
 

@@ -117,26 +117,43 @@ struct Layer {
     q3xk_matrix router{};   // MoE: BF16 [experts + 1][H] = router rows + shared gate row
 };
 
-// Tensor-parallel share of one rank (world = 1: everything).  Column-parallel
-// (split output rows): DeltaNet q/k by key head, v/z/a/b by value head,
-// attention q+gate by query head, k/v by KV head (replicated when there are
-// fewer KV heads than ranks), FFN gate/up by intermediate row, lm_head by
-// vocabulary row.  Row-parallel (split input columns, partial sums
-// all-reduced): DeltaNet out, attention out, FFN down.  lc = the rank's dims.
+// Share of one rank (world = 1: everything).  Dense models, tensor
+// parallelism -- column-parallel (split output rows): DeltaNet q/k by key
+// head, v/z/a/b by value head, attention q+gate by query head, k/v by KV head
+// (replicated when there are fewer KV heads than ranks), FFN gate/up by
+// intermediate row, lm_head by vocabulary row; row-parallel (split input
+// columns, partial sums all-reduced): DeltaNet out, attention out, FFN down.
+// MoE models, expert parallelism -- the routed experts [e0, e0 + el) of every
+// layer, everything else (router and shared expert included) replicated; each
+// rank adds the slots it runs into a partial sum that is all-reduced.
+// lc = the rank's dims (lc.experts stays the routed total).
 struct Shard {
     int rank = 0, world = 1;
     int kh0 = 0, vh0 = 0, ah0 = 0, kv0 = 0, i0 = 0, v0 = 0;
+    bool ep = false;
+    int e0 = 0, el = 0;
     Config lc{};
 };
+
+// Pool index of the shared expert where this rank runs it, else -1: under
+// expert parallelism the shared expert of layer i runs on rank i % world.
+int shared_slot(const Shard& sh, int layer) { return layer % sh.world == sh.rank ? sh.el : -1; }
 
 const char* make_shard(const Config& c, int rank, int world, Shard& sh) {
     sh = Shard{};
     sh.rank = rank;
     sh.world = world;
     sh.lc = c;
+    sh.el = c.experts;
     if (world < 1 || rank < 0 || rank >= world) return "invalid tensor-parallel rank";
     if (world == 1) return nullptr;
-    if (c.experts) return "tensor parallelism is not built for MoE models";
+    if (c.experts) {
+        if (c.experts % world) return "the experts do not split over the expert-parallel ranks";
+        sh.ep = true;
+        sh.el = c.experts / world;
+        sh.e0 = rank * sh.el;
+        return nullptr;
+    }
     if (c.KH % world || c.VH % world || c.AH % world || c.V % world || c.I % world || (c.I / world) % 32)
         return "model shape does not split over the tensor-parallel ranks";
     const int ahn = c.AH / world, G = c.AH / c.KVH;
@@ -233,6 +250,8 @@ struct State {
     size_t gemm_ws_bytes = 0;
     int split_len = 0;
     int rank = 0, world = 1;
+    bool tp = false;               // tensor parallelism (dense model, world > 1)
+    bool ep = false;               // expert parallelism (MoE model, world > 1)
     void* comm = nullptr;          // NCCL communicator (world > 1)
     float* partial = nullptr;      // row-parallel partial sums [chunk][H] (world > 1)
     float* full_logits = nullptr;  // gathered logits [V] (world > 1)
@@ -518,15 +537,18 @@ struct Loader {
             }
             l.post_norm = vec(cur.take((size_t)c.H * 2), c.H, true, 1.0f);
             if (E) {
+                // router: all experts; pools: this rank's experts [e0, e0 + El), shared expert at El
+                const int El = sh.el;
                 l.router = matrix(Q3XK_BF16, E + 1, c.H, 1);
                 upload(view(l.router, 0, 0, E), packed(Q3XK_BF16, E, c.H), 1);
-                l.gate_up = matrix(type, 2 * c.I, c.H, E + 1);
-                upload_swiglu(l.gate_up, packed(type, E * 2 * c.I, c.H), (int64_t)E * 2 * c.I, c.I, 0);
-                l.down = matrix(type, c.H, c.I, E + 1);
-                upload(view(l.down, 0, 0, c.H), packed(type, E * c.H, c.I), E);
-                upload_swiglu(view(l.gate_up, E, 0, 2 * c.I), packed(type, c.shared_I, c.H), c.I, c.I, 0);
-                upload_swiglu(view(l.gate_up, E, 0, 2 * c.I), packed(type, c.shared_I, c.H), c.I, c.I, c.I);
-                upload(view(l.down, E, 0, c.H), packed(type, c.H, c.shared_I), 1);
+                l.gate_up = matrix(type, 2 * c.I, c.H, El + 1);
+                upload_swiglu(l.gate_up, at_row(packed(type, E * 2 * c.I, c.H), c.H, sh.e0 * 2 * c.I),
+                              (int64_t)El * 2 * c.I, c.I, 0);
+                l.down = matrix(type, c.H, c.I, El + 1);
+                upload(view(l.down, 0, 0, c.H), at_row(packed(type, E * c.H, c.I), c.I, sh.e0 * c.H), El);
+                upload_swiglu(view(l.gate_up, El, 0, 2 * c.I), packed(type, c.shared_I, c.H), c.I, c.I, 0);
+                upload_swiglu(view(l.gate_up, El, 0, 2 * c.I), packed(type, c.shared_I, c.H), c.I, c.I, c.I);
+                upload(view(l.down, El, 0, c.H), packed(type, c.H, c.shared_I), 1);
                 upload(view(l.router, 0, E, 1), packed(Q3XK_BF16, 1, c.H), 1);
             } else {
                 l.gate_up = matrix(type, 2 * L.I, c.H, 1);
@@ -655,21 +677,40 @@ int rms_input(State& s, const float* x, const float* w1, int n, q3xk_xform* xf, 
     return launch_rms(x, w1, n, 1, s.normed, s.stream);
 }
 
+// y[0..T*H) += the sum over ranks of s.partial[0..T*H) (row-parallel
+// projections, expert-parallel MoE).  Decode: one-shot all-reduce over NVLink
+// peer memory once the peers' buffers are open, else NCCL.
+int allreduce_add(State& s, float* y, int T) {
+    const int H = s.c->H;
+    if (T == 1 && s.peer_ready)
+        return tp_peer_allreduce_add(s.peer_bases, s.rank, s.world, H, s.peer_seq, s.partial, y, H, s.tp_err,
+                                     s.stream);
+    return tp_allreduce_add(s.comm, s.partial, y, (int64_t)T * H, s.stream);
+}
+
 // MoE FFN of token t (engine.cpp:406-430): router logits (+ the shared-expert
 // gate as one more row) from RMS(hidden_t), device top-k, gate|up rows of the
 // selected experts with the weighted SwiGLU in their epilogue, then the down
 // projections of all slots added to hidden_t.
-int moe_token(State& s, const Config& c, const Layer& l, int t) {
+//
+// Expert parallelism: the slots whose expert lives on another rank get id -1
+// (skipped by both GEMVs); this rank's slots are summed into s.partial, and
+// the partial sums of all ranks are all-reduced into hidden_t.
+int moe_token(State& s, const Config& c, const Layer& l, int t, int layer) {
     const cudaStream_t st = s.stream;
+    const Shard& sh = s.model->shard;
     const int S = c.top_k + 1;  // routed slots + the shared expert
     float* h = s.hidden + (size_t)t * c.H;
     q3xk_xform xr;
     const float* in = nullptr;
     Q3XB_TRY(rms_input(s, h, l.post_norm, c.H, &xr, &in));
     Q3XB_TRY(q3xk_gemv_ex(&l.router, in, s.rlogits, 0, &xr, st));
-    Q3XB_TRY(q3xk_router_topk(s.rlogits, c.experts, c.top_k, 1, s.rids, s.rweights, st));
+    Q3XB_TRY(router_topk(s.rlogits, c.experts, c.top_k, 1, sh.e0, sh.el, shared_slot(sh, layer), s.rids, s.rweights,
+                         st));
     Q3XB_TRY(gemv_swiglu(&l.gate_up, in, s.hbuf, s.rids, S, s.rweights, &xr, st));
-    return q3xk_expert_gemv_segments(&l.down, s.rids, S, s.hbuf, h, 1, st);
+    if (!s.ep) return q3xk_expert_gemv_segments(&l.down, s.rids, S, s.hbuf, h, 1, st);
+    Q3XB_TRY(q3xk_expert_gemv_segments(&l.down, s.rids, S, s.hbuf, s.partial, 0, st));
+    return allreduce_add(s, h, 1);
 }
 
 // One decode token (T = 1): every elementwise step that feeds a GEMV is
@@ -678,12 +719,9 @@ int moe_token(State& s, const Config& c, const Layer& l, int t) {
 // out = W x for a row-parallel projection: y += W x on one GPU; with
 // tensor parallelism the rank's partial sum is all-reduced into y.
 int row_parallel(State& s, const q3xk_matrix& w, const float* x, int T, float* y) {
-    if (s.world == 1) return mm(s, w, x, T, y, 1);
+    if (!s.tp) return mm(s, w, x, T, y, 1);
     Q3XB_TRY(mm(s, w, x, T, s.partial, 0));
-    if (T == 1 && s.peer_ready)  // decode: one-shot all-reduce over NVLink peer memory
-        return tp_peer_allreduce_add(s.peer_bases, s.rank, s.world, s.c->H, s.peer_seq, s.partial, y, w.rows,
-                                     s.tp_err, s.stream);
-    return tp_allreduce_add(s.comm, s.partial, y, (int64_t)T * w.rows, s.stream);
+    return allreduce_add(s, y, T);
 }
 
 int forward_token(Model& m, State& s, bool logits) {
@@ -715,7 +753,7 @@ int forward_token(Model& m, State& s, bool logits) {
                 xg.w = l.dnorm;
                 xg.z = s.proj + DQKV;
             }
-            if (s.world == 1 || xg.kind != Q3XK_XFORM_NONE)
+            if (!s.tp || xg.kind != Q3XK_XFORM_NONE)
                 Q3XB_TRY(q3xk_gemv_ex(&l.out, s.mix, s.hidden, 1, &xg, st));
             else
                 Q3XB_TRY(row_parallel(s, l.out, s.mix, 1, s.hidden));
@@ -728,7 +766,7 @@ int forward_token(Model& m, State& s, bool logits) {
             ++ai;
         }
         if (c.experts) {
-            Q3XB_TRY(moe_token(s, c, l, 0));
+            Q3XB_TRY(moe_token(s, c, l, 0, i));
         } else {
             q3xk_xform xpost;
             const float* pin = nullptr;
@@ -793,11 +831,16 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
             a.experts = c.experts;
             a.top_k = c.top_k;
             a.T = T;
+            a.e0 = m.shard.e0;
+            a.local = m.shard.el;
+            a.shared_id = shared_slot(m.shard, i);
             a.x = s.normed;
-            a.hidden = s.hidden;
+            a.hidden = s.ep ? s.partial : s.hidden;
+            a.accumulate = s.ep ? 0 : 1;
             Q3XB_TRY(moe_prefill(a, st));
+            if (s.ep) Q3XB_TRY(allreduce_add(s, s.hidden, T));
         } else if (c.experts) {
-            for (int t = 0; t < T; ++t) Q3XB_TRY(moe_token(s, c, l, t));
+            for (int t = 0; t < T; ++t) Q3XB_TRY(moe_token(s, c, l, t, i));
         } else {
             Q3XB_TRY(launch_rms(s.hidden, l.post_norm, H, T, s.normed, st));
             Q3XB_TRY(mm(s, l.gate_up, s.normed, T, s.proj, 0));
@@ -857,6 +900,8 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
     s->capacity = context;
     s->rank = model->shard.rank;
     s->world = model->shard.world;
+    s->ep = model->shard.ep;
+    s->tp = s->world > 1 && !s->ep;
     if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
         set_error(err, errlen, "cannot create a CUDA stream");
         return nullptr;
@@ -1028,7 +1073,7 @@ int argmax_impl(const State* s, int* token) {
     if (!s || !token) return Q3XK_EINVAL;
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
     Q3XB_TRY(q3xk_argmax(s->logits, s->c->V, s->argmax_out, s->argmax_ws, s->argmax_ws_bytes, s->stream));
-    if (s->world > 1) {
+    if (s->tp) {
         // every rank's (value, global index), gathered; the first maximum wins
         float* mine = s->best + 2 * s->world;
         Q3XB_TRY(tp_pack_best(s->logits, s->argmax_out, s->model->shard.v0, mine, s->stream));
@@ -1052,7 +1097,7 @@ int argmax_impl(const State* s, int* token) {
 int copy_logits_impl(const State* s, float* out) {
     if (!s || !out) return Q3XK_EINVAL;
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
-    if (s->world > 1) {  // vocabulary shards in rank order
+    if (s->tp) {  // vocabulary shards in rank order
         Q3XB_TRY(tp_allgather(s->comm, s->logits, s->full_logits, s->c->V, s->stream));
         if (cudaMemcpyAsync(out, s->full_logits, (size_t)s->c->V * s->world * 4, cudaMemcpyDeviceToHost,
                             s->stream) != cudaSuccess ||
@@ -1173,8 +1218,8 @@ q3xb_state* q3xb_state_create_tp(q3xb_model* model, int context_size, const char
         create_state(reinterpret_cast<Model*>(model), context_size, nccl_id, err, errlen));
 }
 static void shard_fields(const Shard& sh, int* f) {
-    const int v[14] = {sh.rank, sh.world, sh.kh0,     sh.vh0,    sh.ah0,    sh.kv0,   sh.i0,
-                       sh.v0,   sh.lc.KH, sh.lc.VH, sh.lc.AH, sh.lc.KVH, sh.lc.I, sh.lc.V};
+    const int v[16] = {sh.rank,   sh.world,  sh.kh0,   sh.vh0,    sh.ah0,  sh.kv0,  sh.i0, sh.v0,
+                       sh.lc.KH, sh.lc.VH, sh.lc.AH, sh.lc.KVH, sh.lc.I, sh.lc.V, sh.e0, sh.el};
     std::memcpy(f, v, sizeof v);
 }
 int q3xb_state_ipc_handle(const q3xb_state* state, char* handle64) {
@@ -1215,14 +1260,14 @@ int q3xb_state_tp_error(const q3xb_state* state, int* flags) {
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
     return cudaMemcpy(flags, s->tp_err, 4, cudaMemcpyDeviceToHost) == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
 }
-int q3xb_model_shard(const q3xb_model* model, int* fields14) {
-    if (!model || !fields14) return Q3XK_EINVAL;
-    shard_fields(reinterpret_cast<const Model*>(model)->shard, fields14);
+int q3xb_model_shard(const q3xb_model* model, int* fields16) {
+    if (!model || !fields16) return Q3XK_EINVAL;
+    shard_fields(reinterpret_cast<const Model*>(model)->shard, fields16);
     return Q3XK_OK;
 }
-int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields14, char* err, size_t errlen) {
+int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields16, char* err, size_t errlen) {
     const Config* c = config_for_id(model_id);
-    if (!c || !fields14) {
+    if (!c || !fields16) {
         set_error(err, errlen, "unsupported Qwen model ID");
         return Q3XK_EINVAL;
     }
@@ -1231,7 +1276,7 @@ int q3xb_tp_plan(uint32_t model_id, int rank, int world, int* fields14, char* er
         set_error(err, errlen, "%s", e);
         return Q3XK_EUNSUPPORTED;
     }
-    shard_fields(sh, fields14);
+    shard_fields(sh, fields16);
     return Q3XK_OK;
 }
 void q3xb_state_destroy(q3xb_state* state) { delete reinterpret_cast<State*>(state); }

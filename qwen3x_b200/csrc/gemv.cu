@@ -78,6 +78,8 @@ struct GemvParams {
     int ksplit;  // warps sharing a row group (1, 2, 4 or 8), each on a slice of K
     // Expert gathers (MoE): `ids` (device) picks experts of a pool whose
     // matrices are `expert_stride` bytes apart.
+    // An id < 0 skips its slot: rows of a skipped slot are neither read nor
+    // written (row gather); a skipped segment adds nothing (segment gather).
     const int* ids;
     int64_t expert_stride;
     int rows_per_expert;  // row gather: virtual row r = expert ids[r / rpe], row r % rpe
@@ -247,6 +249,14 @@ __device__ __forceinline__ void load_batch(Batch<TYPE>& bt, const GemvParams& p,
                 off = seg_off[seg];
                 u -= seg * p.units_per_seg;
             }
+            if (MODE == kSegGather && off < 0) {  // skipped segment: zero weights (its x is zero too)
+#pragma unroll
+                for (int j = 0; j < kRows; ++j) {
+                    bt.q[i][j] = make_uint4(0u, 0u, 0u, 0u);
+                    bt.d[i][j] = 0;
+                }
+                continue;
+            }
 #pragma unroll
             for (int j = 0; j < kRows; ++j) {
                 bt.q[i][j] = ldg_stream(rec[j] + off + (int64_t)u * 16);
@@ -414,15 +424,26 @@ __device__ __forceinline__ void pass_rows(const GemvParams& p, int gb, int ge, i
     const int gi = gb + it * gpc + group;
     live = gi < ge;
     row0 = gi * kRows;
+    bool any = false;
 #pragma unroll
     for (int j = 0; j < kRows; ++j) {
         const int row = min(row0 + j, p.rows - 1);
-        if (MODE == kRowGather)
-            rec[j] = p.w + (int64_t)p.ids[row / p.rows_per_expert] * p.expert_stride +
-                     (int64_t)(row % p.rows_per_expert) * p.row_stride;
-        else
+        if (MODE == kRowGather) {
+            const int e = p.ids[row / p.rows_per_expert];  // < 0: skipped slot (row 0 stands in)
+            any |= e >= 0;
+            rec[j] = e < 0 ? p.w
+                           : p.w + (int64_t)e * p.expert_stride + (int64_t)(row % p.rows_per_expert) * p.row_stride;
+        } else {
             rec[j] = p.w + (int64_t)row * p.row_stride;
+        }
     }
+    if (MODE == kRowGather) live = live && any;
+}
+
+// False for a row of a skipped slot (row gather), whose output is left as it is.
+template <int MODE>
+__device__ __forceinline__ bool row_kept(const GemvParams& p, int row) {
+    return MODE != kRowGather || __ldg(p.ids + row / p.rows_per_expert) >= 0;
 }
 
 // The CTA's passes over its row groups [gb, ge): dot products, then the
@@ -445,12 +466,12 @@ __device__ __forceinline__ void gemv_passes(const GemvParams& p, const uint8_t**
         if (KS == 1) {
             if (p.epi) {
                 const float u = __shfl_down_sync(0xffffffffu, k, 16);  // lanes 0, 8 <- rows 2, 3
-                if ((lane == 0 || lane == 8) && live && row0 < p.rows) {
+                if ((lane == 0 || lane == 8) && live && row0 < p.rows && row_kept<MODE>(p, row0)) {
                     float h = k * sigmoid_ref(k) * u;
                     if (p.ew) h = __ldg(p.ew + row0 / p.rows_per_expert) * h;
                     p.y[row0 / 2 + (lane >> 3)] = h;
                 }
-            } else if ((lane & 7) == 0 && live && row0 + r < p.rows) {
+            } else if ((lane & 7) == 0 && live && row0 + r < p.rows && row_kept<MODE>(p, row0 + r)) {
                 float* yp = p.y + row0 + r;
                 *yp = p.accumulate ? *yp + k : k;
             }
@@ -464,7 +485,7 @@ __device__ __forceinline__ void gemv_passes(const GemvParams& p, const uint8_t**
             if (tid < groups_per_cta * 2) {
                 const int g = tid / 2, rr = tid % 2;
                 const int grow = (gbase + g) * kRows;
-                if (gbase + g < ge && grow < p.rows) {
+                if (gbase + g < ge && grow < p.rows && row_kept<MODE>(p, grow)) {
                     float vg = 0.f, vu = 0.f;
 #pragma unroll
                     for (int sl = 0; sl < KS; ++sl) {
@@ -479,7 +500,7 @@ __device__ __forceinline__ void gemv_passes(const GemvParams& p, const uint8_t**
         } else if (tid < groups_per_cta * kRows) {
             const int g = tid / kRows, rr = tid % kRows;
             const int row = (gbase + g) * kRows + rr;
-            if (gbase + g < ge && row < p.rows) {
+            if (gbase + g < ge && row < p.rows && row_kept<MODE>(p, row)) {
                 float v = 0.f;
 #pragma unroll
                 for (int sl = 0; sl < KS; ++sl) v += part[(g * KS + sl) * kRows + rr];
@@ -523,7 +544,10 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
     } else {
         griddep_wait();  // the expert ids come from the previous kernel
         if (MODE == kSegGather) {
-            if (tid < p.units / p.units_per_seg) seg_off[tid] = (int64_t)p.ids[tid] * p.expert_stride;
+            if (tid < p.units / p.units_per_seg) {
+                const int e = p.ids[tid];
+                seg_off[tid] = e < 0 ? -1 : (int64_t)e * p.expert_stride;  // -1: skipped segment
+            }
             __syncthreads();
         }
         pass_rows<MODE>(p, gb, ge, 0, groups_per_cta, group, rec, row0, live);
@@ -539,6 +563,9 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
         float v[C::kCols];
         if (XF) stage_x<C::kCols>(p, u, reinterpret_cast<float*>(xs4 + u * C::kChunks), xstat);
         unit_x<C::kCols, XF>(p, u, v, xs4 + u * C::kChunks);
+        if (MODE == kSegGather && seg_off[u / p.units_per_seg] < 0)
+#pragma unroll
+            for (int k = 0; k < C::kCols; ++k) v[k] = 0.f;
         int P = 0;
         float2 gu = f2(1.f, 0.f);
         if (TYPE != Q3XK_BF16) {
@@ -573,6 +600,9 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
             float v[C::kCols];
             if (XF) stage_x<C::kCols>(p, u, reinterpret_cast<float*>(xs4 + u * C::kChunks), xstat);
             unit_x<C::kCols, XF>(p, u, v, xs4 + u * C::kChunks);
+            if (MODE == kSegGather && seg_off[u / p.units_per_seg] < 0)
+#pragma unroll
+                for (int k = 0; k < C::kCols; ++k) v[k] = 0.f;
 #pragma unroll
             for (int j = 0; j < C::kChunks; ++j)
                 xs4[u * C::kChunks + swz<TYPE>(u, j)] =

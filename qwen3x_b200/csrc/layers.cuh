@@ -53,8 +53,13 @@ struct MoePrefillArgs {
     const q3xk_matrix* gate_up;  // pool [E+1][2I][H], SwiGLU-interleaved rows
     const q3xk_matrix* down;     // pool [E+1][H][I]
     int experts, top_k, T;
+    // Expert parallelism: the pools hold experts [e0, e0 + local) and the
+    // shared expert at index `local`; shared_id = local where this GPU runs
+    // the shared expert, else -1.  One GPU: e0 = 0, local = shared_id = E.
+    int e0, local, shared_id;
     const float* x;  // RMSNorm(hidden) [T][H]
-    float* hidden;   // [T][H], += MoE output
+    float* hidden;   // [T][H]: += MoE output (accumulate = 1) or = (0)
+    int accumulate;
     // work (device): sizes for P = T * (top_k + 1) pairs
     float* logits;       // [T][E+1]
     int* ids;            // [T][S]
@@ -73,6 +78,10 @@ struct MoePrefillArgs {
     float* out;          // [P][H]
 };
 int moe_prefill(const MoePrefillArgs& a, cudaStream_t s);
+// Top-k routing of T tokens (router_topk_kernel) with the expert-parallel id
+// mapping of MoePrefillArgs (e0, local, shared_id).
+int router_topk(const float* logits, int experts, int top_k, int T, int e0, int local, int shared_id, int* ids,
+                float* weights, cudaStream_t s);
 
 int launch_embed(const q3xk_matrix& m, const int* tokens, int T, float* out, cudaStream_t s);
 int launch_rms(const float* x, const float* w1, int n, int T, float* out, cudaStream_t s);

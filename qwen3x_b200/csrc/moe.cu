@@ -22,9 +22,14 @@ namespace {
 constexpr int kMaxPerLane = 16;  // experts <= 512
 
 
+// Expert parallelism: the ids written are local to the rank's pool -- a
+// routed expert e becomes e - e0 when e0 <= e < e0 + local, else -1 (not on
+// this rank); the shared slot gets shared_id (-1: another rank runs it).  One
+// GPU: e0 = 0, local = experts, shared_id = experts.
 __global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict__ logits, int experts, int top_k,
                                                          int with_shared, int* __restrict__ ids,
-                                                         float* __restrict__ weights) {
+                                                         float* __restrict__ weights, int e0, int local,
+                                                         int shared_id) {
     griddep_wait();
     griddep_launch_dependents();
     // one token per block: block b reads row b of [T][experts + with_shared] logits
@@ -79,11 +84,12 @@ __global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict
     }
     if (lane == 0) {
         for (int slot = 0; slot < top_k; ++slot) {
-            ids[slot] = chosen_id[slot];
+            const int e = chosen_id[slot] - e0;
+            ids[slot] = e >= 0 && e < local ? e : -1;
             weights[slot] = chosen_p[slot] / selected_total;
         }
         if (with_shared) {
-            ids[top_k] = experts;  // the shared expert is stored as expert `experts` of each pool
+            ids[top_k] = shared_id;  // the shared expert is stored after the routed ones of each pool
             weights[top_k] = sigmoid_ref(logits[experts]);
         }
     }
@@ -193,7 +199,8 @@ __global__ void __launch_bounds__(256) router_batch_kernel(const uint8_t* __rest
     }
 }
 
-// Groups the (token, slot) pairs by expert.  One CTA.  Outputs: xoff[E+1]
+// Groups the (token, slot) pairs by expert (pairs with id < 0 are left out,
+// pos = -1).  One CTA.  Outputs: xoff[E+1]
 // (first packed row of each expert), tile_off_a/b[E+1] (first GEMM tile of each
 // expert for two GEMMs with tiles_a / tiles_b weight-row tiles), pos[T*S]
 // (packed row of each pair), pair_token[P], pair_weight[P].  Positions inside
@@ -211,7 +218,8 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
     int* cursor = gsm + experts;  // [experts]
     for (int e = threadIdx.x; e < experts; e += blockDim.x) count[e] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < pairs; i += blockDim.x) atomicAdd(&count[ids[i]], 1);
+    for (int i = threadIdx.x; i < pairs; i += blockDim.x)
+        if (ids[i] >= 0) atomicAdd(&count[ids[i]], 1);
     __syncthreads();
     if (threadIdx.x == 0) {
         int x = 0, ta = 0, tb = 0;
@@ -231,6 +239,10 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
     }
     __syncthreads();
     for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+        if (ids[i] < 0) {  // expert on another rank
+            pos[i] = -1;
+            continue;
+        }
         const int p = atomicAdd(&cursor[ids[i]], 1);
         pos[i] = p;
         pair_token[p] = i / S;
@@ -238,15 +250,17 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
     }
 }
 
-// x16g[p] = x16[pair_token[p]], scale_g[p] = scale[pair_token[p]] (K halves per row).
+// x16g[p] = x16[pair_token[p]], scale_g[p] = scale[pair_token[p]] (K halves per
+// row) for the *pairs grouped rows.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ x16,
                                                           const float* __restrict__ scale,
-                                                          const int* __restrict__ pair_token, int pairs, int K,
+                                                          const int* __restrict__ pair_token,
+                                                          const int* __restrict__ pairs, int K,
                                                           __half* __restrict__ x16g, float* __restrict__ scale_g) {
     griddep_wait();
     griddep_launch_dependents();
     const int p = blockIdx.x;
-    if (p >= pairs) return;
+    if (p >= *pairs) return;
     const int t = pair_token[p];
     const uint4* src = reinterpret_cast<const uint4*>(x16 + (int64_t)t * K);
     uint4* dst = reinterpret_cast<uint4*>(x16g + (int64_t)p * K);
@@ -258,12 +272,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restri
 // (g(2j) g(2j+1) u(2j) u(2j+1)), then FP16 with a per-row power-of-two scale
 // (as x_to_f16_kernel) for the down GEMM.  I <= 1024.
 __global__ void __launch_bounds__(256) swiglu_f16_kernel(const float* __restrict__ gu, const float* __restrict__ pw,
-                                                         int pairs, int I, __half* __restrict__ h16,
-                                                         float* __restrict__ scale) {
+                                                         const int* __restrict__ pairs, int I,
+                                                         __half* __restrict__ h16, float* __restrict__ scale) {
     griddep_wait();
     griddep_launch_dependents();
     const int p = blockIdx.x;
-    if (p >= pairs) return;
+    if (p >= *pairs) return;
     const float* row = gu + (int64_t)p * 2 * I;
     const float wt = pw[p];
     float h[4];
@@ -297,32 +311,47 @@ __global__ void __launch_bounds__(256) swiglu_f16_kernel(const float* __restrict
     }
 }
 
-// hidden[t] += sum over slots s (in slot order) of out[pos[t*S + s]].
+// hidden[t] (+)= sum over the slots s run here (pos >= 0, in slot order) of
+// out[pos[t*S + s]].
 __global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ out, const int* __restrict__ pos,
-                                                          int S, int H, float* __restrict__ hidden) {
+                                                          int S, int H, float* __restrict__ hidden, int accumulate) {
     griddep_wait();
     griddep_launch_dependents();
     const int t = blockIdx.x;
     const int* pt = pos + (int64_t)t * S;
     for (int j = threadIdx.x; j < H; j += blockDim.x) {
         float acc = 0.f;
-        for (int sl = 0; sl < S; ++sl) acc += out[(int64_t)pt[sl] * H + j];
-        hidden[(int64_t)t * H + j] += acc;
+        for (int sl = 0; sl < S; ++sl) {
+            const int p = pt[sl];
+            if (p >= 0) acc += out[(int64_t)p * H + j];
+        }
+        float* h = hidden + (int64_t)t * H + j;
+        *h = accumulate ? *h + acc : acc;
     }
 }
 
 }  // namespace
 
+int router_topk(const float* logits, int experts, int top_k, int T, int e0, int local, int shared_id, int* ids,
+                float* weights, cudaStream_t s) {
+    if (launch_pdl(router_topk_kernel, dim3(T), dim3(32), 0, s, logits, experts, top_k, 1, ids, weights, e0, local,
+                   shared_id) != cudaSuccess)
+        return Q3XK_ECUDA;
+    count_launch();
+    return Q3XK_OK;
+}
+
 int moe_prefill(const MoePrefillArgs& a, cudaStream_t s) {
-    const int T = a.T, S = a.top_k + 1, E1 = a.experts + 1, P = T * S;
+    // router over all experts (+ shared gate); grouping over the local pool
+    const int T = a.T, S = a.top_k + 1, E1 = a.local + 1, P = T * S, R1 = a.experts + 1;
     const int H = a.gate_up->cols, I = a.down->cols;
     if (I > 1024 || a.gate_up->rows != 2 * I || a.down->rows != H) return Q3XK_EUNSUPPORTED;
     // 1. router logits (+ shared gate) for every token, then top-k per token
-    if (launch_pdl(router_batch_kernel, dim3((T + 7) / 8, (E1 + 31) / 32), dim3(256), 0, s,
-                   (const uint8_t*)a.router->data, a.router->row_stride, E1, H, a.x, T, a.logits) != cudaSuccess)
+    if (launch_pdl(router_batch_kernel, dim3((T + 7) / 8, (R1 + 31) / 32), dim3(256), 0, s,
+                   (const uint8_t*)a.router->data, a.router->row_stride, R1, H, a.x, T, a.logits) != cudaSuccess)
         return Q3XK_ECUDA;
     if (launch_pdl(router_topk_kernel, dim3(T), dim3(32), 0, s, (const float*)a.logits, a.experts, a.top_k, 1,
-                   a.ids, a.weights) != cudaSuccess)
+                   a.ids, a.weights, a.e0, a.local, a.shared_id) != cudaSuccess)
         return Q3XK_ECUDA;
     // 2. group the pairs by expert
     const int bn = (int)gemm_grouped_tile_width();
@@ -334,21 +363,22 @@ int moe_prefill(const MoePrefillArgs& a, cudaStream_t s) {
     // 3. FP16 rows per token, gathered per pair
     int st = launch_x_to_f16(a.x, T, H, a.x16, a.scale, s);
     if (st != Q3XK_OK) return st;
+    const int* grouped = a.xoff + E1;  // pairs run on this GPU (device)
     if (launch_pdl(gather_rows_kernel, dim3(P), dim3(256), 0, s, (const __half*)a.x16, (const float*)a.scale,
-                   (const int*)a.pair_token, P, H, a.x16g, a.scale_g) != cudaSuccess)
+                   (const int*)a.pair_token, grouped, H, a.x16g, a.scale_g) != cudaSuccess)
         return Q3XK_ECUDA;
     // 4. gate|up of every pair on its expert, weighted SwiGLU -> FP16, down
     const GemmGroups ggu{E1, a.xoff, a.tile_gu}, gdn{E1, a.xoff, a.tile_dn};
     st = gemm_f16(a.gate_up, a.x16g, a.scale_g, P, a.gu, 0, &ggu, 0, s);
     if (st != Q3XK_OK) return st;
-    if (launch_pdl(swiglu_f16_kernel, dim3(P), dim3(256), 0, s, (const float*)a.gu, (const float*)a.pair_weight, P,
-                   I, a.h16, a.scale_h) != cudaSuccess)
+    if (launch_pdl(swiglu_f16_kernel, dim3(P), dim3(256), 0, s, (const float*)a.gu, (const float*)a.pair_weight,
+                   grouped, I, a.h16, a.scale_h) != cudaSuccess)
         return Q3XK_ECUDA;
     st = gemm_f16(a.down, a.h16, a.scale_h, P, a.out, 0, &gdn, 0, s);
     if (st != Q3XK_OK) return st;
     // 5. add each token's slots into its hidden row, in slot order
     if (launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, s, (const float*)a.out, (const int*)a.pos, S, H,
-                   a.hidden) != cudaSuccess)
+                   a.hidden, a.accumulate) != cudaSuccess)
         return Q3XK_ECUDA;
     count_launch(7);
     return Q3XK_OK;
@@ -366,7 +396,7 @@ int q3xk_router_topk(const float* logits, int experts, int top_k, int with_share
         top_k > 8 || top_k > experts)
         return Q3XK_EINVAL;
     const cudaError_t e = launch_pdl(router_topk_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
-                                     logits, experts, top_k, with_shared ? 1 : 0, ids, weights);
+                                     logits, experts, top_k, with_shared ? 1 : 0, ids, weights, 0, experts, experts);
     if (e != cudaSuccess) return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;

@@ -1,8 +1,10 @@
-// tp.cu -- NCCL, loaded at run time, for the tensor-parallel backend.
+// tp.cu -- NCCL, loaded at run time, and the peer-memory all-reduce for the
+// multi-GPU backend.
 //
-// Row-parallel projections (attention/DeltaNet out, FFN down) leave a partial
-// [T][H] sum on every rank; tp_allreduce_add sums the partials with one
-// ncclAllReduce on the state's stream (capturable in the decode graph) and
+// Row-parallel projections (tensor parallelism: attention/DeltaNet out, FFN
+// down) and the MoE layer (expert parallelism: the slots a rank runs) leave a
+// partial [T][H] sum on every rank; tp_allreduce_add sums the partials with
+// one ncclAllReduce on the state's stream (capturable in the decode graph) and
 // adds the result into the replicated residual stream.
 #include <dlfcn.h>
 

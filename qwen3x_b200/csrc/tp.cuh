@@ -1,4 +1,5 @@
-// tp.cuh -- tensor parallelism across GPUs: the NCCL calls the backend makes.
+// tp.cuh -- tensor and expert parallelism across GPUs: the collectives the
+// backend makes (NCCL, and a peer-memory all-reduce for decode).
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2: the copy torch already
 // loaded, or the path in Q3XK_NCCL_LIBRARY), so libq3xk.so itself does not

@@ -105,6 +105,47 @@ def test_expert_rows_and_segments(cuda, mtype):
     assert (np.abs(y2.cpu().numpy() - acc) / mag).max() <= 1e-5
 
 
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+def test_expert_gathers_skip_negative_ids(cuda, mtype):
+    """Expert parallelism marks the slots run on other GPUs with id -1: their
+    rows are not written (row gather) and their segments add nothing, even
+    when that segment of x holds NaN (segment gather)."""
+    import torch
+
+    E, R, K, S = 6, 128, 512, 5
+    packed = quant.quantize(quant.gaussian((E * R, K), 19, 0.02), mtype)
+    pool = Linear.from_packed(packed, mtype, R, K, experts=E, device=cuda)
+    per = packed.reshape(E, -1)
+    ids = np.array([4, -1, 0, -1, 5], np.int32)
+    x = quant.gaussian(K, 20)
+    y = torch.full((S * R,), 7.0, device=cuda)
+    expert_mv_rows(pool, dev(ids, cuda), S, dev(x, cuda), y)
+    xs = quant.gaussian(S * K, 21)
+    xs[K:2 * K] = np.nan  # a skipped segment is never read as data
+    y2 = torch.full((R,), 3.0, device=cuda)
+    expert_mv_segments(pool, dev(ids, cuda), S, dev(xs, cuda), y2, accumulate=False)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy().reshape(S, R)
+    acc = np.zeros(R)
+    mag = np.zeros(R)
+    for s, e in enumerate(ids):
+        if e < 0:
+            assert (y[s] == 7.0).all()
+            continue
+        ref = oracle.mv(per[e], mtype, R, K, x)
+        assert (np.abs(y[s] - ref) / oracle.magnitude(per[e], mtype, R, K, x)).max() <= 1e-5
+        acc += oracle.mv(per[e], mtype, R, K, xs[s * K:(s + 1) * K])
+        mag += oracle.magnitude(per[e], mtype, R, K, xs[s * K:(s + 1) * K])
+    got = y2.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert (np.abs(got - acc) / mag).max() <= 1e-5
+    # every slot skipped: the output is written as zero
+    none = np.full(S, -1, np.int32)
+    expert_mv_segments(pool, dev(none, cuda), S, dev(xs, cuda), y2, accumulate=False)
+    torch.cuda.synchronize()
+    assert (y2.cpu().numpy() == 0).all()
+
+
 def moe_layer_on_device(cuda, router, gate_up, down, sg, su, sd, ss, p, x):
     """engine.cpp:406-430 composed from the device kernels, shared expert as
     expert `experts` of each pool."""

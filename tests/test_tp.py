@@ -39,9 +39,23 @@ def test_plans_tile_every_dimension(mid, world):
         assert covered(plans, "kv0", "KVH", c.KVH)
 
 
+@pytest.mark.parametrize("mid", [36035, 35091])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_expert_parallel_plans(mid, world):
+    """MoE models: the routed experts tile [0, E) over the ranks; heads,
+    FFN-free dims and the vocabulary stay whole (replicated)."""
+    c = modelfile.CONFIGS[mid]
+    plans = [tp_plan(mid, r, world) for r in range(world)]
+    assert covered(plans, "e0", "experts", c.experts)
+    for p in plans:
+        assert p["experts"] == c.experts // world
+        assert (p["KH"], p["VH"], p["AH"], p["KVH"], p["V"]) == (c.KH, c.VH, c.AH, c.KVH, c.V)
+        assert p["kh0"] == p["vh0"] == p["ah0"] == p["v0"] == 0
+
+
 def test_plan_rejections():
-    with pytest.raises(ValueError, match="MoE"):
-        tp_plan(36035, 0, 2)
+    with pytest.raises(ValueError, match="experts"):
+        tp_plan(35091, 0, 3)  # 16 experts over 3 ranks
     with pytest.raises(ValueError, match="split"):
         tp_plan(27008, 0, 3)
     with pytest.raises(ValueError, match="rank"):

@@ -1,6 +1,7 @@
-"""Tensor-parallel backend on 2 GPUs (one process per GPU, NCCL): the same
-logits and greedy tokens as the single-GPU backend on a seeded test model.
-Needs 2 GPUs; on a 1-GPU box it is skipped (the host-side logic is covered by
+"""Multi-GPU backend on 2 GPUs (one process per GPU, NCCL + peer memory):
+tensor parallelism (dense test model) and expert parallelism (MoE test model)
+give the same logits and greedy tokens as the single-GPU backend.  Needs 2
+GPUs; on a 1-GPU box it is skipped (the host-side logic is covered by
 tests/test_tp.py on CPU)."""
 import os
 
@@ -11,10 +12,10 @@ from qwen3x_b200 import modelfile
 
 pytestmark = pytest.mark.gpu
 
-MID = 9091
-# decode (GEMV path): partial sums of the row-parallel projections are added in
-# another order; prompt (FP16 dequant-GEMM): a rank's K slice gets its own
-# per-token FP16 scale, so rounding differs within the GEMM bar
+# decode (GEMV path): partial sums of the row-parallel projections / of the
+# ranks' experts are added in another order; prompt (FP16 dequant-GEMM): a
+# rank's K slice gets its own per-token FP16 scale, so rounding differs within
+# the GEMM bar
 TOL = {"decode": 1e-4, "prefill": 5e-3}
 
 
@@ -63,7 +64,8 @@ def _tp_rank(rank, world, port, path, out, prompt, steps):
         np.savez(out, **res)
 
 
-def test_tp2_matches_single_gpu(cuda, tmp_path):
+@pytest.mark.parametrize("mid", [9091, 35091], ids=["tensor-parallel", "expert-parallel"])
+def test_tp2_matches_single_gpu(cuda, tmp_path, mid):
     import multiprocessing as mp
     import socket
 
@@ -71,8 +73,8 @@ def test_tp2_matches_single_gpu(cuda, tmp_path):
 
     if torch.cuda.device_count() < 2:
         pytest.skip("tensor parallelism needs 2 GPUs (host-side logic: tests/test_tp.py)")
-    path = modelfile.write_model(tmp_path / "m.bin", modelfile.CONFIGS[MID], seed=5)
-    prompt = np.random.default_rng(8).integers(0, modelfile.CONFIGS[MID].V, 40).astype(np.int32)
+    path = modelfile.write_model(tmp_path / "m.bin", modelfile.CONFIGS[mid], seed=5)
+    prompt = np.random.default_rng(8).integers(0, modelfile.CONFIGS[mid].V, 40).astype(np.int32)
     steps = 24
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
