@@ -78,6 +78,43 @@ __global__ void __launch_bounds__(256) rms_kernel(const float* __restrict__ x, c
     for (int i = threadIdx.x; i < n; i += 256) o[i] = xr[i] * scale * w1[i];
 }
 
+// The same sums in the same order for n <= 256 * PER, with the row held in
+// registers: the norm weights are loaded before the dependency wait, and all
+// of a thread's loads of x are in flight at once (a decode row is one CTA, so
+// its time is load latency).
+template <int PER>
+__global__ void __launch_bounds__(256) rms_reg_kernel(const float* __restrict__ x, const float* __restrict__ w1,
+                                                      int n, float* __restrict__ out) {
+    __shared__ float red[8];
+    const int tid = threadIdx.x;
+    float wv[PER], xv[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = tid + 256 * j;
+        wv[j] = i < n ? __ldg(w1 + i) : 0.f;
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    const float* xr = x + (int64_t)blockIdx.x * n;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = tid + 256 * j;
+        xv[j] = i < n ? xr[i] : 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+        if (tid + 256 * j < n) ss += xv[j] * xv[j];
+    ss = block_sum<256>(ss, red);
+    const float scale = 1.0f / sqrtf(ss / (float)n + kEps);
+    float* o = out + (int64_t)blockIdx.x * n;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int i = tid + 256 * j;
+        if (i < n) o[i] = xv[j] * scale * wv[j];
+    }
+}
+
 // ---- causal conv1d over T tokens with SiLU and history (engine.cpp:264-273).
 // proj[t][c] for c < channels is replaced by the activated conv output.  One
 // thread per channel; KC is the kernel width when known at compile time
@@ -837,7 +874,16 @@ int launch_embed(const q3xk_matrix& m, const int* tokens, int T, float* out, cud
 }
 
 int launch_rms(const float* x, const float* w1, int n, int T, float* out, cudaStream_t s) {
-    if (launch_pdl(rms_kernel, dim3(T), dim3(256), 0, s, x, w1, n, out) != cudaSuccess) return Q3XK_ECUDA;
+    cudaError_t e;
+    if (n <= 256 * 8)
+        e = launch_pdl(rms_reg_kernel<8>, dim3(T), dim3(256), 0, s, x, w1, n, out);
+    else if (n <= 256 * 16)
+        e = launch_pdl(rms_reg_kernel<16>, dim3(T), dim3(256), 0, s, x, w1, n, out);
+    else if (n <= 256 * 24)
+        e = launch_pdl(rms_reg_kernel<24>, dim3(T), dim3(256), 0, s, x, w1, n, out);
+    else
+        e = launch_pdl(rms_kernel, dim3(T), dim3(256), 0, s, x, w1, n, out);
+    if (e != cudaSuccess) return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;
 }
