@@ -163,6 +163,10 @@ Q3XK_API int q3xk_expert_gemv(const q3xk_matrix* w, int expert, const float* x, 
  *   rows:     y[s * pool->rows + r] (+)= W[ids[s]][r] . x          (s < slots)
  *   segments: y[r] (+)= sum_s W[ids[s]][r] . x[s * cols .. (s+1) * cols)
  * `ids` (int32) and x, y are device pointers; slots <= 16 for segments.
+ * An id < 0 skips its slot (expert parallelism: an expert held by another
+ * GPU): rows leaves that slot's y rows untouched and reads none of its
+ * weights; segments adds nothing for it and never reads that segment of x
+ * as data.  With every slot skipped, segments writes y = 0 (or leaves y).
  * Replace expert_gate_up_q4_kernel (rows) and expert_down_weighted_q4_kernel
  * (segments, weights folded into x; engine.cu:1186-1250) and the CPU loop of
  * engine.cpp:412-420.

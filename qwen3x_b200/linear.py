@@ -95,13 +95,15 @@ def expert_mv(linear: Linear, expert: int, x, y, stream=None, accumulate: bool =
 
 
 def expert_mv_rows(pool: Linear, ids, slots: int, x, y, accumulate=False, stream=None) -> None:
-    """y[s*rows + r] (+)= W[ids[s]][r] . x for s < slots; ids on the device."""
+    """y[s*rows + r] (+)= W[ids[s]][r] . x for s < slots; ids on the device
+    (an id < 0 skips its slot: those rows of y are left as they are)."""
     check(lib().q3xk_expert_gemv_rows(ctypes.byref(pool.m), ptr(ids), int(slots), ptr(x), ptr(y),
                                       int(accumulate), stream_ptr(stream)), "q3xk_expert_gemv_rows")
 
 
 def expert_mv_segments(pool: Linear, ids, slots: int, x, y, accumulate=False, stream=None) -> None:
-    """y[r] (+)= sum_s W[ids[s]][r] . x[s*cols:(s+1)*cols]; ids on the device."""
+    """y[r] (+)= sum_s W[ids[s]][r] . x[s*cols:(s+1)*cols]; ids on the device
+    (an id < 0 skips its segment)."""
     check(lib().q3xk_expert_gemv_segments(ctypes.byref(pool.m), ptr(ids), int(slots), ptr(x), ptr(y),
                                           int(accumulate), stream_ptr(stream)),
           "q3xk_expert_gemv_segments")
