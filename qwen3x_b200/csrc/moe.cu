@@ -169,33 +169,72 @@ constexpr int kArgmaxParts = 148;
 
 // ---- MoE over a prompt: routing for all tokens, grouping by expert ------------
 
-// logits[t][e] = router row e . x_t for T tokens (BF16 row records, FP32 sums);
-// CTA = 8 tokens (one per warp) x 32 router rows.
-__global__ void __launch_bounds__(256) router_batch_kernel(const uint8_t* __restrict__ w, int64_t row_stride,
-                                                           int rows, int H, const float* __restrict__ x, int T,
-                                                           float* __restrict__ logits) {
+// logits[t][e] = router row e . x_t for T tokens (BF16 row records, FP32):
+// a register-tiled FP32 GEMM on CUDA cores.  CTA = 64 tokens x 64 router rows,
+// 256 threads with 4 x 4 outputs each; K in steps of 32 staged in shared
+// memory, transposed ([k][token], [k][row]), BF16 widened to FP32.  Each
+// output is one fmaf chain over k in ascending order.
+constexpr int kRtT = 64, kRtE = 64, kRtK = 32, kRtPad = 4;
+
+__global__ void __launch_bounds__(256) router_gemm_kernel(const uint8_t* __restrict__ w, int64_t row_stride,
+                                                          int rows, int H, const float* __restrict__ x, int T,
+                                                          float* __restrict__ logits) {
+    __shared__ __align__(16) float xs[kRtK][kRtT + kRtPad];
+    __shared__ __align__(16) float ws[kRtK][kRtE + kRtPad];
     griddep_wait();
     griddep_launch_dependents();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 8 + warp;
-    if (t >= T) return;
-    const float* xt = x + (int64_t)t * H;
-    for (int j = 0; j < 32; ++j) {
-        const int e = blockIdx.y * 32 + j;
-        if (e >= rows) break;
-        const uint16_t* wr = reinterpret_cast<const uint16_t*>(w + (int64_t)e * row_stride);
-        float acc = 0.f;
-        for (int k = lane * 8; k < H; k += 256) {
-            const uint4 q = *reinterpret_cast<const uint4*>(wr + k);
-            const float4 x0 = *reinterpret_cast<const float4*>(xt + k);
-            const float4 x1 = *reinterpret_cast<const float4*>(xt + k + 4);
-            acc += __uint_as_float(q.x << 16) * x0.x + __uint_as_float(q.x & 0xFFFF0000u) * x0.y +
-                   __uint_as_float(q.y << 16) * x0.z + __uint_as_float(q.y & 0xFFFF0000u) * x0.w +
-                   __uint_as_float(q.z << 16) * x1.x + __uint_as_float(q.z & 0xFFFF0000u) * x1.y +
-                   __uint_as_float(q.w << 16) * x1.z + __uint_as_float(q.w & 0xFFFF0000u) * x1.w;
+    const int t0 = blockIdx.x * kRtT, e0 = blockIdx.y * kRtE;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;  // rows 4tx.., tokens 4ty..
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < H; k0 += kRtK) {
+#pragma unroll
+        for (int r = 0; r < kRtT * kRtK / 4 / 256; ++r) {  // 64 tokens x 8 float4
+            const int i = tid + 256 * r, tt = i >> 3, kq = i & 7;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + tt < T) v = *reinterpret_cast<const float4*>(x + (int64_t)(t0 + tt) * H + k0 + 4 * kq);
+            xs[4 * kq][tt] = v.x;
+            xs[4 * kq + 1][tt] = v.y;
+            xs[4 * kq + 2][tt] = v.z;
+            xs[4 * kq + 3][tt] = v.w;
         }
-        acc = warp_sum(acc);
-        if (lane == 0) logits[(int64_t)t * rows + e] = acc;
+        {  // 64 rows x 4 uint4 (8 BF16 each)
+            const int ee = tid >> 2, kq = tid & 3;
+            uint4 q = make_uint4(0u, 0u, 0u, 0u);
+            if (e0 + ee < rows)
+                q = __ldg(reinterpret_cast<const uint4*>(w + (int64_t)(e0 + ee) * row_stride + (k0 + 8 * kq) * 2));
+            const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                ws[8 * kq + 2 * c][ee] = __uint_as_float(u[c] << 16);
+                ws[8 * kq + 2 * c + 1][ee] = __uint_as_float(u[c] & 0xFFFF0000u);
+            }
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kRtK; ++k) {
+            const float4 a = *reinterpret_cast<const float4*>(&xs[k][4 * ty]);
+            const float4 b = *reinterpret_cast<const float4*>(&ws[k][4 * tx]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + 4 * ty + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + 4 * tx + j;
+            if (e < rows) logits[(int64_t)t * rows + e] = acc[i][j];
+        }
     }
 }
 
@@ -347,7 +386,8 @@ int moe_prefill(const MoePrefillArgs& a, cudaStream_t s) {
     const int H = a.gate_up->cols, I = a.down->cols;
     if (I > 1024 || a.gate_up->rows != 2 * I || a.down->rows != H) return Q3XK_EUNSUPPORTED;
     // 1. router logits (+ shared gate) for every token, then top-k per token
-    if (launch_pdl(router_batch_kernel, dim3((T + 7) / 8, (R1 + 31) / 32), dim3(256), 0, s,
+    if (H % kRtK || (a.router->row_stride & 15)) return Q3XK_EUNSUPPORTED;
+    if (launch_pdl(router_gemm_kernel, dim3((T + kRtT - 1) / kRtT, (R1 + kRtE - 1) / kRtE), dim3(256), 0, s,
                    (const uint8_t*)a.router->data, a.router->row_stride, R1, H, a.x, T, a.logits) != cudaSuccess)
         return Q3XK_ECUDA;
     if (launch_pdl(router_topk_kernel, dim3(T), dim3(32), 0, s, (const float*)a.logits, a.experts, a.top_k, 1,
