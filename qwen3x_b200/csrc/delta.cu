@@ -14,7 +14,8 @@
 //   delta_prep  one CTA per (chunk, head), all chunks in parallel: q/k
 //               l2-norms, beta, G, A, U', W, M = tril(Q K^T o Gam), Q~, K~;
 //   delta_scan  one CTA per (head, 32-column block of S), chunks in order:
-//               U = U' - W S, O = Q~ S + M U, S = exp(G_C) S + K~^T U.
+//               U = U' - W S, O = Q~ S + M U, S = exp(G_C) S + K~^T U,
+//               the next chunk's blocks loading (cp.async) meanwhile.
 // The output is the raw o; gated_rms_kernel applies the gated RMS after.
 #include "layers.cuh"
 
@@ -162,18 +163,36 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const float* __restrict
 }
 
 // ---- scan: one CTA per (head, 32-column block), chunks in order ----------------
-// Register tiles: U and O as 4 rows x 2 columns per thread, S as 4 x 4.
+// Register tiles: U and O as 4 rows x 2 columns per thread, S as 4 x 4.  The
+// chunk blocks stream in with cp.async: W^T, Q~^T and M^T of chunk c + 1 are in
+// flight while chunk c computes (two buffers each), and K~ of chunk c while its
+// U and O phases run.
+__device__ __forceinline__ void cp_async16(float* smem, const float* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void copy_async(float* dst, const float* src, int n4) {
+    for (int e = threadIdx.x; e < n4; e += 256) cp_async16(dst + 4 * e, src + 4 * e);
+}
+
 __global__ void __launch_bounds__(256) delta_scan_kernel(const float* __restrict__ work, int T,
                                                          float* __restrict__ state /*[VH][KD][VD]*/,
                                                          float* __restrict__ out, int64_t out_stride) {
     griddep_wait();
     griddep_launch_dependents();
     extern __shared__ __align__(16) float sm[];
-    float* S = sm;               // [kD][kCols]
-    float* U = S + kD * kCols;   // [kC][kCols]
-    float* A1 = U + kC * kCols;  // W^T [kD][kC], then K~ [kC][kD]
-    float* A2 = A1 + kC * kD;    // Q~^T [kD][kC]
-    float* Ms = A2 + kC * kD;    // M^T [kC][kC]
+    float* S = sm;                       // [kD][kCols]
+    float* U = S + kD * kCols;           // [kC][kCols]
+    float* Kb = U + kC * kCols;          // K~ [kC][kD] of the current chunk
+    float* Wbase = Kb + kC * kD;         // W^T [kD][kC], two buffers
+    float* Qbase = Wbase + 2 * kC * kD;  // Q~^T [kD][kC], two buffers
+    float* Mbase = Qbase + 2 * kC * kD;  // M^T [kC][kC], two buffers
     const int head = blockIdx.x, cb = blockIdx.y;
     const int nchunks = (T + kC - 1) / kC;
     const int tid = threadIdx.x;
@@ -181,18 +200,28 @@ __global__ void __launch_bounds__(256) delta_scan_kernel(const float* __restrict
     const int r0 = 4 * (tid & 31), c4 = 4 * (tid >> 5);  // S tile
     float* st = state + (int64_t)head * kD * kD + cb * kCols;
     for (int e = tid; e < kD * kCols; e += 256) S[e] = st[(e / kCols) * kD + e % kCols];
-
-    auto stage = [&](float* dst, const float* src, int n4) {
-        for (int e = tid; e < n4; e += 256) reinterpret_cast<float4*>(dst)[e] = reinterpret_cast<const float4*>(src)[e];
+    auto block_of = [&](int chunk) { return work + ((int64_t)head * nchunks + chunk) * kBlockFloats; };
+    auto issue_wqm = [&](int chunk, int par) {
+        const float* blk = block_of(chunk);
+        copy_async(Wbase + par * kC * kD, blk + kOffWT, kC * kD / 4);
+        copy_async(Qbase + par * kC * kD, blk + kOffQT, kC * kD / 4);
+        copy_async(Mbase + par * kC * kC, blk + kOffMT, kC * kC / 4);
     };
+    issue_wqm(0, 0);
+    cp_async_commit();
+
     for (int chunk = 0; chunk < nchunks; ++chunk) {
-        const float* blk = work + ((int64_t)head * nchunks + chunk) * kBlockFloats;
-        const int t0 = chunk * kC, n = min(kC, T - t0);
-        __syncthreads();  // S final for this chunk; A1/A2/Ms free
-        stage(A1, blk + kOffWT, kC * kD / 4);
-        stage(A2, blk + kOffQT, kC * kD / 4);
-        stage(Ms, blk + kOffMT, kC * kC / 4);
-        __syncthreads();
+        const float* blk = block_of(chunk);
+        const int par = chunk & 1, t0 = chunk * kC, n = min(kC, T - t0);
+        const float* A1 = Wbase + par * kC * kD;
+        const float* A2 = Qbase + par * kC * kD;
+        const float* Ms = Mbase + par * kC * kC;
+        cp_async_wait<0>();  // this chunk's W^T, Q~^T, M^T have landed
+        __syncthreads();     // ... for every thread; the previous chunk is done with Kb and the other buffers
+        copy_async(Kb, blk + kOffK, kC * kD / 4);
+        cp_async_commit();
+        if (chunk + 1 < nchunks) issue_wqm(chunk + 1, par ^ 1);
+        cp_async_commit();
         // U = U' - W S
         float u[4][2];
 #pragma unroll
@@ -238,8 +267,7 @@ __global__ void __launch_bounds__(256) delta_scan_kernel(const float* __restrict
             if (i0 + a < n)
                 *reinterpret_cast<float2*>(out + (int64_t)(t0 + i0 + a) * out_stride + head * kD + cb * kCols + c0) =
                     make_float2(o[a][0], o[a][1]);
-        __syncthreads();  // W^T no longer needed
-        stage(A1, blk + kOffK, kC * kD / 4);
+        cp_async_wait<1>();  // K~ of this chunk has landed (the next chunk's blocks may still be in flight)
         __syncthreads();
         // S = gamma S + K~^T U
         const float gam = blk[kOffGamma];
@@ -251,7 +279,7 @@ __global__ void __launch_bounds__(256) delta_scan_kernel(const float* __restrict
         }
 #pragma unroll 4
         for (int j = 0; j < kC; ++j) {
-            const float4 kk = *reinterpret_cast<const float4*>(A1 + j * kD + r0);
+            const float4 kk = *reinterpret_cast<const float4*>(Kb + j * kD + r0);
             const float4 uv = *reinterpret_cast<const float4*>(U + j * kCols + c4);
             const float kr[4] = {kk.x, kk.y, kk.z, kk.w};
 #pragma unroll
@@ -266,6 +294,7 @@ __global__ void __launch_bounds__(256) delta_scan_kernel(const float* __restrict
             *reinterpret_cast<float4*>(S + (r0 + a) * kCols + c4) =
                 make_float4(sacc[a][0], sacc[a][1], sacc[a][2], sacc[a][3]);
     }
+    cp_async_wait<0>();
     __syncthreads();
     for (int e = tid; e < kD * kCols; e += 256) st[(e / kCols) * kD + e % kCols] = S[e];
 }
@@ -298,7 +327,8 @@ __global__ void __launch_bounds__(256) gated_rms_kernel(float* __restrict__ out,
 }
 
 constexpr size_t kPrepSmem = (size_t)(3 * kC * kLd + kC * (kC + 1) + 3 * kC) * 4;
-constexpr size_t kScanSmem = (size_t)(kD * kCols + kC * kCols + 2 * kC * kD + kC * kC) * 4;
+constexpr size_t kScanSmem = (size_t)(kD * kCols + kC * kCols + 5 * kC * kD + 2 * kC * kC) * 4;  // 216 KB
+static_assert(kScanSmem <= 227 * 1024, "scan shared memory");
 
 }  // namespace
 
