@@ -619,9 +619,9 @@ def main(argv=None):
         peak_tf = measured_tflops()
         for mtype, name in ((1, "q8_0"), (2, "q4_0")):
             for T in (1, 8, 64, 512, 4096):
-                secs = time_gemm(mtype, T, 10 if T >= 512 else 50, device, world)
-                tf = world * 2 * T * ROWS * COLS / secs / 1e12
-                gemm[f"{name}_T{T}"] = {"us": round(secs * 1e6, 1), "tflops": round(tf, 1),
+                gemm_secs = time_gemm(mtype, T, 10 if T >= 512 else 50, device, world)
+                tf = world * 2 * T * ROWS * COLS / gemm_secs / 1e12
+                gemm[f"{name}_T{T}"] = {"us": round(gemm_secs * 1e6, 1), "tflops": round(tf, 1),
                                         "frac_of_bf16_peak": round(tf / world / peak_tf[0], 4)}
         gemm["peak_tflops"] = peak_tf[0]
         gemm["peak_kind"] = peak_tf[1]
