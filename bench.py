@@ -266,9 +266,10 @@ def time_e2e(mtype: int, steps: int, warmup: int, device, world: int):
     return secs, {"h2d_bytes_per_step": COPIES * COLS * 4, "d2h_bytes_per_step": COPIES * ROWS * 4}
 
 
-def time_gemm(mtype: int, T: int, reps: int, device, world: int):
-    """Prefill dequant-GEMM Y[T, 12288] = X[T, 4096] W^T (BASELINE config 2);
-    returns (seconds per call, max over ranks)."""
+def time_gemm(mtype: int, T: int, reps: int, device, world: int, precision=None):
+    """Prefill dequant-GEMM Y[T, 12288] = X[T, 4096] W^T at
+    `precision` (None = q3xk_gemm's split default); returns seconds per call,
+    max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -281,14 +282,14 @@ def time_gemm(mtype: int, T: int, reps: int, device, world: int):
     Y = torch.empty(T, ROWS, device=device)
     ws = torch.empty(gemm_workspace_bytes(T, COLS), dtype=torch.uint8, device=device)
     for _ in range(3):
-        batch_mv(lin, X, Y, workspace=ws)
+        batch_mv(lin, X, Y, workspace=ws, precision=precision)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(reps):
-        batch_mv(lin, X, Y, workspace=ws)
+        batch_mv(lin, X, Y, workspace=ws, precision=precision)
     end.record()
     torch.cuda.synchronize()
     secs = start.elapsed_time(end) / 1e3 / reps
@@ -572,11 +573,12 @@ def main(argv=None):
     rank, world, local = dist_setup(args.gpus)
     device = torch.device("cuda", torch.cuda.current_device())
     if args.only == "gemm":
-        for mtype in (1, 2):
-            secs = time_gemm(mtype, 4096, max(args.steps, 1), device, world)
-            if rank == 0:
-                print(f"gemm type={mtype} T=4096: {secs * 1e6:.1f} us "
-                      f"{2 * 4096 * ROWS * COLS / secs / 1e12:.1f} TFLOP/s", flush=True)
+        for precision, pname in ((None, "split"), (capi.GEMM_FP16, "fp16")):
+            for mtype in (1, 2):
+                secs = time_gemm(mtype, 4096, max(args.steps, 1), device, world, precision)
+                if rank == 0:
+                    print(f"gemm {pname} type={mtype} T=4096: {secs * 1e6:.1f} us "
+                          f"{2 * 4096 * ROWS * COLS / secs / 1e12:.1f} TFLOP/s", flush=True)
         return 0
 
     prompts = {9000: 4096, 36035: 2048, 27008: 16384}  # BASELINE configs 3, 4, 5
@@ -617,12 +619,13 @@ def main(argv=None):
     gemm = {}
     if args.only is None:
         peak_tf = measured_tflops()
-        for mtype, name in ((1, "q8_0"), (2, "q4_0")):
-            for T in (1, 8, 64, 512, 4096):
-                gemm_secs = time_gemm(mtype, T, 10 if T >= 512 else 50, device, world)
-                tf = world * 2 * T * ROWS * COLS / gemm_secs / 1e12
-                gemm[f"{name}_T{T}"] = {"us": round(gemm_secs * 1e6, 1), "tflops": round(tf, 1),
-                                        "frac_of_bf16_peak": round(tf / world / peak_tf[0], 4)}
+        for precision, suffix in ((None, ""), (capi.GEMM_FP16, "_fp16")):
+            for mtype, name in ((1, "q8_0"), (2, "q4_0")):
+                for T in (1, 8, 64, 512, 4096):
+                    gemm_secs = time_gemm(mtype, T, 10 if T >= 512 else 50, device, world, precision)
+                    tf = world * 2 * T * ROWS * COLS / gemm_secs / 1e12
+                    gemm[f"{name}{suffix}_T{T}"] = {"us": round(gemm_secs * 1e6, 1), "tflops": round(tf, 1),
+                                                    "frac_of_bf16_peak": round(tf / world / peak_tf[0], 4)}
         gemm["peak_tflops"] = peak_tf[0]
         gemm["peak_kind"] = peak_tf[1]
 
@@ -659,7 +662,9 @@ def main(argv=None):
                               "frac": round(q4_achieved / peak, 4),
                               "bytes_per_launch": q4_bytes},
                 "gemm_cfg2": dict(gemm, workload="cfg2: Y[T,12288] = X[T,4096] W^T, dequant-GEMM on "
-                                                  "tcgen05 (FP16 x FP16 -> FP32), T sweep"),
+                                                  "tcgen05, T sweep; q8_0_T*/q4_0_T*: split precision "
+                                                  "(default: hi+lo FP16 planes of X and d*q, 3 MMAs per "
+                                                  "K-step, FP32-grade); *_fp16_T*: FP16 operands, 1 MMA"),
                 "engine_9b": engine,
             },
         }

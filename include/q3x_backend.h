@@ -90,8 +90,12 @@ Q3XK_API void* q3xb_state_stream(const q3xb_state* state);
 Q3XK_API int q3xb_state_set_graphs(q3xb_state* state, int enabled);
 /* 1 = prompts (count > 1) run every matrix through the CUDA-core GEMV, one
  * token at a time, with the decode path's FP32 accuracy; 0 (default) = the
- * tcgen05 dequant-GEMM with FP16 operands. */
+ * tcgen05 dequant-GEMM. */
 Q3XK_API int q3xb_state_set_exact_prefill(q3xb_state* state, int enabled);
+/* Precision of the prompt GEMMs (q3xk.h): Q3XK_GEMM_SPLIT (default; split
+ * FP16 operands, FP32-grade logits) or Q3XK_GEMM_FP16 (one FP16 MMA per
+ * K-step: faster, logits within ~3e-3). */
+Q3XK_API int q3xb_state_set_prefill_precision(q3xb_state* state, int precision);
 /* Tokens per forward pass of a prompt, 1..min(context, 2048) (the default is
  * the maximum; the work buffers are sized for it at state creation). */
 Q3XK_API int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens);
@@ -122,8 +126,17 @@ Q3XK_API q3xb_state* q3xb_state_create_tp(q3xb_model* model, int context_size, c
  * Without this step the state uses NCCL for every all-reduce. */
 Q3XK_API int q3xb_state_ipc_handle(const q3xb_state* state, char* handle64);
 Q3XK_API int q3xb_state_ipc_open(q3xb_state* state, const char* handles_world_x_64);
-/* 1 if a peer all-reduce gave up waiting for a peer (~1 s), else 0. */
+/* 1 if a peer all-reduce gave up waiting for a peer, else 0 (synchronous).
+ * A rank whose wait ran out is out of step with its peers for good: its
+ * later all-reduces return at once, and state_forward, state_argmax,
+ * state_copy_logits and q3xb_state_synchronize report Q3XK_ETIMEOUT (the C++
+ * q3x_backend calls abort, as the reference's Q3X_ASSERT does) -- from the
+ * first of them that runs after the failed step's work has finished. */
 Q3XK_API int q3xb_state_tp_error(const q3xb_state* state, int* flags);
+/* Bound of the peer all-reduce's wait for a peer, in seconds (0 < s <= 60,
+ * default 1).  Set it before the first decode step: the captured decode
+ * graph keeps the bound it was made with (Q3XK_EUNSUPPORTED afterwards). */
+Q3XK_API int q3xb_state_set_peer_timeout(q3xb_state* state, double seconds);
 /* The rank's share: rank, world, first key/value/query/KV head, first
  * intermediate row, first vocabulary row, the local KH, VH, AH, KVH, I, V,
  * then the first routed expert and the local routed-expert count (MoE). */

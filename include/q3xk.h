@@ -201,16 +201,26 @@ Q3XK_API int q3xk_argmax(const float* values, int n, int* out_index, void* works
 /*
  * Prefill dequant-GEMM on tcgen05: Y[T, rows] = X[T, cols] W^T (accumulate =
  * 0) or Y += X W^T, all row-major FP32 (Y[t][r] at t * rows + r).  Q8_0/Q4_0
- * only; cols % 32 == 0.  X is rounded to FP16 with a per-token power-of-two
- * scale, W to FP16 (d*q), FP32 accumulation; error within 2e-3 of
- * sum_k |w x| (measured ~1e-4).  `workspace` is a caller-owned DEVICE buffer
- * of q3xk_gemm_workspace_bytes(T, cols) bytes, 256-byte aligned.
+ * only; cols % 32 == 0.  FP32 accumulation in tensor memory; X is scaled per
+ * token by a power of two.  Two precisions:
+ *   Q3XK_GEMM_SPLIT (q3xk_gemm's): X and d*q each as two FP16 planes (hi +
+ *     residual; d*q is split exactly), three MMAs per K-step: FP32-grade,
+ *     error ~1e-7 of sum_k |w x|.
+ *   Q3XK_GEMM_FP16: X and d*q rounded to FP16, one MMA per K-step: error
+ *     ~1e-4 of sum_k |w x|, about 1.5x the throughput.
+ * `workspace` is a caller-owned DEVICE buffer of
+ * q3xk_gemm_workspace_bytes(T, cols) bytes, 256-byte aligned (either
+ * precision).
  * Replaces engine.cu:1568-1597 batch_mv (batch_mv_q8_kernel, engine.cu:751-
  * 839) and adds the Q4_0 prefill the reference asserts on (engine.cu:1580).
  */
+#define Q3XK_GEMM_SPLIT 0
+#define Q3XK_GEMM_FP16 1
 Q3XK_API int q3xk_gemm_workspace_bytes(int T, int cols, size_t* bytes);
 Q3XK_API int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate,
                        void* workspace, size_t workspace_bytes, void* stream);
+Q3XK_API int q3xk_gemm_ex(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate,
+                          int precision, void* workspace, size_t workspace_bytes, void* stream);
 /* Device error word of the GEMM kernels (bit 0: a bounded wait gave up). */
 Q3XK_API int q3xk_gemm_device_error(int* flags);
 
@@ -237,7 +247,9 @@ Q3XK_API int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* 
  * device: cols rounded up to 4, plus rows, must not exceed 1048576 floats,
  * otherwise Q3XK_EWORKSPACE is returned before any CUDA call.  The first call
  * on a device (the current one) looks the array's address up with
- * cudaGetSymbolAddress; make it before any stream capture.  The array is
+ * cudaGetSymbolAddress; make it before any stream capture.  The address is
+ * kept per device and CUDA context: after cudaDeviceReset (a new context) the
+ * next call looks it up again.  The array is
  * shared: calls whose work overlaps on the GPU (other streams or host threads
  * on the same device) race on it, so run them one at a time.  Nothing in it
  * needs to start at zero: each call overwrites the x and y it reads.
@@ -246,14 +258,34 @@ Q3XK_API int q3xk_try_mv_host_noalloc(const q3xk_matrix* w, const float* x_host,
                                       void* stream);
 
 /*
- * Device-side error word of the current device: bit 0 = a producer gave up
- * waiting for a free stage, bit 1 = a consumer gave up waiting for data.
- * Every device-side wait in these kernels is bounded (about one second);
- * on a timeout the kernel sets a bit, lets its own in-flight copies land and
- * returns, so the context stays usable.  Reading synchronises the device.
+ * Device-side error word of the current device: bit 0 = a wait inside the
+ * dequant-GEMM's pipeline (TMA producer, dequantisers, MMA issuer or
+ * epilogue, each on an mbarrier) gave up.  The GEMVs have no device-side
+ * waits.  Every such wait is bounded (about one second); on a timeout the
+ * kernel sets the bit and its CTA leaves its tile loop, so the context stays
+ * usable.  Reading synchronises the device; clearing resets the word.
+ * (The peer all-reduce has an error word per State: q3xb_state_tp_error.)
  */
 Q3XK_API int q3xk_device_error(int* flags);
 Q3XK_API int q3xk_clear_device_error(void);
+
+/*
+ * One-shot all-reduce of a short vector over peer memory (decode-sized:
+ * n <= 5120 floats, up to 8 ranks), the collective of the multi-GPU backend's
+ * decode step: y[0..n) += the sum over ranks of partial[0..n), added in rank
+ * order, so every rank gets bit-identical results.  bases[r] = rank r's
+ * buffer of q3xk_peer_buffer_bytes(n_max) bytes (this rank's own one, zeroed
+ * before first use, and the peers' mapped with CUDA IPC); seq = a device int,
+ * zero at first, advanced by each call; err = a device int.  Each rank waits
+ * for the others' flags at most timeout_s seconds (0 < timeout_s <= 60);
+ * then it sets *err = 1, leaves y alone and returns, and every later call
+ * with *err set returns at once.  No counterpart in the reference
+ * (single-GPU backends only).
+ */
+Q3XK_API size_t q3xk_peer_buffer_bytes(int n_max);
+Q3XK_API int q3xk_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, int* seq,
+                                     const float* partial, float* y, int n, int* err, double timeout_s,
+                                     void* stream);
 
 /* Number of kernel launches the calls above made since the last reset
  * (host-side counter used by the benchmark's gpu_launches report). */

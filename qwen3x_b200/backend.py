@@ -153,6 +153,15 @@ class State:
         capi.check(self.lib.q3xb_state_set_exact_prefill(self.handle, int(enabled)),
                    "state_set_exact_prefill")
 
+    def set_peer_timeout(self, seconds: float):
+        """Bound of the decode all-reduce's wait for a peer (before the first decode step)."""
+        capi.check(self.lib.q3xb_state_set_peer_timeout(self.handle, float(seconds)), "state_set_peer_timeout")
+
+    def set_prefill_precision(self, precision: int):
+        """capi.GEMM_SPLIT (default) or capi.GEMM_FP16 for the prompt GEMMs."""
+        capi.check(self.lib.q3xb_state_set_prefill_precision(self.handle, int(precision)),
+                   "state_set_prefill_precision")
+
     def set_prefill_chunk(self, tokens: int):
         capi.check(self.lib.q3xb_state_set_prefill_chunk(self.handle, int(tokens)),
                    "state_set_prefill_chunk")

@@ -16,6 +16,8 @@ OK, EINVAL, EUNSUPPORTED, ECUDA, EALIGN, ETIMEOUT, EWORKSPACE = range(7)
 # q3xk_matrix_type == q3x_model::MatrixType (model_config.h:16-20)
 BF16, Q8_0, Q4_0 = 0, 1, 2
 TYPE_NAMES = {BF16: "BF16", Q8_0: "Q8_0", Q4_0: "Q4_0"}
+# q3xk_gemm_ex precisions (include/q3xk.h)
+GEMM_SPLIT, GEMM_FP16 = 0, 1
 
 
 class Matrix(ctypes.Structure):
@@ -98,8 +100,15 @@ _SIGNATURES = {
     "q3xk_gemm": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
                                  ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
                                  ctypes.c_void_p]),
+    "q3xk_gemm_ex": (ctypes.c_int, [ctypes.POINTER(Matrix), ctypes.c_void_p, ctypes.c_int,
+                                    ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                    ctypes.c_size_t, ctypes.c_void_p]),
     "q3xk_gemm_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "q3xk_device_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "q3xk_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int]),
+    "q3xk_peer_allreduce_add": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                               ctypes.c_void_p, ctypes.c_double, ctypes.c_void_p]),
     "q3xk_clear_device_error": (ctypes.c_int, []),
     "q3xk_launch_count": (ctypes.c_uint64, []),
     "q3xk_reset_launch_count": (None, []),
@@ -125,6 +134,7 @@ _SIGNATURES = {
     "q3xb_state_set_graphs": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "q3xb_state_set_exact_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "q3xb_state_set_prefill_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "q3xb_state_set_prefill_precision": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "q3xb_model_create_tp": (ctypes.c_void_p, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p,
                                                ctypes.c_size_t]),
     "q3xb_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
@@ -134,6 +144,7 @@ _SIGNATURES = {
     "q3xb_state_ipc_handle": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
     "q3xb_state_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
     "q3xb_state_tp_error": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "q3xb_state_set_peer_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_double]),
     "q3xb_tp_plan": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                     ctypes.c_char_p, ctypes.c_size_t]),
 }

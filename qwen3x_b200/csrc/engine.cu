@@ -261,8 +261,11 @@ struct State {
     bool peer_ready = false;       // decode all-reduces go over peer memory
     int* peer_seq = nullptr;       // call counter of the peer all-reduce
     int* tp_err = nullptr;         // set by a peer all-reduce that gave up waiting
+    int* tp_err_host = nullptr;    // pinned copy of tp_err, refreshed after every forward
+    double peer_timeout_s = 1.0;   // bound of the peer all-reduce's wait for a peer
     bool use_graphs = true;
-    bool exact_prefill = false;  // T > 1 through per-token GEMVs instead of the FP16 GEMM
+    bool exact_prefill = false;  // T > 1 through per-token GEMVs instead of the GEMM
+    int gemm_precision = Q3XK_GEMM_SPLIT;  // prompt GEMMs: split (FP32-grade) or FP16
     int chunk = 0;               // tokens per forward pass (work buffers hold `chunk_capacity`)
     int chunk_capacity = 0;
     cudaGraph_t graph = nullptr;
@@ -277,6 +280,7 @@ struct State {
         for (int r = 0; r < world && r < 8; ++r)
             if (peer_ready && r != rank && peer_bases[r]) cudaIpcCloseMemHandle(peer_bases[r]);
         for (void* p : allocations) cudaFree(p);
+        if (tp_err_host) cudaFreeHost(tp_err_host);
         tp_comm_destroy(comm);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -643,7 +647,7 @@ int mm(State& s, const q3xk_matrix& w, const float* X, int T, float* Y, int accu
             Q3XB_TRY(q3xk_gemv(&w, X + (size_t)t * w.cols, Y + (size_t)t * w.rows, accumulate, s.stream));
         return Q3XK_OK;
     }
-    return q3xk_gemm(&w, X, T, Y, accumulate, s.gemm_ws, s.gemm_ws_bytes, s.stream);
+    return q3xk_gemm_ex(&w, X, T, Y, accumulate, s.gemm_precision, s.gemm_ws, s.gemm_ws_bytes, s.stream);
 }
 
 q3xk_xform rms_xf(const float* w1) {
@@ -684,7 +688,7 @@ int allreduce_add(State& s, float* y, int T) {
     const int H = s.c->H;
     if (T == 1 && s.peer_ready)
         return tp_peer_allreduce_add(s.peer_bases, s.rank, s.world, H, s.peer_seq, s.partial, y, H, s.tp_err,
-                                     s.stream);
+                                     s.peer_timeout_s, s.stream);
     return tp_allreduce_add(s.comm, s.partial, y, (int64_t)T * H, s.stream);
 }
 
@@ -837,6 +841,7 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
             a.x = s.normed;
             a.hidden = s.ep ? s.partial : s.hidden;
             a.accumulate = s.ep ? 0 : 1;
+            a.split = s.gemm_precision == Q3XK_GEMM_SPLIT;
             Q3XB_TRY(moe_prefill(a, st));
             if (s.ep) Q3XB_TRY(allreduce_add(s, s.hidden, T));
         } else if (c.experts) {
@@ -935,8 +940,9 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
         ok = s->alloc(&a.logits, (size_t)chunk * E1) && s->alloc(&a.ids, P) && s->alloc(&a.weights, P) &&
              s->alloc(&a.xoff, E1 + 1) && s->alloc(&a.tile_gu, E1 + 1) && s->alloc(&a.tile_dn, E1 + 1) &&
              s->alloc(&a.pos, P) && s->alloc(&a.pair_token, P) && s->alloc(&a.pair_weight, P) &&
-             s->alloc(&a.x16, (size_t)chunk * c.H) && s->alloc(&a.scale, chunk) && s->alloc(&a.x16g, P * c.H) &&
-             s->alloc(&a.scale_g, P) && s->alloc(&a.gu, P * 2 * c.I) && s->alloc(&a.h16, P * c.I) &&
+             s->alloc(&a.x16, 2 * (size_t)chunk * c.H) && s->alloc(&a.scale, chunk) &&
+             s->alloc(&a.x16g, 2 * P * c.H) && s->alloc(&a.scale_g, P) && s->alloc(&a.gu, P * 2 * c.I) &&
+             s->alloc(&a.h16, 2 * P * c.I) &&
              s->alloc(&a.scale_h, P) && s->alloc(&a.out, P * c.H);
     }
     if (ok && s->world > 1) {
@@ -947,7 +953,10 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
         s->peer_buf = pb;
         if (ok)
             ok = cudaMemset(pb, 0, tp_peer_buffer_bytes(c.H)) == cudaSuccess &&
-                 cudaMemset(s->peer_seq, 0, 4) == cudaSuccess && cudaMemset(s->tp_err, 0, 4) == cudaSuccess;
+                 cudaMemset(s->peer_seq, 0, 4) == cudaSuccess && cudaMemset(s->tp_err, 0, 4) == cudaSuccess &&
+                 cudaHostAlloc(reinterpret_cast<void**>(&s->tp_err_host), sizeof(int), cudaHostAllocDefault) ==
+                     cudaSuccess;
+        if (ok) *s->tp_err_host = 0;
     }
     if (ok && chunk > 1 && delta_layers > 0)
         ok = s->alloc(&s->delta_work, delta_chunked_workspace_bytes(chunk, c.VH) / 4) &&
@@ -1010,8 +1019,17 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
     return s.release();
 }
 
+// Status of the peer all-reduces so far, as last copied to the host: a peer
+// that never published within the bound leaves this State out of step with
+// its peers for good (Q3XK_ETIMEOUT from every later call).  Exact once the
+// state's stream has been synchronised.
+int peer_status(const State* s) {
+    return s->tp_err_host && *(volatile int*)s->tp_err_host ? Q3XK_ETIMEOUT : Q3XK_OK;
+}
+
 int state_forward_impl(Model* m, State* s, const int* tokens, int count, bool logits) {
     if (!m || !s || !tokens || count <= 0 || s->model != m) return Q3XK_EINVAL;
+    Q3XB_TRY(peer_status(s));
     const Config& c = *m->config;
     for (int i = 0; i < count; ++i)
         if (tokens[i] < 0 || tokens[i] >= c.V) return Q3XK_EINVAL;
@@ -1033,6 +1051,9 @@ int state_forward_impl(Model* m, State* s, const int* tokens, int count, bool lo
         s->position += T;
         done += T;
     }
+    if (s->tp_err_host &&
+        cudaMemcpyAsync(s->tp_err_host, s->tp_err, 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+        return Q3XK_ECUDA;
     return Q3XK_OK;
 }
 
@@ -1082,6 +1103,7 @@ int argmax_impl(const State* s, int* token) {
         if (cudaMemcpyAsync(all.data(), s->best, all.size() * 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
             cudaStreamSynchronize(s->stream) != cudaSuccess)
             return Q3XK_ECUDA;
+        Q3XB_TRY(peer_status(s));
         int bi = 0;
         for (int r = 1; r < s->world; ++r)
             if (all[2 * r] > all[2 * bi] || (all[2 * r] == all[2 * bi] && all[2 * r + 1] < all[2 * bi + 1])) bi = r;
@@ -1091,7 +1113,7 @@ int argmax_impl(const State* s, int* token) {
     if (cudaMemcpyAsync(token, s->argmax_out, 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess)
         return Q3XK_ECUDA;
-    return Q3XK_OK;
+    return peer_status(s);
 }
 
 int copy_logits_impl(const State* s, float* out) {
@@ -1103,12 +1125,12 @@ int copy_logits_impl(const State* s, float* out) {
                             s->stream) != cudaSuccess ||
             cudaStreamSynchronize(s->stream) != cudaSuccess)
             return Q3XK_ECUDA;
-        return Q3XK_OK;
+        return peer_status(s);
     }
     if (cudaMemcpyAsync(out, s->logits, (size_t)s->c->V * 4, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess)
         return Q3XK_ECUDA;
-    return Q3XK_OK;
+    return peer_status(s);
 }
 
 // The reference's Q3X_ASSERT: report, then abort (internal.h:70-80).
@@ -1252,6 +1274,13 @@ int q3xb_state_ipc_open(q3xb_state* state, const char* handles) {
     s->peer_ready = true;
     return Q3XK_OK;
 }
+int q3xb_state_set_peer_timeout(q3xb_state* state, double seconds) {
+    State* s = reinterpret_cast<State*>(state);
+    if (!s || !(seconds > 0.0) || seconds > 60.0) return Q3XK_EINVAL;
+    if (s->graph_exec) return Q3XK_EUNSUPPORTED;  // the captured decode step keeps the bound it was made with
+    s->peer_timeout_s = seconds;
+    return Q3XK_OK;
+}
 int q3xb_state_tp_error(const q3xb_state* state, int* flags) {
     const State* s = reinterpret_cast<const State*>(state);
     if (!s || !flags) return Q3XK_EINVAL;
@@ -1302,7 +1331,8 @@ int q3xb_state_synchronize(const q3xb_state* state) {
     if (!state) return Q3XK_EINVAL;
     const State* s = reinterpret_cast<const State*>(state);
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
-    return cudaStreamSynchronize(s->stream) == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess) return Q3XK_ECUDA;
+    return peer_status(s);
 }
 void* q3xb_state_stream(const q3xb_state* state) {
     return state ? static_cast<void*>(reinterpret_cast<const State*>(state)->stream) : nullptr;
@@ -1310,6 +1340,11 @@ void* q3xb_state_stream(const q3xb_state* state) {
 int q3xb_state_set_exact_prefill(q3xb_state* state, int enabled) {
     if (!state) return Q3XK_EINVAL;
     reinterpret_cast<State*>(state)->exact_prefill = enabled != 0;
+    return Q3XK_OK;
+}
+int q3xb_state_set_prefill_precision(q3xb_state* state, int precision) {
+    if (!state || (precision != Q3XK_GEMM_SPLIT && precision != Q3XK_GEMM_FP16)) return Q3XK_EINVAL;
+    reinterpret_cast<State*>(state)->gemm_precision = precision;
     return Q3XK_OK;
 }
 int q3xb_state_set_prefill_chunk(q3xb_state* state, int tokens) {

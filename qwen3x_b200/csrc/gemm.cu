@@ -7,6 +7,15 @@
 //    (x * 2^s_t has its largest magnitude in [2^14, 2^15)), so FP16 cannot
 //    overflow whatever the activations' range; the epilogue multiplies by
 //    2^-s_t exactly.
+//  * Two precisions.  FP16: one MMA per K-step on fp16(x) and fp16(d*q).
+//    SPLIT (the default of q3xk_gemm): both operands carry a second FP16
+//    plane, x = x_hi + x_lo (x_lo = fp16(x - x_hi), ~22 significant bits in
+//    all) and d*q = w_hi + w_lo exactly (w_lo = fma(q, d, -w_hi) in FP16:
+//    the residual of an 11-bit x 8-bit product always fits), and three MMAs
+//    per K-step accumulate w_hi x_hi + w_hi x_lo + w_lo x_hi in FP32.  The
+//    dropped w_lo x_lo term is ~2^-22 of the product, so the result is
+//    FP32-grade (the reference's per-token FP32 matvec, engine.cpp:580-583,
+//    rounds at ~2^-24 per add).
 //  * One tcgen05.mma tile is 128 weight rows (M, operand A) x 128 tokens (N,
 //    operand B) x 16 K, FP16 x FP16 -> FP32 accumulated in tensor memory.
 //    Operands are K-major in the 128-byte-swizzled layout: B (X16) arrives by
@@ -37,7 +46,6 @@ namespace {
 
 constexpr int BM = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 64;   // K per stage: 64 FP16 = one 128-byte swizzle row
-constexpr int kStages = Q3XK_GEMM_STAGES;
 constexpr int kAcc = 2;  // TMEM accumulator buffers
 constexpr int kDqWarps = Q3XK_GEMM_DQ_WARPS;   // dequantiser warps
 constexpr int kDqThreads = kDqWarps * 32;
@@ -103,17 +111,32 @@ __device__ __forceinline__ int tile_count(const GemmParams& p) {
 }
 
 // Per token-tile-width geometry: BN tokens per tile = MMA N (64, 128, 256).
-template <int BN>
+// SPLIT stages hold two planes of each operand (hi, lo), so they get fewer
+// stages and at most 128 tokens: 2 x 64 KB (BN 128) or 3 x 48 KB (BN 64),
+// plus the raw weight ring, within the 227 KB of shared memory.
+template <int BN, bool SPLIT>
 struct TileN {
-    static constexpr int kTileBytesX = BN * BK * 2;
+    static_assert(!SPLIT || BN <= 128, "split stages hold at most 128 tokens");
+    static constexpr int kTileBytesX = BN * BK * 2;  // one plane
+    static constexpr int kPlanes = SPLIT ? 2 : 1;
+    static constexpr int kStageX = kPlanes * kTileBytesX;
+    static constexpr int kStageW = kPlanes * kTileBytesW;
+    static constexpr int kStages = SPLIT ? (BN <= 64 ? 3 : 2) : Q3XK_GEMM_STAGES;
     static constexpr uint32_t kTmemCols = kAcc * BN < 32 ? 32 : kAcc * BN;  // power of 2 >= 32
     static constexpr uint32_t kIdesc = f16_idesc(BM, BN, 0);
+    static constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * (kStageX + kStageW) +
+                                    (size_t)kRawStages * kRawBytes +
+                                    (size_t)(3 * kStages + 2 * kAcc + 2 * kRawStages) * 8 + 16;
+    static_assert(kSmem <= 232448, "shared memory per CTA");
 };
 
 // ---- X -> FP16 with a per-token power-of-two scale -----------------------------
 
+// x16lo != nullptr: also the residual plane, x16lo = fp16(x * 2^s - x16) (the
+// subtraction is exact in FP32).
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ x16,
-                                                       float* __restrict__ tok_scale, int K) {
+                                                       __half* __restrict__ x16lo, float* __restrict__ tok_scale,
+                                                       int K) {
     griddep_wait();
     griddep_launch_dependents();
     const int t = blockIdx.x;
@@ -137,10 +160,18 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
     const float up = __uint_as_float((uint32_t)(s + 127) << 23);
     if (threadIdx.x == 0) tok_scale[t] = __uint_as_float((uint32_t)(127 - s) << 23);
     __half2* out = reinterpret_cast<__half2*>(x16 + (int64_t)t * K);
+    __half2* lo = x16lo ? reinterpret_cast<__half2*>(x16lo + (int64_t)t * K) : nullptr;
     for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
         const float4 v = *reinterpret_cast<const float4*>(row + k);
-        out[k / 2] = __floats2half2_rn(v.x * up, v.y * up);
-        out[k / 2 + 1] = __floats2half2_rn(v.z * up, v.w * up);
+        const float a0 = v.x * up, a1 = v.y * up, a2 = v.z * up, a3 = v.w * up;
+        const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+        out[k / 2] = h01;
+        out[k / 2 + 1] = h23;
+        if (lo) {
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            lo[k / 2] = __floats2half2_rn(a0 - f01.x, a1 - f01.y);
+            lo[k / 2 + 1] = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
+        }
     }
 }
 
@@ -155,24 +186,36 @@ __device__ __forceinline__ uint32_t sw128_off(int m, int c) {
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// 4 bytes of offset-binary Q8 (q + 128) -> 4 FP16 d*q (two half2).
-__device__ __forceinline__ void q8_word(uint32_t w, __half2 d2, uint32_t& o01, uint32_t& o23) {
+// Two exact FP16 weights q (as half2) times the scale: hi = fp16(d*q); with a
+// residual plane also r = fma(q, d, -hi), one rounding of a value that always
+// fits FP16 (an 11-bit scale times a <= 8-bit integer leaves at most 8 bits
+// below hi's rounding point), so hi + r == d*q exactly.
+__device__ __forceinline__ void mul_split(__half2 q, __half2 d2, uint32_t& hi, uint32_t* r) {
+    const __half2 h = __hmul2(q, d2);
+    hi = h2u(h);
+    if (r) *r = h2u(__hfma2(q, d2, __hneg2(h)));
+}
+
+// 4 bytes of offset-binary Q8 (q + 128) -> 4 FP16 d*q (two half2), and the
+// residuals when r != nullptr (r[0], r[1]).
+__device__ __forceinline__ void q8_word(uint32_t w, __half2 d2, uint32_t& o01, uint32_t& o23, uint32_t* r) {
     const __half2 bias = u2h(0x64806480u);  // 1024 + 128 in both halves
     const __half2 h01 = __hsub2(u2h(__byte_perm(w, 0x64646464u, 0x4140)), bias);  // exact q
     const __half2 h23 = __hsub2(u2h(__byte_perm(w, 0x64646464u, 0x4342)), bias);
-    o01 = h2u(__hmul2(h01, d2));
-    o23 = h2u(__hmul2(h23, d2));
+    mul_split(h01, d2, o01, r);
+    mul_split(h23, d2, o23, r ? r + 1 : nullptr);
 }
 
 // Two Q4 bytes (b0 in byte 0, b1 in byte 2 of `x`) -> low and high nibbles as
-// exact FP16 (n - 8), multiplied by d.
-__device__ __forceinline__ void q4_pair(uint32_t x, __half2 d2, uint32_t& lo, uint32_t& hi) {
+// exact FP16 (n - 8), multiplied by d (residuals into rl / rh when given).
+__device__ __forceinline__ void q4_pair(uint32_t x, __half2 d2, uint32_t& lo, uint32_t& hi, uint32_t* rl,
+                                        uint32_t* rh) {
     const __half2 lo_h = __hsub2(u2h((x & 0x000F000Fu) | 0x64006400u), u2h(0x64086408u));  // 1024+n - 1032
     // (x & 0xF0) | 0x6400 = 1024 + 16 n; /16 - 72 = n - 8 (exact, one rounding)
     const __half2 hi_h = __hfma2(u2h((x & 0x00F000F0u) | 0x64006400u), u2h(0x2C002C00u) /* 1/16 */,
                                  u2h(0xD480D480u) /* -72 */);
-    lo = h2u(__hmul2(lo_h, d2));
-    hi = h2u(__hmul2(hi_h, d2));
+    mul_split(lo_h, d2, lo, rl);
+    mul_split(hi_h, d2, hi, rh);
 }
 
 template <int TYPE>
@@ -185,7 +228,9 @@ struct Dequant<Q3XK_Q8_0> {
     static constexpr int kPerThread = 512 / kDqThreads;  // 128 rows x 4 raw chunks
     static constexpr int kRawRow = RAWK;  // quant bytes per staged row
     // raw: [128 rows][256 B] quants, then [128 rows][8] FP16 scales.
-    // kk: which 64-column K-step of the 256-column raw stage.
+    // kk: which 64-column K-step of the 256-column raw stage.  SPLIT: the
+    // residual plane goes to dst + kTileBytesW in the same layout.
+    template <bool SPLIT>
     __device__ static void run(const uint8_t* raw, uint8_t* dst, int d, int kk) {
         const uint16_t* scales = reinterpret_cast<const uint16_t*>(raw + kRawQuantBytes);
 #pragma unroll
@@ -196,12 +241,18 @@ struct Dequant<Q3XK_Q8_0> {
             const uint4 q = *reinterpret_cast<const uint4*>(raw + m * kRawRow + col);
             const __half2 d2 = __half2half2(__ushort_as_half(scales[m * 8 + (col >> 5)]));
             uint4 o0, o1;
-            q8_word(q.x, d2, o0.x, o0.y);
-            q8_word(q.y, d2, o0.z, o0.w);
-            q8_word(q.z, d2, o1.x, o1.y);
-            q8_word(q.w, d2, o1.z, o1.w);
+            uint32_t r[8];
+            q8_word(q.x, d2, o0.x, o0.y, SPLIT ? r + 0 : nullptr);
+            q8_word(q.y, d2, o0.z, o0.w, SPLIT ? r + 2 : nullptr);
+            q8_word(q.z, d2, o1.x, o1.y, SPLIT ? r + 4 : nullptr);
+            q8_word(q.w, d2, o1.z, o1.w, SPLIT ? r + 6 : nullptr);
             *reinterpret_cast<uint4*>(dst + sw128_off(m, 2 * c)) = o0;
             *reinterpret_cast<uint4*>(dst + sw128_off(m, 2 * c + 1)) = o1;
+            if (SPLIT) {
+                *reinterpret_cast<uint4*>(dst + kTileBytesW + sw128_off(m, 2 * c)) = make_uint4(r[0], r[1], r[2], r[3]);
+                *reinterpret_cast<uint4*>(dst + kTileBytesW + sw128_off(m, 2 * c + 1)) =
+                    make_uint4(r[4], r[5], r[6], r[7]);
+            }
         }
     }
 };
@@ -213,6 +264,7 @@ template <>
 struct Dequant<Q3XK_Q4_0> {
     static constexpr int kPerThread = 256 / kDqThreads;  // 128 rows x 2 blocks
     static constexpr int kRawRow = RAWK / 2;
+    template <bool SPLIT>
     __device__ static void run(const uint8_t* raw, uint8_t* dst, int d, int kk) {
         const uint16_t* scales = reinterpret_cast<const uint16_t*>(raw + kRawQuantBytes);
 #pragma unroll
@@ -222,18 +274,27 @@ struct Dequant<Q3XK_Q4_0> {
             const int blk = kk * 2 + b;           // block within the raw stage
             const uint4 q = *reinterpret_cast<const uint4*>(raw + m * kRawRow + 16 * blk);
             const __half2 d2 = __half2half2(__ushort_as_half(scales[m * 8 + blk]));
-            uint32_t l[8], h[8];
+            uint32_t l[8], h[8], rl[8], rh[8];
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {  // bytes (4j, 4j+1) and (4j+2, 4j+3) -> elements in order
-                q4_pair(__byte_perm(w[j], 0u, 0x5150), d2, l[2 * j], h[2 * j]);
-                q4_pair(__byte_perm(w[j], 0u, 0x5352), d2, l[2 * j + 1], h[2 * j + 1]);
+                q4_pair(__byte_perm(w[j], 0u, 0x5150), d2, l[2 * j], h[2 * j], SPLIT ? rl + 2 * j : nullptr,
+                        SPLIT ? rh + 2 * j : nullptr);
+                q4_pair(__byte_perm(w[j], 0u, 0x5352), d2, l[2 * j + 1], h[2 * j + 1],
+                        SPLIT ? rl + 2 * j + 1 : nullptr, SPLIT ? rh + 2 * j + 1 : nullptr);
             }
             const int c0 = 4 * b;  // 16-byte FP16 chunk of element 32b within the K-step
             *reinterpret_cast<uint4*>(dst + sw128_off(m, c0)) = make_uint4(l[0], l[1], l[2], l[3]);
             *reinterpret_cast<uint4*>(dst + sw128_off(m, c0 + 1)) = make_uint4(l[4], l[5], l[6], l[7]);
             *reinterpret_cast<uint4*>(dst + sw128_off(m, c0 + 2)) = make_uint4(h[0], h[1], h[2], h[3]);
             *reinterpret_cast<uint4*>(dst + sw128_off(m, c0 + 3)) = make_uint4(h[4], h[5], h[6], h[7]);
+            if (SPLIT) {
+                uint8_t* lo = dst + kTileBytesW;
+                *reinterpret_cast<uint4*>(lo + sw128_off(m, c0)) = make_uint4(rl[0], rl[1], rl[2], rl[3]);
+                *reinterpret_cast<uint4*>(lo + sw128_off(m, c0 + 1)) = make_uint4(rl[4], rl[5], rl[6], rl[7]);
+                *reinterpret_cast<uint4*>(lo + sw128_off(m, c0 + 2)) = make_uint4(rh[0], rh[1], rh[2], rh[3]);
+                *reinterpret_cast<uint4*>(lo + sw128_off(m, c0 + 3)) = make_uint4(rh[4], rh[5], rh[6], rh[7]);
+            }
         }
     }
 };
@@ -245,18 +306,21 @@ __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, int
     return false;
 }
 
-template <int TYPE, int BN>
+// xlomap: the residual plane of X (SPLIT only; ignored otherwise).
+template <int TYPE, int BN, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap qmap,
-            const __grid_constant__ CUtensorMap smap, const GemmParams p) {
+gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xlomap,
+            const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap smap, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    constexpr int kTileBytesX = TileN<BN>::kTileBytesX;
-    constexpr uint32_t kTmemCols = TileN<BN>::kTmemCols;
-    constexpr uint32_t kIdesc = TileN<BN>::kIdesc;
-    uint8_t* sx = smem;                                // kStages x BN x 128 B
-    uint8_t* sw = smem + kStages * kTileBytesX;        // kStages x 16 KB
-    uint8_t* sraw = sw + kStages * kTileBytesW;        // kRawStages x (32 + 2) KB
+    using G = TileN<BN, SPLIT>;
+    constexpr int kTileBytesX = G::kTileBytesX;
+    constexpr int kStageX = G::kStageX, kStageW = G::kStageW, kStages = G::kStages;
+    constexpr uint32_t kTmemCols = G::kTmemCols;
+    constexpr uint32_t kIdesc = G::kIdesc;
+    uint8_t* sx = smem;                                // kStages x planes x BN x 128 B (hi, then lo)
+    uint8_t* sw = smem + kStages * kStageX;            // kStages x planes x 16 KB (hi, then lo)
+    uint8_t* sraw = sw + kStages * kStageW;            // kRawStages x (32 + 2) KB
     uint64_t* bars = reinterpret_cast<uint64_t*>(sraw + kRawStages * kRawBytes);
     uint64_t* full = bars;   // X bytes landed and every dequant warp arrived
     uint64_t* empty = bars + 2 * kStages;
@@ -323,8 +387,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], kTileBytesX);
-                    tma_load_2d(sx + s * kTileBytesX, &xmap, ks * BK, tc.x_row, &full[s]);
+                    mbar_arrive_expect_tx(&full[s], kStageX);
+                    tma_load_2d(sx + s * kStageX, &xmap, ks * BK, tc.x_row, &full[s]);
+                    if (SPLIT) tma_load_2d(sx + s * kStageX + kTileBytesX, &xlomap, ks * BK, tc.x_row, &full[s]);
                 }
                 if (!ok) break;
             }
@@ -347,11 +412,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sw + s * kTileBytesW), b0 = smem_u32(sx + s * kTileBytesX);
+                    const uint32_t a0 = smem_u32(sw + s * kStageW), b0 = smem_u32(sx + s * kStageX);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_f16(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), kIdesc,
-                                 (ks | kk) ? 1u : 0u);
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ah = sw128_desc(a0 + kk * 32), bh = sw128_desc(b0 + kk * 32);
+                        umma_f16(d_tmem, ah, bh, kIdesc, (ks | kk) ? 1u : 0u);
+                        if (SPLIT) {  // + w_hi x_lo + w_lo x_hi
+                            umma_f16(d_tmem, ah, sw128_desc(b0 + kTileBytesX + kk * 32), kIdesc, 1u);
+                            umma_f16(d_tmem, sw128_desc(a0 + kTileBytesW + kk * 32), bh, kIdesc, 1u);
+                        }
+                    }
                     umma_commit(&empty[s]);  // stage s free once these MMAs finish
                 }
                 if (!ok) break;
@@ -386,7 +456,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                         break;
                     }
                 }
-                Dequant<TYPE>::run(sraw + r * kRawBytes, sw + s * kTileBytesW, d, kk);
+                Dequant<TYPE>::template run<SPLIT>(sraw + r * kRawBytes, sw + s * kStageW, d, kk);
                 fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
@@ -437,11 +507,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     }
 }
 
-size_t gemm_smem_bytes() {
-    return 1024 /* alignment slack */ + (size_t)kStages * (TileN<256>::kTileBytesX + kTileBytesW) +
-           (size_t)kRawStages * kRawBytes + (size_t)(3 * kStages + 2 * kAcc + 2 * kRawStages) * 8 + 16;
-}
-
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -472,37 +537,72 @@ int sm_count() {
 
 }  // namespace
 
-int launch_x_to_f16(const float* x, int T, int K, __half* x16, float* tok_scale, cudaStream_t s) {
+int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s) {
     if (K % 8) return Q3XK_EINVAL;  // TMA row stride of X16 must be a multiple of 16 bytes
-    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, tok_scale, K) != cudaSuccess)
+    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, x16lo, tok_scale, K) != cudaSuccess)
         return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;
 }
 
-int gemm_f16(const q3xk_matrix* w, const __half* x16, const float* tok_scale, int T, float* y, int accumulate,
-             const GemmGroups* groups, int bn_hint, cudaStream_t s) {
-    const int K = w->cols;
-    if (K % 8 || ((uintptr_t)x16 & 15) || ((uintptr_t)w->data & 15)) return Q3XK_EALIGN;
-    // Token tile = MMA N: the smallest of 64/128/256 that covers T, else 256 (grouped: 64).
-    const int bn = groups ? 64 : bn_hint ? bn_hint : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-    EncodeTiled enc = encode_fn();
-    if (!enc) return Q3XK_ECUDA;
-    CUtensorMap map;
+namespace {
+
+using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+
+struct KernSlot {
+    Kern fn;
+    size_t smem;
+    bool configured;
+};
+
+template <int TYPE, int BN, bool SPLIT>
+constexpr KernSlot slot_of() {
+    return KernSlot{gemm_kernel<TYPE, BN, SPLIT>, TileN<BN, SPLIT>::kSmem, false};
+}
+
+// [type: Q8_0, Q4_0][BN: 64, 128, 256][FP16, SPLIT]; split has no 256-token tile.
+KernSlot g_kernels[2][3][2] = {
+    {{slot_of<Q3XK_Q8_0, 64, false>(), slot_of<Q3XK_Q8_0, 64, true>()},
+     {slot_of<Q3XK_Q8_0, 128, false>(), slot_of<Q3XK_Q8_0, 128, true>()},
+     {slot_of<Q3XK_Q8_0, 256, false>(), KernSlot{nullptr, 0, false}}},
+    {{slot_of<Q3XK_Q4_0, 64, false>(), slot_of<Q3XK_Q4_0, 64, true>()},
+     {slot_of<Q3XK_Q4_0, 128, false>(), slot_of<Q3XK_Q4_0, 128, true>()},
+     {slot_of<Q3XK_Q4_0, 256, false>(), KernSlot{nullptr, 0, false}}},
+};
+
+bool encode_x_map(EncodeTiled enc, CUtensorMap* map, const __half* x16, int T, int K, int bn) {
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     const cuuint32_t box[2] = {BK, (cuuint32_t)bn};
     const cuuint32_t estr[2] = {1, 1};
-    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return Q3XK_ECUDA;
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+int gemm_f16(const q3xk_matrix* w, const __half* x16, const __half* x16lo, const float* tok_scale, int T, float* y,
+             int accumulate, const GemmGroups* groups, int bn_hint, cudaStream_t s) {
+    const int K = w->cols;
+    const bool split = x16lo != nullptr;
+    if (K % 8 || ((uintptr_t)x16 & 15) || ((uintptr_t)x16lo & 15) || ((uintptr_t)w->data & 15)) return Q3XK_EALIGN;
+    // Token tile = MMA N: the smallest of 64/128/256 that covers T, else 256
+    // (split: at most 128; grouped: 64).
+    int bn = groups ? 64 : bn_hint ? bn_hint : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    if (split && bn > 128) bn = 128;
+    EncodeTiled enc = encode_fn();
+    if (!enc) return Q3XK_ECUDA;
+    CUtensorMap map, lomap;
+    if (!encode_x_map(enc, &map, x16, T, K, bn)) return Q3XK_ECUDA;
+    if (!encode_x_map(enc, &lomap, split ? x16lo : x16, T, K, bn)) return Q3XK_ECUDA;
 
     // Raw weights: the quant bytes of every row record (uint8, [rows][qbytes])
     // and the scales ([rows][cols/32] FP16), both with the record stride; a
     // pool is one tensor of experts * rows rows.
     const int64_t qbytes = quant_bytes(w->type, K);
     const int64_t all_rows = (int64_t)w->rows * (groups ? w->experts : 1);
+    const cuuint32_t estr[2] = {1, 1};
     CUtensorMap qmap, smap;
     {
         const cuuint64_t qd[2] = {(cuuint64_t)qbytes, (cuuint64_t)all_rows};
@@ -538,30 +638,28 @@ int gemm_f16(const q3xk_matrix* w, const __half* x16, const float* tok_scale, in
         p.xoff = groups->xoff;
         p.tile_off = groups->tile_off;
     }
-    const size_t smem = gemm_smem_bytes();
-    using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
-    const int q8 = w->type == Q3XK_Q8_0;
-    const int slot = (q8 ? 0 : 3) + (bn == 64 ? 0 : bn == 128 ? 1 : 2);
-    static const Kern kernels[6] = {gemm_kernel<Q3XK_Q8_0, 64>, gemm_kernel<Q3XK_Q8_0, 128>,
-                                    gemm_kernel<Q3XK_Q8_0, 256>, gemm_kernel<Q3XK_Q4_0, 64>,
-                                    gemm_kernel<Q3XK_Q4_0, 128>, gemm_kernel<Q3XK_Q4_0, 256>};
-    static bool configured[6] = {false, false, false, false, false, false};
-    const Kern kern = kernels[slot];
-    if (!configured[slot]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    KernSlot& ks = g_kernels[w->type == Q3XK_Q8_0 ? 0 : 1][bn == 64 ? 0 : bn == 128 ? 1 : 2][split ? 1 : 0];
+    if (!ks.fn) return Q3XK_EUNSUPPORTED;
+    if (!ks.configured) {
+        if (cudaFuncSetAttribute(ks.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks.smem) != cudaSuccess)
             return Q3XK_ECUDA;
-        configured[slot] = true;
+        ks.configured = true;
     }
     // grouped: the tile count is only known on the device -> one CTA per SM
     const int tiles = groups ? sm_count() : p.tiles_w * p.tiles_t;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    const cudaError_t e1 = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, map, qmap, smap, p);
+    const cudaError_t e1 = launch_pdl(ks.fn, dim3(grid), dim3(kThreads), ks.smem, s, map, lomap, qmap, smap, p);
     if (e1 != cudaSuccess) return Q3XK_ECUDA;
     count_launch();
     return last_launch_status();
 }
 
 size_t gemm_grouped_tile_width() { return 64; }
+
+int gemm_clear_error() {
+    const int zero = 0;
+    return cuda_status(cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof zero));
+}
 
 }  // namespace q3xk
 
@@ -571,13 +669,16 @@ extern "C" {
 
 int q3xk_gemm_workspace_bytes(int T, int K, size_t* bytes) {
     if (!bytes || T <= 0 || K <= 0) return Q3XK_EINVAL;
-    *bytes = (((size_t)T * K * 2 + 255) & ~(size_t)255) + (size_t)T * 4;
+    // two FP16 planes of X (hi, lo), each 256-byte aligned, then the token scales
+    const size_t plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
+    *bytes = 2 * plane + (size_t)T * 4;
     return Q3XK_OK;
 }
 
-int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate, void* workspace,
-              size_t workspace_bytes, void* stream) {
+int q3xk_gemm_ex(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate, int precision,
+                 void* workspace, size_t workspace_bytes, void* stream) {
     if (!w || !w->data || !x || !y || T <= 0 || w->rows <= 0 || w->cols <= 0) return Q3XK_EINVAL;
+    if (precision != Q3XK_GEMM_SPLIT && precision != Q3XK_GEMM_FP16) return Q3XK_EINVAL;
     if (w->type != Q3XK_Q8_0 && w->type != Q3XK_Q4_0) return Q3XK_EUNSUPPORTED;
     if (w->cols % kBlock || w->row_stride != row_record_bytes(w->type, w->cols)) return Q3XK_EINVAL;
     size_t need = 0;
@@ -587,11 +688,20 @@ int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumul
         return Q3XK_EALIGN;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int K = w->cols;
+    const size_t plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
     __half* x16 = static_cast<__half*>(workspace);
-    float* tok_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (((size_t)T * K * 2 + 255) & ~(size_t)255));
-    const int st = launch_x_to_f16(x, T, K, x16, tok_scale, s);
+    __half* x16lo = precision == Q3XK_GEMM_SPLIT
+                        ? reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + plane)
+                        : nullptr;
+    float* tok_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 2 * plane);
+    const int st = launch_x_to_f16(x, T, K, x16, x16lo, tok_scale, s);
     if (st != Q3XK_OK) return st;
-    return gemm_f16(w, x16, tok_scale, T, y, accumulate, nullptr, 0, s);
+    return gemm_f16(w, x16, x16lo, tok_scale, T, y, accumulate, nullptr, 0, s);
+}
+
+int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate, void* workspace,
+              size_t workspace_bytes, void* stream) {
+    return q3xk_gemm_ex(w, x, T, y, accumulate, Q3XK_GEMM_SPLIT, workspace, workspace_bytes, stream);
 }
 
 int q3xk_gemm_device_error(int* flags) {

@@ -29,6 +29,8 @@
 //    the stream is still finishing; x and y are only touched after it.
 #include <mutex>
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "layers.cuh"
 
@@ -903,9 +905,11 @@ int q3xk_try_mv_host(const q3xk_matrix* w, const float* x_host, float* y_host, v
 // ---- q3xk_try_mv_host_noalloc: q3xk_try_mv_host with a fixed scratch ---------------
 //
 // The staging copies of x and y live in this module's own device array instead
-// of a caller workspace.  Its device address is looked up once per device with
-// cudaGetSymbolAddress (on the first call made with that device current) and
-// kept in g_static_scratch; nothing is allocated at any time.
+// of a caller workspace.  Its device address is looked up with
+// cudaGetSymbolAddress on the first call made with a device current and kept
+// in g_static_scratch together with the CUDA context it belongs to; a call
+// made under another context of that device (after cudaDeviceReset, or a
+// driver-API context) looks it up again.  Nothing is allocated at any time.
 namespace q3xk {
 namespace {
 
@@ -914,21 +918,46 @@ constexpr int kMaxScratchDevices = 64;
 
 static __device__ __align__(256) float g_mv_scratch[kStaticScratchFloats];
 
-std::mutex g_scratch_mutex;
-float* g_static_scratch[kMaxScratchDevices] = {};
+struct ScratchEntry {
+    CUcontext ctx;
+    float* ptr;
+};
 
-// Address of g_mv_scratch on the current device (looked up on first use).
+std::mutex g_scratch_mutex;
+ScratchEntry g_static_scratch[kMaxScratchDevices] = {};
+
+// The driver's cuCtxGetCurrent, through the runtime (the library does not
+// link libcuda, so it also loads on machines without a GPU driver).
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+CtxGetCurrent ctx_get_current() {
+    static CtxGetCurrent fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrent>(p);
+    }
+    return fn;
+}
+
+// Address of g_mv_scratch in the current device's current context.
 int static_scratch(float** out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return Q3XK_ECUDA;
     if (dev < 0 || dev >= kMaxScratchDevices) return Q3XK_EUNSUPPORTED;
+    CUcontext ctx = nullptr;
+    const CtxGetCurrent get = ctx_get_current();
+    if (!get || cudaFree(nullptr) != cudaSuccess || get(&ctx) != CUDA_SUCCESS || !ctx) return Q3XK_ECUDA;
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_static_scratch[dev]) {
+    ScratchEntry& e = g_static_scratch[dev];
+    if (!e.ptr || e.ctx != ctx) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_mv_scratch) != cudaSuccess || !p) return Q3XK_ECUDA;
-        g_static_scratch[dev] = static_cast<float*>(p);
+        e.ptr = static_cast<float*>(p);
+        e.ctx = ctx;
     }
-    *out = g_static_scratch[dev];
+    *out = e.ptr;
     return Q3XK_OK;
 }
 
@@ -956,14 +985,13 @@ int q3xk_try_mv_host_noalloc(const q3xk_matrix* w, const float* x_host, float* y
     return cuda_status(cudaStreamSynchronize(s));
 }
 
-// This GEMV has no device-side waits; the error word is kept for the kernels
-// that do (and for ABI stability) and is always 0 here.
+// The GEMVs have no device-side waits: the word is the dequant-GEMM's.
 int q3xk_device_error(int* flags) {
     if (!flags) return Q3XK_EINVAL;
-    *flags = 0;
-    return cuda_status(cudaDeviceSynchronize());
+    if (cudaDeviceSynchronize() != cudaSuccess) return Q3XK_ECUDA;
+    return q3xk_gemm_device_error(flags);
 }
 
-int q3xk_clear_device_error(void) { return Q3XK_OK; }
+int q3xk_clear_device_error(void) { return gemm_clear_error(); }
 
 }  // extern "C"

@@ -37,13 +37,17 @@ struct GemmGroups {
     const int* xoff;
     const int* tile_off;
 };
-// X (FP32 [T][K]) -> FP16 with a per-row power-of-two scale (tok_scale = 2^-s).
-int launch_x_to_f16(const float* x, int T, int K, __half* x16, float* tok_scale, cudaStream_t s);
+// X (FP32 [T][K]) -> FP16 with a per-row power-of-two scale (tok_scale = 2^-s);
+// x16lo != nullptr also gets the residual plane fp16(x 2^s - x16).
+int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s);
 // Y[T][N] (+)= X16 W^T * tok_scale on tcgen05; `groups` selects the expert-grouped tiles
-// (then W is a pool of groups experts and T the packed row count).
-int gemm_f16(const q3xk_matrix* w, const __half* x16, const float* tok_scale, int T, float* y, int accumulate,
-             const GemmGroups* groups, int bn_hint, cudaStream_t s);
+// (then W is a pool of groups experts and T the packed row count).  x16lo !=
+// nullptr selects the split precision (X = x16 + x16lo, three MMAs per K-step).
+int gemm_f16(const q3xk_matrix* w, const __half* x16, const __half* x16lo, const float* tok_scale, int T, float* y,
+             int accumulate, const GemmGroups* groups, int bn_hint, cudaStream_t s);
 size_t gemm_grouped_tile_width();
+// Resets the GEMM's device error word (bounded mbarrier waits that gave up).
+int gemm_clear_error();
 
 // MoE FFN over T prompt tokens on tcgen05 (moe.cu): router for all tokens,
 // device top-k, pairs grouped by expert, grouped gate|up GEMM, weighted
@@ -68,14 +72,17 @@ struct MoePrefillArgs {
     int* pos;            // [P]
     int* pair_token;     // [P]
     float* pair_weight;  // [P]
-    __half* x16;         // [T][H]
+    // FP16 planes: split precision keeps a residual plane after each
+    // (x16 + T*H, x16g + P*H, h16 + P*I), FP16 precision only the first.
+    __half* x16;         // [2][T][H]
     float* scale;        // [T]
-    __half* x16g;        // [P][H]
+    __half* x16g;        // [2][P][H]
     float* scale_g;      // [P]
     float* gu;           // [P][2I]
-    __half* h16;         // [P][I]
+    __half* h16;         // [2][P][I]
     float* scale_h;      // [P]
     float* out;          // [P][H]
+    bool split;          // split precision in the expert GEMMs
 };
 int moe_prefill(const MoePrefillArgs& a, cudaStream_t s);
 // Top-k routing of T tokens (router_topk_kernel) with the expert-parallel id

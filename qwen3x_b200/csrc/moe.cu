@@ -290,12 +290,15 @@ __global__ void __launch_bounds__(1024) moe_group_kernel(const int* __restrict__
 }
 
 // x16g[p] = x16[pair_token[p]], scale_g[p] = scale[pair_token[p]] (K halves per
-// row) for the *pairs grouped rows.
+// row) for the *pairs grouped rows; with lo planes (split precision) the
+// residual row too.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restrict__ x16,
+                                                          const __half* __restrict__ x16lo,
                                                           const float* __restrict__ scale,
                                                           const int* __restrict__ pair_token,
                                                           const int* __restrict__ pairs, int K,
-                                                          __half* __restrict__ x16g, float* __restrict__ scale_g) {
+                                                          __half* __restrict__ x16g, __half* __restrict__ x16glo,
+                                                          float* __restrict__ scale_g) {
     griddep_wait();
     griddep_launch_dependents();
     const int p = blockIdx.x;
@@ -304,15 +307,22 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __half* __restri
     const uint4* src = reinterpret_cast<const uint4*>(x16 + (int64_t)t * K);
     uint4* dst = reinterpret_cast<uint4*>(x16g + (int64_t)p * K);
     for (int i = threadIdx.x; i < K / 8; i += blockDim.x) dst[i] = src[i];
+    if (x16lo) {
+        const uint4* srcl = reinterpret_cast<const uint4*>(x16lo + (int64_t)t * K);
+        uint4* dstl = reinterpret_cast<uint4*>(x16glo + (int64_t)p * K);
+        for (int i = threadIdx.x; i < K / 8; i += blockDim.x) dstl[i] = srcl[i];
+    }
     if (threadIdx.x == 0) scale_g[p] = scale[t];
 }
 
 // Per packed row p: h = w_p * silu(g) * u over the interleaved gate|up row
 // (g(2j) g(2j+1) u(2j) u(2j+1)), then FP16 with a per-row power-of-two scale
-// (as x_to_f16_kernel) for the down GEMM.  I <= 1024.
+// (as x_to_f16_kernel) for the down GEMM, plus the residual plane when
+// h16lo != nullptr.  I <= 1024.
 __global__ void __launch_bounds__(256) swiglu_f16_kernel(const float* __restrict__ gu, const float* __restrict__ pw,
                                                          const int* __restrict__ pairs, int I,
-                                                         __half* __restrict__ h16, float* __restrict__ scale) {
+                                                         __half* __restrict__ h16, __half* __restrict__ h16lo,
+                                                         float* __restrict__ scale) {
     griddep_wait();
     griddep_launch_dependents();
     const int p = blockIdx.x;
@@ -346,7 +356,12 @@ __global__ void __launch_bounds__(256) swiglu_f16_kernel(const float* __restrict
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
         const int i = threadIdx.x + 256 * a;
-        if (i < I) h16[(int64_t)p * I + i] = __float2half_rn(h[a] * up);
+        if (i < I) {
+            const float v = h[a] * up;
+            const __half hv = __float2half_rn(v);
+            h16[(int64_t)p * I + i] = hv;
+            if (h16lo) h16lo[(int64_t)p * I + i] = __float2half_rn(v - __half2float(hv));
+        }
     }
 }
 
@@ -400,21 +415,25 @@ int moe_prefill(const MoePrefillArgs& a, cudaStream_t s) {
                    (const float*)a.weights, P, S, E1, tiles_a, tiles_b, bn, a.xoff, a.tile_gu, a.tile_dn, a.pos,
                    a.pair_token, a.pair_weight) != cudaSuccess)
         return Q3XK_ECUDA;
-    // 3. FP16 rows per token, gathered per pair
-    int st = launch_x_to_f16(a.x, T, H, a.x16, a.scale, s);
+    // 3. FP16 rows per token (+ residual planes), gathered per pair
+    __half* x16lo = a.split ? a.x16 + (size_t)T * H : nullptr;
+    __half* x16glo = a.split ? a.x16g + (size_t)P * H : nullptr;
+    __half* h16lo = a.split ? a.h16 + (size_t)P * I : nullptr;
+    int st = launch_x_to_f16(a.x, T, H, a.x16, x16lo, a.scale, s);
     if (st != Q3XK_OK) return st;
     const int* grouped = a.xoff + E1;  // pairs run on this GPU (device)
-    if (launch_pdl(gather_rows_kernel, dim3(P), dim3(256), 0, s, (const __half*)a.x16, (const float*)a.scale,
-                   (const int*)a.pair_token, grouped, H, a.x16g, a.scale_g) != cudaSuccess)
+    if (launch_pdl(gather_rows_kernel, dim3(P), dim3(256), 0, s, (const __half*)a.x16, (const __half*)x16lo,
+                   (const float*)a.scale, (const int*)a.pair_token, grouped, H, a.x16g, x16glo,
+                   a.scale_g) != cudaSuccess)
         return Q3XK_ECUDA;
     // 4. gate|up of every pair on its expert, weighted SwiGLU -> FP16, down
     const GemmGroups ggu{E1, a.xoff, a.tile_gu}, gdn{E1, a.xoff, a.tile_dn};
-    st = gemm_f16(a.gate_up, a.x16g, a.scale_g, P, a.gu, 0, &ggu, 0, s);
+    st = gemm_f16(a.gate_up, a.x16g, x16glo, a.scale_g, P, a.gu, 0, &ggu, 0, s);
     if (st != Q3XK_OK) return st;
     if (launch_pdl(swiglu_f16_kernel, dim3(P), dim3(256), 0, s, (const float*)a.gu, (const float*)a.pair_weight,
-                   grouped, I, a.h16, a.scale_h) != cudaSuccess)
+                   grouped, I, a.h16, h16lo, a.scale_h) != cudaSuccess)
         return Q3XK_ECUDA;
-    st = gemm_f16(a.down, a.h16, a.scale_h, P, a.out, 0, &gdn, 0, s);
+    st = gemm_f16(a.down, a.h16, h16lo, a.scale_h, P, a.out, 0, &gdn, 0, s);
     if (st != Q3XK_OK) return st;
     // 5. add each token's slots into its hidden row, in slot order
     if (launch_pdl(moe_combine_kernel, dim3(T), dim3(256), 0, s, (const float*)a.out, (const int*)a.pos, S, H,

@@ -83,12 +83,21 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
     asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
 __global__ void __launch_bounds__(1024) peer_allreduce_kernel(PeerArgs a, int* __restrict__ seq_ptr,
                                                               const float* __restrict__ partial,
                                                               float* __restrict__ y, int n,
-                                                              int* __restrict__ err) {
+                                                              int* __restrict__ err, uint64_t limit_ns) {
     griddep_wait();
     __shared__ int s_ok;
+    // A rank whose earlier call gave up is out of step with its peers: every
+    // later call returns at once, leaving y alone, with the error word kept.
+    if (*(volatile int*)err) return;
     const int seq = *seq_ptr + 1, phase = seq & 1;
     float* mine = a.data[a.rank] + (int64_t)phase * a.n_max;
     {
@@ -113,10 +122,10 @@ __global__ void __launch_bounds__(1024) peer_allreduce_kernel(PeerArgs a, int* _
     __syncthreads();
     if (threadIdx.x < a.world) {  // one thread per source rank
         const int* f = a.flags[a.rank] + phase * kMaxRanks + threadIdx.x;
-        const long long start = clock64();
+        const uint64_t start = global_ns();
         int n_try = 0;
         while (ld_acquire_sys(f) != seq) {
-            if ((++n_try & 63) == 0 && clock64() - start > 2000000000LL) {
+            if ((++n_try & 63) == 0 && global_ns() - start > limit_ns) {
                 atomicExch(err, 1);
                 s_ok = 0;
                 break;
@@ -159,8 +168,12 @@ size_t tp_peer_buffer_bytes(int n_max) {
 }
 
 int tp_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, int* seq, const float* partial,
-                          float* y, int n, int* err, cudaStream_t s) {
+                          float* y, int n, int* err, double timeout_s, cudaStream_t s) {
+    if (world < 1 || rank < 0 || rank >= world || n < 0 || !(timeout_s > 0.0) || timeout_s > 60.0)
+        return Q3XK_EINVAL;
     if (world > kMaxRanks || n > n_max || n > kPerThread * 1024) return Q3XK_EUNSUPPORTED;
+    for (int r = 0; r < world; ++r)
+        if (!bases[r]) return Q3XK_EINVAL;
     PeerArgs a{};
     const size_t data_bytes = ((size_t)2 * n_max * 4 + 255) / 256 * 256;
     for (int r = 0; r < world; ++r) {
@@ -170,7 +183,9 @@ int tp_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, in
     a.rank = rank;
     a.world = world;
     a.n_max = n_max;
-    if (launch_pdl(peer_allreduce_kernel, dim3(1), dim3(1024), 0, s, a, seq, partial, y, n, err) != cudaSuccess)
+    const uint64_t limit_ns = (uint64_t)(timeout_s * 1e9);
+    if (launch_pdl(peer_allreduce_kernel, dim3(1), dim3(1024), 0, s, a, seq, partial, y, n, err, limit_ns) !=
+        cudaSuccess)
         return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;
@@ -254,3 +269,18 @@ int tp_allgather(void* comm, const float* in, float* out, int64_t n, cudaStream_
 }
 
 }  // namespace q3xk
+
+using namespace q3xk;
+
+extern "C" {
+
+size_t q3xk_peer_buffer_bytes(int n_max) { return n_max > 0 ? tp_peer_buffer_bytes(n_max) : 0; }
+
+int q3xk_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, int* seq, const float* partial,
+                            float* y, int n, int* err, double timeout_s, void* stream) {
+    if (!bases || !seq || !partial || !y || !err || n_max <= 0) return Q3XK_EINVAL;
+    return tp_peer_allreduce_add(bases, rank, world, n_max, seq, partial, y, n, err, timeout_s,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

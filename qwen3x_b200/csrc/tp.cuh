@@ -27,11 +27,13 @@ int tp_allreduce_add(void* comm, float* partial, float* hidden, int64_t n, cudaS
 // bases[r] = rank r's buffer of tp_peer_buffer_bytes(n_max) bytes (own one
 // included, the others mapped with CUDA IPC), flags zeroed at creation; `seq`
 // a device int (zero-initialised, identical call sequence on every rank);
-// `err` a device int set to 1 if a peer did not publish within ~1 s.
-// y[0..n) += sum over ranks of partial[0..n), bit-identical on every rank.
+// `err` a device int set to 1 if a peer did not publish within timeout_s
+// seconds (then y is left alone, and every later call with err set returns at
+// once).  y[0..n) += sum over ranks of partial[0..n), bit-identical on every
+// rank.
 size_t tp_peer_buffer_bytes(int n_max);
 int tp_peer_allreduce_add(void* const* bases, int rank, int world, int n_max, int* seq, const float* partial,
-                          float* y, int n, int* err, cudaStream_t s);
+                          float* y, int n, int* err, double timeout_s, cudaStream_t s);
 // out2 = {logits[*idx], *idx + v0} (a rank's argmax in global numbering).
 int tp_pack_best(const float* logits, const int* idx, int v0, float* out2, cudaStream_t s);
 // out[world * n] = concatenation of every rank's in[n] (floats).

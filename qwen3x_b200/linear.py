@@ -140,8 +140,12 @@ def gemm_workspace_bytes(T: int, cols: int) -> int:
     return out.value
 
 
-def batch_mv(linear: Linear, X, Y, add: bool = False, workspace=None, stream=None) -> None:
-    """Y[T, rows] (+)= X[T, cols] W^T on tcgen05 (engine.cu:1568 batch_mv)."""
+def batch_mv(linear: Linear, X, Y, add: bool = False, workspace=None, stream=None,
+             precision: int | None = None) -> None:
+    """Y[T, rows] (+)= X[T, cols] W^T on tcgen05 (engine.cu:1568 batch_mv).
+
+    precision None calls q3xk_gemm (split FP16 operands, FP32-grade);
+    capi.GEMM_SPLIT / capi.GEMM_FP16 call q3xk_gemm_ex with that precision."""
     import torch
 
     T = int(X.shape[0])
@@ -149,8 +153,12 @@ def batch_mv(linear: Linear, X, Y, add: bool = False, workspace=None, stream=Non
     if workspace is None:
         workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
     nbytes = workspace.numel() * workspace.element_size()
-    check(lib().q3xk_gemm(ctypes.byref(linear.m), ptr(X), T, ptr(Y), int(add), ptr(workspace),
-                          nbytes, stream_ptr(stream)), "q3xk_gemm")
+    if precision is None:
+        check(lib().q3xk_gemm(ctypes.byref(linear.m), ptr(X), T, ptr(Y), int(add), ptr(workspace),
+                              nbytes, stream_ptr(stream)), "q3xk_gemm")
+    else:
+        check(lib().q3xk_gemm_ex(ctypes.byref(linear.m), ptr(X), T, ptr(Y), int(add), int(precision),
+                                 ptr(workspace), nbytes, stream_ptr(stream)), "q3xk_gemm_ex")
 
 
 def try_mv(linear: Linear, x_host, y_host, workspace, stream=None) -> None:

@@ -4,14 +4,16 @@ model.bin files of the small test configurations (modelfile.CONFIGS 9091,
 9092, 35091: real head sizes, few layers, 4096-token vocabulary).
 
 Tolerances, as absolute logit error over max(1, max|logit|):
-  every matrix on the CUDA-core GEMV (decode, and prefill in exact mode): 5e-4
-    (measured 1.6e-6 .. 2.9e-6)
-  prefill through the tcgen05 dequant-GEMM (FP16 operands, FP32 accumulation):
-    5e-3 (measured 6.7e-4 .. 2.7e-3).  A MoE model's top-k routing can flip
-    where two expert probabilities are closer than that error, after which
-    the logits differ by much more (a 100-token prompt of model 35091 flips
-    one route: 4.2e-2), so the GEMM-prefill case of the MoE model uses a
-    prompt without a flip;
+  5e-4, the reference's own cross-backend bar (tests/backend_smoke.py:28 of
+  qwen3x), for every default path: decode (CUDA-core GEMV) and prompts
+  through the tcgen05 dequant-GEMM in its default split precision (both
+  operands as two FP16 planes, FP32-grade);
+  5e-3 for the optional FP16-precision prompt GEMM (measured 6.7e-4 ..
+  2.7e-3 on the dense models).  At that precision a MoE model's top-k
+  routing can flip where two expert probabilities are closer than the
+  rounding error (the 100-token prompt of model 35091 flips one route and
+  misses by 4.2e-2), so the FP16-precision test covers the dense models and
+  the MoE flip is pinned as an expected failure;
 and greedy decoding must produce the same tokens as the reference.
 """
 import numpy as np
@@ -23,7 +25,8 @@ from qwen3x_b200 import modelfile
 pytestmark = pytest.mark.gpu
 
 DECODE_TOL = 5e-4
-PREFILL_TOL = 5e-3
+PREFILL_TOL = 5e-4
+FP16_PREFILL_TOL = 5e-3
 IDS = [9091, 9092, 35091]
 
 
@@ -65,16 +68,47 @@ def test_decode_path_matches_reference_token_by_token(cuda, model_files, mid):
     assert st.position == 24
 
 
-@pytest.mark.parametrize("mid,n", [(9091, 100), (9092, 100), (35091, 33)])
+@pytest.mark.parametrize("mid,n", [(9091, 100), (9092, 100), (35091, 100), (35091, 33), (35091, 300)])
 def test_prefill_matches_reference(cuda, model_files, mid, n):
-    """A prompt in one call: the dequant-GEMM path for T > 1."""
+    """A prompt in one call: the dequant-GEMM path (split precision) for T > 1.
+    The 100-token MoE prompt is the one that flips a route at FP16 precision."""
     model, st, ref = engines(model_files[mid], mid, 512)
     p = prompt(mid, n, seed=1)
     st.forward(p)
     ref.forward(p)
     e = err(st.logits(), ref.logits())
     assert e <= PREFILL_TOL, e
+    assert st.argmax() == ref.argmax()
     assert st.position == n
+
+
+@pytest.mark.parametrize("mid,n", [(9091, 100), (9092, 100), (35091, 33)])
+def test_fp16_prefill_matches_reference(cuda, model_files, mid, n):
+    """The optional FP16-precision prompt GEMM, at its looser bar."""
+    from qwen3x_b200.capi import GEMM_FP16
+
+    model, st, ref = engines(model_files[mid], mid, 512)
+    st.set_prefill_precision(GEMM_FP16)
+    p = prompt(mid, n, seed=1)
+    st.forward(p)
+    ref.forward(p)
+    e = err(st.logits(), ref.logits())
+    assert e <= FP16_PREFILL_TOL, e
+
+
+@pytest.mark.xfail(strict=True, reason="FP16 operands flip one top-8 route of this prompt (4.2e-2)")
+def test_fp16_prefill_moe_route_flip(cuda, model_files):
+    """Pins the known limit of FP16 precision on MoE models: this prompt
+    misses the reference by far more than the FP16 bar once a route flips."""
+    from qwen3x_b200.capi import GEMM_FP16
+
+    mid = 35091
+    model, st, ref = engines(model_files[mid], mid, 512)
+    st.set_prefill_precision(GEMM_FP16)
+    p = prompt(mid, 100, seed=1)
+    st.forward(p)
+    ref.forward(p)
+    assert err(st.logits(), ref.logits()) <= FP16_PREFILL_TOL
 
 
 @pytest.mark.parametrize("mid", IDS)
@@ -94,10 +128,10 @@ def test_exact_prefill_in_chunks_matches_reference(cuda, model_files, mid):
     assert st.argmax() == ref.argmax()
 
 
-def test_gemm_prefill_in_chunks(cuda, model_files):
-    """The GEMM path over several passes equals one pass to FP16 accuracy and
-    the reference to the prefill tolerance."""
-    mid = 9092
+@pytest.mark.parametrize("mid", [9092, 35091])
+def test_gemm_prefill_in_chunks(cuda, model_files, mid):
+    """The GEMM path over several passes matches the reference to the prefill
+    tolerance."""
     model, st, ref = engines(model_files[mid], mid, 512)
     p = prompt(mid, 150, seed=6)
     st.set_prefill_chunk(64)  # 64 + 64 + 22
@@ -128,19 +162,23 @@ def test_greedy_256_steps_identical(cuda, model_files, mid):
     assert worst <= DECODE_TOL, worst
 
 
-def test_prefill_then_greedy_tokens_identical(cuda, model_files):
-    mid = 9091
+@pytest.mark.parametrize("mid", [9091, 35091])
+def test_prefill_then_greedy_tokens_identical(cuda, model_files, mid):
+    """GEMM-path prompt (the MoE model's route-sensitive 100-token one), then
+    64 greedy steps: identical tokens, logits within the bar at every step."""
     model, st, ref = engines(model_files[mid], mid, 512)
-    p = prompt(mid, 64, seed=3)
+    p = prompt(mid, 100, seed=1)
     st.forward(p)
     ref.forward(p)
-    ours, theirs = [], []
-    for _ in range(32):
+    ours, theirs, worst = [], [], 0.0
+    for _ in range(64):
         ours.append(st.argmax())
         theirs.append(ref.argmax())
+        worst = max(worst, err(st.logits(), ref.logits()))
         st.forward([ours[-1]])
         ref.forward([theirs[-1]])
     assert ours == theirs
+    assert worst <= PREFILL_TOL, worst
 
 
 def test_checkpoint_restore_and_reset(cuda, model_files):

@@ -199,12 +199,26 @@ def test_bf16_chunked(cuda, cols):
     assert scaled_err(y, ref, bits, BF16, rows, cols, x) <= TOL
 
 
-def test_no_device_timeouts(cuda):
-    """Every bounded wait of the runs above completed (error word still 0)."""
+def test_device_error_word_is_the_gemm_word(cuda):
+    """q3xk_device_error reports the dequant-GEMM's bounded-wait word (the
+    GEMVs have no device-side waits): after a GEMM it is 0 and equal to
+    q3xk_gemm_device_error, and clearing keeps it 0."""
     import ctypes
 
-    from qwen3x_b200.capi import lib
+    import torch
 
-    flags = ctypes.c_int(-1)
+    from qwen3x_b200.capi import lib
+    from qwen3x_b200.linear import Linear, batch_mv
+
+    rows, cols, T = 256, 512, 16
+    lin = Linear.from_packed(quant.quantize_q8_0(quant.gaussian((rows, cols), 30, 0.02)), Q8_0, rows, cols,
+                             device=cuda)
+    X = torch.randn(T, cols, device=cuda)
+    Y = torch.empty(T, rows, device=cuda)
+    batch_mv(lin, X, Y)
+    flags, gemm = ctypes.c_int(-1), ctypes.c_int(-1)
     assert lib().q3xk_device_error(ctypes.byref(flags)) == 0
-    assert flags.value == 0
+    assert lib().q3xk_gemm_device_error(ctypes.byref(gemm)) == 0
+    assert flags.value == gemm.value == 0
+    assert lib().q3xk_clear_device_error() == 0
+    assert lib().q3xk_device_error(ctypes.byref(flags)) == 0 and flags.value == 0

@@ -12,11 +12,11 @@ from qwen3x_b200 import modelfile
 
 pytestmark = pytest.mark.gpu
 
-# decode (GEMV path): partial sums of the row-parallel projections / of the
-# ranks' experts are added in another order; prompt (FP16 dequant-GEMM): a
-# rank's K slice gets its own per-token FP16 scale, so rounding differs within
-# the GEMM bar
-TOL = {"decode": 1e-4, "prefill": 5e-3}
+# decode (GEMV path) and prompt (split-precision dequant-GEMM, FP32-grade):
+# partial sums of the row-parallel projections / of the ranks' experts are
+# added in another order, so results agree to FP32 rounding, within the
+# reference's cross-backend bar of 5e-4
+TOL = {"decode": 1e-4, "prefill": 5e-4}
 
 
 def _tp_rank(rank, world, port, path, out, prompt, steps):

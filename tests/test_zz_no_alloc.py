@@ -1,5 +1,7 @@
 """q3xk_try_mv_host_noalloc (fixed device scratch, no allocation) against
-q3xk_try_mv_host (caller workspace), both through the C ABI.
+q3xk_try_mv_host (caller workspace), both through the C ABI, and both against
+the reference CPU matvec (oracle.mv: arch/cpu.cpp's mv, compiled unmodified)
+at the GEMV bar, max |y - y_ref| / sum_k |w x| <= 1e-5.
 
 Collected last on purpose: it must pass after every other test has run in the
 same process, and alone in a fresh one.
@@ -9,9 +11,12 @@ import ctypes
 import numpy as np
 import pytest
 
+import oracle
 from qwen3x_b200 import capi
 from qwen3x_b200.capi import Matrix, lib
-from qwen3x_b200.quant import Q4_0, Q8_0, gaussian, quantize
+from qwen3x_b200.quant import Q4_0, Q8_0, dequantize, gaussian, quantize
+
+GEMV_TOL = 1e-5
 
 SCRATCH_FLOATS = 1 << 20
 
@@ -37,7 +42,9 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, mtype, rows, cols):
     from qwen3x_b200.linear import Linear
 
     w = gaussian((rows, cols), seed=71, std=0.02)
-    lin = Linear.from_packed(quantize(w, mtype), mtype, rows, cols, device=cuda)
+    packed = quantize(w, mtype)
+    lin = Linear.from_packed(packed, mtype, rows, cols, device=cuda)
+    wabs = np.abs(dequantize(packed, mtype, rows, cols))
     ws_bytes = ((cols * 4 + 15) & ~15) + rows * 4
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
     stream = torch.cuda.current_stream().cuda_stream
@@ -51,3 +58,8 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, mtype, rows, cols):
                    "q3xk_try_mv_host_noalloc")
         scale = np.abs(y_ref).max()
         assert np.abs(y - y_ref).max() <= 1e-6 * scale, call
+        # the reference's own CPU matvec (the try_mv contract this replaces)
+        ref = oracle.mv(packed, mtype, rows, cols, x, threads=8).astype(np.float64)
+        mag = np.maximum(wabs @ np.abs(x), 1e-30)
+        assert float((np.abs(y_ref - ref) / mag).max()) <= GEMV_TOL, call
+        assert float((np.abs(y - ref) / mag).max()) <= GEMV_TOL, call
