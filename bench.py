@@ -78,6 +78,23 @@ def profile_traffic(name: str):
     return None
 
 
+def recorded_reference_programs():
+    """The reference's own CUDA and CPU programs timed on a B200 box
+    (profiles/reference_programs_b200.md, made by oracle/time_reference_cli.py):
+    read from the committed summary, not run here."""
+    p = ROOT / "profiles" / "reference_programs_b200.md"
+    if not p.exists():
+        return None
+    text = p.read_text()
+    try:
+        block = text.split("```json", 1)[1].split("```", 1)[0]
+        d = json.loads(block)
+    except Exception:
+        return None
+    d["source"] = "recorded: profiles/reference_programs_b200.md (oracle/time_reference_cli.py, same model.bin)"
+    return d
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
 
@@ -634,6 +651,14 @@ def main(argv=None):
         engine = time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
                              rank == 0 and world == 1 and not args.no_cpu_baseline)
 
+    ref_programs = recorded_reference_programs()
+    if ref_programs and engine and args.engine_config == 9000:
+        rc = ref_programs.get("reference_cuda_9000", {})
+        if rc.get("prefill_tok_s") and rc.get("decode_tok_s"):
+            ref_programs["engine_9b_vs_reference_cuda"] = {
+                "prefill": round(engine["prefill_tok_s"] / rc["prefill_tok_s"], 2),
+                "decode": round(engine["decode_tok_s"] / rc["decode_tok_s"], 2)}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, kind, sample = cpu_reference_gbs(1, threads=1, budget_s=10.0)
@@ -666,6 +691,7 @@ def main(argv=None):
                                                   "(default: hi+lo FP16 planes of X and d*q, 3 MMAs per "
                                                   "K-step, FP32-grade); *_fp16_T*: FP16 operands, 1 MMA"),
                 "engine_9b": engine,
+                "reference_programs": ref_programs,
             },
         }
         print(json.dumps(line), flush=True)
