@@ -286,7 +286,10 @@ def time_e2e(mtype: int, steps: int, warmup: int, device, world: int):
 def time_gemm(mtype: int, T: int, reps: int, device, world: int, precision=None):
     """Prefill dequant-GEMM Y[T, 12288] = X[T, 4096] W^T at
     `precision` (None = q3xk_gemm's split default); returns seconds per call,
-    max over ranks."""
+    max over ranks.  The calls are replayed from a CUDA graph (no host time in
+    the measurement) and rotate over weight copies whose total exceeds the
+    126 MB L2 (3 x 53.5 MB for Q8_0, 5 x 28.3 MB for Q4_0), so every call
+    streams its weights from HBM as a prompt chunk does."""
     import torch
     import torch.distributed as dist
 
@@ -294,22 +297,33 @@ def time_gemm(mtype: int, T: int, reps: int, device, world: int, precision=None)
     from qwen3x_b200.linear import Linear, batch_mv, gemm_workspace_bytes
 
     packed = quant.quantize(quant.gaussian((ROWS, COLS), 1, 0.02), mtype)
-    lin = Linear.from_packed(packed, mtype, ROWS, COLS, device=device)
+    copies = 3 if mtype == 1 else 5
+    lins = [Linear.from_packed(packed, mtype, ROWS, COLS, device=device) for _ in range(copies)]
     X = torch.from_numpy(quant.gaussian((T, COLS), 3)).to(device)
     Y = torch.empty(T, ROWS, device=device)
     ws = torch.empty(gemm_workspace_bytes(T, COLS), dtype=torch.uint8, device=device)
-    for _ in range(3):
-        batch_mv(lin, X, Y, workspace=ws, precision=precision)
-    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device)
+    per_graph = max(1, reps // copies) * copies
+    with torch.cuda.stream(stream):
+        for lin in lins:  # warm-up (configures the kernels before capture)
+            batch_mv(lin, X, Y, workspace=ws, stream=stream, precision=precision)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(per_graph):
+                batch_mv(lins[i % copies], X, Y, workspace=ws, stream=stream, precision=precision)
+        g.replay()
+        stream.synchronize()
     if world > 1:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(reps):
-        batch_mv(lin, X, Y, workspace=ws, precision=precision)
-    end.record()
-    torch.cuda.synchronize()
-    secs = start.elapsed_time(end) / 1e3 / reps
+    with torch.cuda.stream(stream):  # the graph replays on the current stream: time it there
+        start.record(stream)
+        g.replay()
+        end.record(stream)
+    end.synchronize()
+    secs = start.elapsed_time(end) / 1e3 / per_graph
+    del g
     if world > 1:
         t = torch.tensor([secs], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -493,6 +507,99 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
     return out
 
 
+def time_engine_batch(cfg_id: int, prompt_len: int, decode_steps: int, batch: int, device):
+    """Batched decode through q3xb_state_forward_batch (one GPU): `batch`
+    independent sequences, each prefilled with its own uniform-random
+    `prompt_len`-token prompt, then `decode_steps` greedy steps in which every
+    sequence takes one token per call (every matrix read once for all of
+    them).  Reported next to the same decode with one sequence (state_forward),
+    as tokens per second over all sequences; CUDA events on the lead state's
+    stream, host argmax round trips included as in the single-sequence leg."""
+    import numpy as np
+    import torch
+
+    from qwen3x_b200 import modelfile
+    from qwen3x_b200.backend import Model, State, forward_batch
+
+    c = modelfile.CONFIGS[cfg_id]
+    size = modelfile.file_size(c)
+    path = os.path.join(model_file_dir(size), f"q3x_bench_batch_{cfg_id}_{os.getpid()}.bin")
+    out = {"config": f"{cfg_id} ({c.name})", "prompt_tokens": prompt_len, "decode_steps": decode_steps,
+           "batch": batch, "parallelism": "single GPU"}
+    try:
+        t0 = time.time()
+        modelfile.write_model(path, c, seed=7, device=device)
+        out["model_write_s"] = round(time.time() - t0, 1)
+        model = Model(path)
+        ctx = prompt_len + decode_steps + 8
+        states = [State(model, ctx) for _ in range(batch)]
+        rng = np.random.default_rng(13)
+        t1 = time.time()
+        for s in states:
+            s.forward(rng.integers(0, c.V, prompt_len).astype(np.int32))
+        states[0].synchronize()
+        for s in states:
+            s.synchronize()
+        out["prefill_all_s"] = round(time.time() - t1, 1)
+        stream = torch.cuda.ExternalStream(states[0].stream)
+        for s in states[1:]:
+            s.checkpoint_save()
+        states[0].checkpoint_save()
+        # warm-up step, then restore the prompts' end state
+        forward_batch(model, states, [s.argmax() for s in states])
+        for s in states:
+            s.checkpoint_restore()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(device.index) as clk:
+            toks = [s.argmax() for s in states]
+            e0.record(stream)
+            for _ in range(decode_steps):
+                forward_batch(model, states, toks)
+                toks = [s.argmax() for s in states]
+            e1.record(stream)
+            e1.synchronize()
+        batch_s = e0.elapsed_time(e1) / 1e3
+        # the same decode with one sequence through state_forward
+        for s in states:
+            s.checkpoint_restore()
+        s0 = states[0]
+        stream0 = torch.cuda.ExternalStream(s0.stream)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tok = s0.argmax()
+        e2.record(stream0)
+        for _ in range(decode_steps):
+            s0.forward([tok])
+            tok = s0.argmax()
+        e3.record(stream0)
+        e3.synchronize()
+        single_s = e2.elapsed_time(e3) / 1e3
+        out.update({
+            "batch_decode_tok_s": round(batch * decode_steps / batch_s, 1),
+            "batch_ms_per_step": round(batch_s / decode_steps * 1e3, 3),
+            "single_decode_tok_s": round(decode_steps / single_s, 1),
+            "single_ms_per_token": round(single_s / decode_steps * 1e3, 3),
+            "speedup": round((batch * decode_steps / batch_s) / (decode_steps / single_s), 2),
+            "clocks": clk.summary(),
+        })
+        for s in states:
+            s.close()
+        model.close()
+    finally:
+        if os.path.exists(path):
+            os.unlink(path)
+    return out
+
+
+def recorded_first_tokens():
+    """Greedy tokens of the single-GPU engine legs (tests/golden/bench_first_tokens.json),
+    the parity check of the tensor- and expert-parallel legs."""
+    p = ROOT / "tests" / "golden" / "bench_first_tokens.json"
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return {}
+
+
 def cpu_engine_tok_s(path, c, prompt=2, steps=2):
     """The reference CPU forward (engine.cpp via oracle/_ref; single-threaded,
     one token per forward as the reference runs) on the same model.bin: a
@@ -576,6 +683,10 @@ def main(argv=None):
                          "MoE Q4_0), 27008 (cfg5, 27B-shaped Q8_0)")
     ap.add_argument("--engine-prompt", type=int, default=None, help="prompt tokens (default per config)")
     ap.add_argument("--engine-decode", type=int, default=256)
+    ap.add_argument("--engine-batch", type=int, default=0,
+                    help="with --only engine: batched decode of this many sequences (one GPU)")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="N > 1: skip the tensor-/expert-parallel engine legs")
     ap.add_argument("--only", choices=["gemv", "gemm", "engine"], default=None,
                     help="run one kernel family only (for profiling; no JSON line)")
     args = ap.parse_args(argv)
@@ -592,15 +703,21 @@ def main(argv=None):
     if args.only == "gemm":
         for precision, pname in ((None, "split"), (capi.GEMM_FP16, "fp16")):
             for mtype in (1, 2):
-                secs = time_gemm(mtype, 4096, max(args.steps, 1), device, world, precision)
-                if rank == 0:
-                    print(f"gemm {pname} type={mtype} T=4096: {secs * 1e6:.1f} us "
-                          f"{2 * 4096 * ROWS * COLS / secs / 1e12:.1f} TFLOP/s", flush=True)
+                for T in (1, 2, 8, 16, 32, 64, 128, 512, 4096):
+                    secs = time_gemm(mtype, T, 10 if T >= 512 else 50, device, world, precision)
+                    if rank == 0:
+                        print(f"gemm {pname} type={mtype} T={T}: {secs * 1e6:.1f} us "
+                              f"{2 * T * ROWS * COLS / secs / 1e12:.1f} TFLOP/s "
+                              f"{algorithmic_bytes(mtype) / secs / 1e9:.0f} GB/s(weights)", flush=True)
         return 0
 
     prompts = {9000: 4096, 36035: 2048, 27008: 16384}  # BASELINE configs 3, 4, 5
     if args.engine_prompt is None:
         args.engine_prompt = prompts.get(args.engine_config, 4096)
+    if args.only == "engine" and args.engine_batch > 0 and world == 1:
+        print(json.dumps(time_engine_batch(args.engine_config, args.engine_prompt, args.engine_decode,
+                                           args.engine_batch, device)), flush=True)
+        return 0
     if args.only == "engine":
         res = time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
                           rank == 0 and world == 1 and not args.no_cpu_baseline, rank, world)
@@ -647,9 +764,22 @@ def main(argv=None):
         gemm["peak_kind"] = peak_tf[1]
 
     engine = None
-    if args.only is None and not args.no_engine and world == 1:  # tensor-parallel runs: --only engine
+    if args.only is None and not args.no_engine and world == 1:
         engine = time_engine(args.engine_config, args.engine_prompt, args.engine_decode, device,
                              rank == 0 and world == 1 and not args.no_cpu_baseline)
+    # N > 1: the sharded paths, each rank holding a share of one model --
+    # tensor parallelism on the 27B-shaped dense model (16K prompt, 256 greedy
+    # steps) and expert parallelism on the 35B-A3B MoE (2K prompt) -- with the
+    # greedy tokens checked against the recorded single-GPU run
+    sharded = {}
+    if args.only is None and world > 1 and not args.no_sharded:
+        golden = recorded_first_tokens()
+        for cfg_id, key in ((27008, "engine_tp27b"), (36035, "engine_ep35b")):
+            res = time_engine(cfg_id, prompts[cfg_id], 256, device, False, rank, world)
+            ref = golden.get(str(cfg_id))
+            if ref is not None:
+                res["first_tokens_match_single_gpu"] = res.get("first_tokens") == ref[:len(res.get("first_tokens", []))]
+            sharded[key] = res
 
     ref_programs = recorded_reference_programs()
     if ref_programs and engine and args.engine_config == 9000:
@@ -691,6 +821,7 @@ def main(argv=None):
                                                   "(default: hi+lo FP16 planes of X and d*q, 3 MMAs per "
                                                   "K-step, FP32-grade); *_fp16_T*: FP16 operands, 1 MMA"),
                 "engine_9b": engine,
+                **sharded,
                 "reference_programs": ref_programs,
             },
         }

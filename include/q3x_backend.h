@@ -45,6 +45,14 @@ Q3XK_API int state_argmax(const State* state);
 Q3XK_API void state_copy_logits(const State* state, float* output);
 Q3XK_API uint32_t model_id(const Model* model);
 
+/* Batched decode (no counterpart in the reference, which advances one State
+ * per call): one token for each of `count` (1..16) distinct States of the
+ * same model, each computing its logits -- the same as state_forward(
+ * states[b], &tokens[b], 1, true) for every b, with every matrix read once
+ * for all of them.  Runs on states[0]'s stream (the others' streams are
+ * joined before and after); one GPU. */
+Q3XK_API void state_forward_batch(Model* model, State* const* states, const int* tokens, int count);
+
 /* internal.h:32-34 (constants of the registered Qwen family). */
 Q3XK_API int vocab_size();
 Q3XK_API int max_context();
@@ -76,6 +84,8 @@ Q3XK_API int q3xb_state_reset(q3xb_state* state);
  * state's stream (logits/argmax calls synchronise). */
 Q3XK_API int q3xb_state_forward(q3xb_model* model, q3xb_state* state, const int* tokens, int count,
                                 int compute_logits);
+/* state_forward_batch of part 1 (tokens: host int32[count]). */
+Q3XK_API int q3xb_state_forward_batch(q3xb_model* model, q3xb_state* const* states, const int* tokens, int count);
 Q3XK_API int q3xb_state_checkpoint_save(q3xb_state* state);
 Q3XK_API int q3xb_state_checkpoint_restore(q3xb_state* state);
 Q3XK_API int q3xb_state_argmax(const q3xb_state* state, int* token);

@@ -23,6 +23,20 @@ SHARD_FIELDS = ("rank", "world", "kh0", "vh0", "ah0", "kv0", "i0", "v0", "KH", "
                 "e0", "experts")
 
 
+def forward_batch(model: "Model", states, tokens) -> None:
+    """One decode step of independent sequences: states[b] takes tokens[b]
+    (q3xb_state_forward_batch; every matrix is read once for all of them)."""
+    import ctypes
+
+    n = len(states)
+    handles = (ctypes.c_void_p * n)(*[s.handle for s in states])
+    t = np.ascontiguousarray(tokens, np.int32)
+    if t.size != n:
+        raise ValueError("one token per state")
+    capi.check(capi.lib().q3xb_state_forward_batch(model.handle, ctypes.cast(handles, ctypes.c_void_p),
+                                                   t.ctypes.data, n), "state_forward_batch")
+
+
 def tp_plan(model_id: int, rank: int, world: int) -> dict:
     """This rank's tensor-parallel share of a registered model (no loading)."""
     f = (ctypes.c_int * 16)()

@@ -124,6 +124,8 @@ _SIGNATURES = {
     "q3xb_state_reset": (ctypes.c_int, [ctypes.c_void_p]),
     "q3xb_state_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_int, ctypes.c_int]),
+    "q3xb_state_forward_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_int]),
     "q3xb_state_checkpoint_save": (ctypes.c_int, [ctypes.c_void_p]),
     "q3xb_state_checkpoint_restore": (ctypes.c_int, [ctypes.c_void_p]),
     "q3xb_state_argmax": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),

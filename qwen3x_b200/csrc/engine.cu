@@ -41,6 +41,7 @@ constexpr int kMaxContext = 262144;                 // model_config.h:13
 constexpr size_t kHeaderSize = 8 + 16 * 4;          // model_config.h:10-12
 constexpr int kEndOfText = 248044, kImEnd = 248046;  // engine.cpp:28
 constexpr int kChunk = 2048;                        // prefill tokens per pass
+constexpr int kMaxBatch = 16;                       // sequences per batched decode step
 constexpr size_t kAlign = 256;
 
 struct Config {
@@ -270,6 +271,8 @@ struct State {
     int chunk_capacity = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
+    cudaEvent_t batch_event = nullptr;  // orders this state's stream against a batched step it joins
+    float* batch_logits = nullptr;      // [chunk][V] lm_head output of a batched step this state leads
     std::vector<void*> allocations;
 
     ~State() {
@@ -281,6 +284,7 @@ struct State {
             if (peer_ready && r != rank && peer_bases[r]) cudaIpcCloseMemHandle(peer_bases[r]);
         for (void* p : allocations) cudaFree(p);
         if (tp_err_host) cudaFreeHost(tp_err_host);
+        if (batch_event) cudaEventDestroy(batch_event);
         tp_comm_destroy(comm);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -860,6 +864,90 @@ int forward_chunk(Model& m, State& s, int T, bool logits) {
     return launch_advance(s.pos, T, st);
 }
 
+// One decode step of n independent sequences (batched decode): sequence b
+// is states[b], fed tokens[b].  Every matrix is read once for all n tokens
+// (the dequant-GEMM over T = n, few-token tiles with split-K); the
+// recurrent and attention steps run per sequence on its own state (DeltaNet
+// memory and conv history, KV cache, position); MoE layers route all n
+// tokens together through the grouped expert GEMMs.  Work buffers are the
+// lead state's (states[0]), whose stream runs the step; the other states'
+// streams are joined before and after with events.  Equivalent to
+// state_forward(states[b], &tokens[b], 1, true) for every b, up to the
+// rounding of the split-precision GEMM (FP32-grade) against the GEMV.
+int forward_batch(Model& m, State** states, int n) {
+    State& L = *states[0];
+    const Config& c = m.shard.lc;
+    const cudaStream_t st = L.stream;
+    const int H = c.H, DO = c.VH * c.VD, DQKV = 2 * c.KH * c.KD + DO, AS = c.AH * c.AD;
+    Q3XB_TRY(launch_embed(m.embedding, L.tokens, n, L.hidden, st));
+    int di = 0, ai = 0;
+    for (int i = 0; i < c.N; ++i) {
+        const Layer& l = m.layer[i];
+        Q3XB_TRY(launch_rms(L.hidden, l.in_norm, H, n, L.normed, st));
+        const int P = l.in_proj.rows;
+        Q3XB_TRY(mm(L, l.in_proj, L.normed, n, L.proj, 0));
+        if (l.delta) {
+            const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
+            for (int b = 0; b < n; ++b) {
+                State& s = *states[b];
+                float* pb = L.proj + (size_t)b * P;
+                if (c.CK == 4) {
+                    Q3XB_TRY(launch_delta(pb, P, 1, dd, l.alog, l.dt, l.dnorm, s.memory[di], L.mix + (size_t)b * DO, DO,
+                                          st, l.conv, s.conv[di], c.CK, s.group_count));
+                } else {
+                    Q3XB_TRY(launch_conv(pb, P, 1, DQKV, l.conv, c.CK, s.conv[di], st));
+                    Q3XB_TRY(launch_delta(pb, P, 1, dd, l.alog, l.dt, l.dnorm, s.memory[di], L.mix + (size_t)b * DO,
+                                          DO, st));
+                }
+            }
+            ++di;
+        } else {
+            const AttnDims ad{c.AH, c.KVH, c.AD, c.RD};
+            for (int b = 0; b < n; ++b) {
+                State& s = *states[b];
+                Q3XB_TRY(launch_attention(L.proj + (size_t)b * P, P, 1, ad, l.qn1, l.kn1, s.pos, s.kcache[ai],
+                                          s.vcache[ai], s.capacity, s.part, s.split_len, L.mix + (size_t)b * AS, AS,
+                                          st));
+            }
+            ++ai;
+        }
+        // the n mixer outputs are dense rows of the out projection's width
+        Q3XB_TRY(mm(L, l.out, L.mix, n, L.hidden, 1));
+        Q3XB_TRY(launch_rms(L.hidden, l.post_norm, H, n, L.normed, st));
+        if (c.experts) {
+            MoePrefillArgs a = L.moe;
+            a.router = &l.router;
+            a.gate_up = &l.gate_up;
+            a.down = &l.down;
+            a.experts = c.experts;
+            a.top_k = c.top_k;
+            a.T = n;
+            a.e0 = m.shard.e0;
+            a.local = m.shard.el;
+            a.shared_id = shared_slot(m.shard, i);
+            a.x = L.normed;
+            a.hidden = L.hidden;
+            a.accumulate = 1;
+            a.split = L.gemm_precision == Q3XK_GEMM_SPLIT;
+            Q3XB_TRY(moe_prefill(a, st));
+        } else {
+            Q3XB_TRY(mm(L, l.gate_up, L.normed, n, L.proj, 0));
+            Q3XB_TRY(launch_ffn_swiglu(L.proj, 2 * c.I, n, c.I, L.mix, st));
+            Q3XB_TRY(mm(L, l.down, L.mix, n, L.hidden, 1));
+        }
+    }
+    Q3XB_TRY(launch_rms(L.hidden, m.final_norm, H, n, L.normed, st));
+    Q3XB_TRY(mm(L, m.lm_head, L.normed, n, L.batch_logits, 0));
+    for (int b = 0; b < n; ++b) {
+        State& s = *states[b];
+        if (cudaMemcpyAsync(s.logits, L.batch_logits + (size_t)b * c.V, (size_t)c.V * 4, cudaMemcpyDeviceToDevice,
+                            st) != cudaSuccess)
+            return Q3XK_ECUDA;
+        Q3XB_TRY(launch_advance(s.pos, 1, st));
+    }
+    return Q3XK_OK;
+}
+
 int capture_decode_graph(Model& m, State& s) {
     if (cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return Q3XK_ECUDA;
     const int st = forward_chunk(m, s, 1, true);
@@ -1057,6 +1145,47 @@ int state_forward_impl(Model* m, State* s, const int* tokens, int count, bool lo
     return Q3XK_OK;
 }
 
+// Checks and stream joins around forward_batch.
+int state_forward_batch_impl(Model* m, State** states, const int* tokens, int n) {
+    if (!m || !states || !tokens || n < 1 || n > kMaxBatch) return Q3XK_EINVAL;
+    const Config& c = *m->config;
+    for (int b = 0; b < n; ++b) {
+        State* s = states[b];
+        if (!s || s->model != m || tokens[b] < 0 || tokens[b] >= c.V || s->position + 1 > s->capacity)
+            return Q3XK_EINVAL;
+        for (int q = 0; q < b; ++q)
+            if (states[q] == s) return Q3XK_EINVAL;  // a sequence appears once per step
+        Q3XB_TRY(peer_status(s));
+    }
+    State& L = *states[0];
+    if (L.world > 1) return Q3XK_EUNSUPPORTED;  // batched decode runs on one GPU
+    if (n > L.chunk_capacity) return Q3XK_EINVAL;
+    if (m->layer.empty() || c.V <= 0) return Q3XK_EINVAL;
+    if (cudaSetDevice(L.device) != cudaSuccess) return Q3XK_ECUDA;
+    if (!L.batch_logits && !L.alloc(&L.batch_logits, (size_t)kMaxBatch * c.V)) return Q3XK_ECUDA;
+    // the other sequences' queued work comes first, their later work after the step
+    for (int b = 1; b < n; ++b) {
+        State& s = *states[b];
+        if (!s.batch_event && cudaEventCreateWithFlags(&s.batch_event, cudaEventDisableTiming) != cudaSuccess)
+            return Q3XK_ECUDA;
+        if (cudaEventRecord(s.batch_event, s.stream) != cudaSuccess ||
+            cudaStreamWaitEvent(L.stream, s.batch_event, 0) != cudaSuccess)
+            return Q3XK_ECUDA;
+    }
+    if (cudaMemcpyAsync(L.tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, L.stream) != cudaSuccess)
+        return Q3XK_ECUDA;
+    Q3XB_TRY(forward_batch(*m, states, n));
+    if (n > 1) {
+        if (!L.batch_event && cudaEventCreateWithFlags(&L.batch_event, cudaEventDisableTiming) != cudaSuccess)
+            return Q3XK_ECUDA;
+        if (cudaEventRecord(L.batch_event, L.stream) != cudaSuccess) return Q3XK_ECUDA;
+        for (int b = 1; b < n; ++b)
+            if (cudaStreamWaitEvent(states[b]->stream, L.batch_event, 0) != cudaSuccess) return Q3XK_ECUDA;
+    }
+    for (int b = 0; b < n; ++b) states[b]->position += 1;
+    return Q3XK_OK;
+}
+
 int checkpoint_copy(State* s, bool save) {
     if (!s) return Q3XK_EINVAL;
     if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
@@ -1196,6 +1325,10 @@ void state_copy_logits(const State* state, float* output) {
     const int st = copy_logits_impl(state, output);
     if (st != Q3XK_OK) fatal("state_copy_logits", st);
 }
+void state_forward_batch(Model* model, State* const* states, const int* tokens, int count) {
+    const int st = state_forward_batch_impl(model, const_cast<State**>(states), tokens, count);
+    if (st != Q3XK_OK) fatal("state_forward_batch", st);
+}
 uint32_t model_id(const Model* model) { return model->config->id; }
 int vocab_size() { return 248320; }
 int max_context() { return kMaxContext; }
@@ -1315,6 +1448,10 @@ int q3xb_state_forward(q3xb_model* model, q3xb_state* state, const int* tokens, 
                               compute_logits != 0);
 }
 int q3xb_state_checkpoint_save(q3xb_state* state) { return checkpoint_copy(reinterpret_cast<State*>(state), true); }
+int q3xb_state_forward_batch(q3xb_model* model, q3xb_state* const* states, const int* tokens, int count) {
+    return state_forward_batch_impl(reinterpret_cast<Model*>(model),
+                                    reinterpret_cast<State**>(const_cast<q3xb_state**>(states)), tokens, count);
+}
 int q3xb_state_checkpoint_restore(q3xb_state* state) {
     return checkpoint_copy(reinterpret_cast<State*>(state), false);
 }

@@ -11,8 +11,10 @@
 //    SPLIT (the default of q3xk_gemm): both operands carry a second FP16
 //    plane, x = x_hi + x_lo (x_lo = fp16(x - x_hi), ~22 significant bits in
 //    all) and d*q = w_hi + w_lo exactly (w_lo = fma(q, d, -w_hi) in FP16:
-//    the residual of an 11-bit x 8-bit product always fits), and three MMAs
-//    per K-step accumulate w_hi x_hi + w_hi x_lo + w_lo x_hi in FP32.  The
+//    the residual of an 11-bit x 8-bit product always fits), and the MMAs
+//    accumulate w_hi x_hi + w_hi x_lo + w_lo x_hi in FP32 (two MMAs per
+//    16-wide K-step: w_hi against [x_hi; x_lo] stacked as one 2 BN-token
+//    operand, then w_lo against x_hi).  The
 //    dropped w_lo x_lo term is ~2^-22 of the product, so the result is
 //    FP32-grade (the reference's per-token FP32 matvec, engine.cpp:580-583,
 //    rounds at ~2^-24 per add).
@@ -23,9 +25,16 @@
 //    that layout (value = fp16(d * q), one rounding of the exact product).
 //  * Warp roles: 0 TMA producer, 1 MMA issuer (one thread) and TMEM owner,
 //    2..1+kDqWarps dequantisers, then 4 epilogue warps (TMEM -> registers -> Y).
-//    A 4-stage shared-memory ring and two TMEM accumulators let the dequant,
-//    the MMAs and the epilogue of consecutive tiles overlap.  Persistent CTAs
-//    walk the tiles; every mbarrier wait is bounded.
+//    A ring of raw-weight stages (TMA), a ring of operand stages and two TMEM
+//    accumulators let the loads, the dequant, the MMAs and the epilogue of
+//    consecutive tiles overlap.  Persistent CTAs walk the work units; every
+//    mbarrier wait is bounded.
+//  * Few tokens (T <= 64): token tiles of 16 or 64, a deeper raw ring, and,
+//    when the tiles cannot fill the SMs, split-K: a work unit is one K segment
+//    of a tile (segments are whole raw stages), its FP32 partial goes to the
+//    workspace, and the last unit of a tile to finish (an atomic counter per
+//    tile) adds the segments in segment order and writes Y -- deterministic,
+//    one launch.
 #include <cuda.h>
 
 #include "layers.cuh"
@@ -57,10 +66,17 @@ constexpr int kTileBytesW = BM * BK * 2;   // 16 KB
 // quants (Q8_0: 256 B per row, Q4_0: 128 B) and the 8 FP16 scales of the
 // 256 columns (16 B per row).
 constexpr int RAWK = 256;
-constexpr int kRawStages = Q3XK_GEMM_RAW_STAGES;
+constexpr int kKPerRaw = RAWK / BK;        // MMA K-steps per raw stage
 constexpr int kRawQuantBytes = BM * RAWK;  // sized for Q8_0 (Q4_0 uses half)
 constexpr int kRawScaleBytes = BM * 16;
 constexpr int kRawBytes = kRawQuantBytes + kRawScaleBytes;
+// Split-K bounds: work units (tiles x segments) per call, so the partials
+// fit a fixed part of the workspace, and per-tile counters.
+constexpr int kMaxSplitUnits = 320;
+constexpr int kMaxSplit = 8;
+constexpr int kSplitMaxBN = 64;
+constexpr int kCounterInts = 1024;
+constexpr size_t kPartBytes = (size_t)kMaxSplitUnits * BM * kSplitMaxBN * 4;
 
 __device__ int g_gemm_error;
 
@@ -73,6 +89,12 @@ struct GemmParams {
     float* y;
     int accumulate;
     int tiles_w, tiles_t, ksteps;
+    // Split-K (ksplit > 1, plain mode only): unit u = tile u / ksplit, K
+    // segment u % ksplit of nraw raw stages; partials [unit][BM][BN] in
+    // `part`, arrival counters per tile in `counters` (zero between calls).
+    int ksplit, nraw;
+    float* part;
+    int* counters;
     // Expert-grouped mode (groups > 0): X rows [xoff[e], xoff[e+1]) use expert
     // e of the pool (weight rows e*N ..), their tiles are [tile_off[e],
     // tile_off[e+1]) of the tile space; both arrays live on the device.
@@ -105,15 +127,30 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmParams& p, int tile) {
     return {lo * p.N + wt * BM, wt * BM, x0 + tt * BN, min(BN, count - tt * BN)};
 }
 
+// Work units: tiles (x K segments under split-K).
 template <int BN>
-__device__ __forceinline__ int tile_count(const GemmParams& p) {
-    return p.groups ? __ldg(p.tile_off + p.groups) : p.tiles_w * p.tiles_t;
+__device__ __forceinline__ int unit_count(const GemmParams& p) {
+    return p.groups ? __ldg(p.tile_off + p.groups) : p.tiles_w * p.tiles_t * p.ksplit;
+}
+
+// First K-step of segment s (whole raw stages; segment ksplit ends at ksteps).
+__device__ __forceinline__ int seg_begin(const GemmParams& p, int s) {
+    return s >= p.ksplit ? p.ksteps : min(p.ksteps, (s * p.nraw / p.ksplit) * kKPerRaw);
 }
 
 // Per token-tile-width geometry: BN tokens per tile = MMA N (64, 128, 256).
 // SPLIT stages hold two planes of each operand (hi, lo), so they get fewer
 // stages and at most 128 tokens: 2 x 64 KB (BN 128) or 3 x 48 KB (BN 64),
 // plus the raw weight ring, within the 227 KB of shared memory.
+// Operand stages (kStages) and raw-weight stages (kRaw) per shape, within the
+// 227 KB of shared memory:
+//            FP16                       SPLIT
+//   BN 256   3 x 48 KB + 2 x 34 KB      -
+//   BN 128   3 x 32 KB + 3 x 34 KB      2 x 64 KB + 2 x 34 KB
+//   BN  64   3 x 24 KB + 4 x 34 KB      3 x 48 KB + 2 x 34 KB
+//   BN  16   3 x 18 KB + 4 x 34 KB      2 x 36 KB + 4 x 34 KB
+// Narrow token tiles are weight-streaming bound, so they get the deeper raw
+// ring (more bytes in flight per SM).
 template <int BN, bool SPLIT>
 struct TileN {
     static_assert(!SPLIT || BN <= 128, "split stages hold at most 128 tokens");
@@ -121,25 +158,42 @@ struct TileN {
     static constexpr int kPlanes = SPLIT ? 2 : 1;
     static constexpr int kStageX = kPlanes * kTileBytesX;
     static constexpr int kStageW = kPlanes * kTileBytesW;
-    static constexpr int kStages = SPLIT ? (BN <= 64 ? 3 : 2) : Q3XK_GEMM_STAGES;
-    static constexpr uint32_t kTmemCols = kAcc * BN < 32 ? 32 : kAcc * BN;  // power of 2 >= 32
+    static constexpr int kStages = SPLIT ? (BN == 64 ? 3 : 2) : Q3XK_GEMM_STAGES;
+    static constexpr int kRaw = BN == 256 ? Q3XK_GEMM_RAW_STAGES
+                                : BN == 128 ? (SPLIT ? 2 : 3)
+                                : BN == 64 ? (SPLIT ? 2 : 4)
+                                           : 4;
+    // SPLIT: an accumulator is 2 BN columns wide, [w_hi x_hi + w_lo x_hi | w_hi x_lo]:
+    // the hi and lo X planes sit back to back in shared memory, so one MMA
+    // with N = 2 BN reads w_hi once for both, and a second (N = BN) adds
+    // w_lo x_hi into the first half; the epilogue adds the two halves.
+    static constexpr int kAccCols = kPlanes * BN;
+    static constexpr uint32_t kTmemCols = kAcc * kAccCols < 32 ? 32 : kAcc * kAccCols;  // power of 2 >= 32
     static constexpr uint32_t kIdesc = f16_idesc(BM, BN, 0);
+    static constexpr uint32_t kIdescWide = f16_idesc(BM, kAccCols, 0);
     static constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * (kStageX + kStageW) +
-                                    (size_t)kRawStages * kRawBytes +
-                                    (size_t)(3 * kStages + 2 * kAcc + 2 * kRawStages) * 8 + 16;
+                                    (size_t)kRaw * kRawBytes + (size_t)(3 * kStages + 2 * kAcc + 2 * kRaw) * 8 +
+                                    16;
     static_assert(kSmem <= 232448, "shared memory per CTA");
+    static_assert(BN % 16 == 0 && BN >= 16 && kAccCols <= 256, "MMA N for M = 128");
+    static_assert(kTmemCols <= 512, "tensor memory columns");
 };
 
 // ---- X -> FP16 with a per-token power-of-two scale -----------------------------
 
 // x16lo != nullptr: also the residual plane, x16lo = fp16(x * 2^s - x16) (the
 // subtraction is exact in FP32).
+// counters != nullptr: block 0 also zeroes the split-K arrival counters that
+// the following GEMM uses (they are left at zero by every GEMM, but the
+// caller's workspace starts out undefined).
 __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ x16,
                                                        __half* __restrict__ x16lo, float* __restrict__ tok_scale,
-                                                       int K) {
+                                                       int K, int* __restrict__ counters) {
     griddep_wait();
     griddep_launch_dependents();
     const int t = blockIdx.x;
+    if (counters && t == 0)
+        for (int i = threadIdx.x; i < kCounterInts; i += blockDim.x) counters[i] = 0;
     const float* row = x + (int64_t)t * K;
     uint32_t emax = 0;
     for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
@@ -306,7 +360,54 @@ __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, int
     return false;
 }
 
-// xlomap: the residual plane of X (SPLIT only; ignored otherwise).
+// Named barrier 1 over the 4 epilogue warps; the _and form returns whether
+// every participating thread passed `ok` (so the warps leave together).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ bool epi_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)ok)
+        : "memory");
+    return r != 0;
+}
+
+// Accumulator columns [c0, c0 + 32) (16-token tiles: [c0, c0 + 16)) of this
+// warp's lanes as floats; SPLIT adds the second half (column + BN).
+template <int BN, bool SPLIT>
+__device__ __forceinline__ void tmem_cols(uint32_t taddr, float (&v)[32]) {
+    constexpr int W = BN >= 32 ? 32 : 16;
+    uint32_t r[32], h[32];
+    if constexpr (W == 32) {
+        tmem_ld32(taddr, r);
+        if (SPLIT) tmem_ld32(taddr + BN, h);
+    } else {
+        uint32_t a[16], b[16];
+        tmem_ld16(taddr, a);
+        if (SPLIT) tmem_ld16(taddr + BN, b);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            r[j] = a[j];
+            h[j] = SPLIT ? b[j] : 0u;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) v[j] = SPLIT ? __uint_as_float(r[j]) + __uint_as_float(h[j]) : __uint_as_float(r[j]);
+}
+
+// K-steps [k0, k1) of unit `unit`.
+__device__ __forceinline__ void unit_ksteps(const GemmParams& p, int unit, int& k0, int& k1) {
+    if (p.ksplit > 1) {
+        const int s = unit % p.ksplit;
+        k0 = seg_begin(p, s);
+        k1 = seg_begin(p, s + 1);
+    } else {
+        k0 = 0;
+        k1 = p.ksteps;
+    }
+}
+
 template <int TYPE, int BN, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap xlomap,
@@ -315,21 +416,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     using G = TileN<BN, SPLIT>;
     constexpr int kTileBytesX = G::kTileBytesX;
-    constexpr int kStageX = G::kStageX, kStageW = G::kStageW, kStages = G::kStages;
+    constexpr int kStageX = G::kStageX, kStageW = G::kStageW, kStages = G::kStages, kRaw = G::kRaw;
     constexpr uint32_t kTmemCols = G::kTmemCols;
-    constexpr uint32_t kIdesc = G::kIdesc;
+    constexpr uint32_t kIdesc = G::kIdesc, kIdescWide = G::kIdescWide;
+    constexpr int kAccCols = G::kAccCols;
     uint8_t* sx = smem;                                // kStages x planes x BN x 128 B (hi, then lo)
     uint8_t* sw = smem + kStages * kStageX;            // kStages x planes x 16 KB (hi, then lo)
-    uint8_t* sraw = sw + kStages * kStageW;            // kRawStages x (32 + 2) KB
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sraw + kRawStages * kRawBytes);
+    uint8_t* sraw = sw + kStages * kStageW;            // kRaw x (32 + 2) KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sraw + kRaw * kRawBytes);
     uint64_t* full = bars;   // X bytes landed and every dequant warp arrived
     uint64_t* empty = bars + 2 * kStages;
     uint64_t* acc_full = bars + 3 * kStages;
     uint64_t* acc_empty = acc_full + kAcc;
     uint64_t* raw_full = acc_empty + kAcc;
-    uint64_t* raw_empty = raw_full + kRawStages;
-    uint32_t* tmem_base_p = reinterpret_cast<uint32_t*>(raw_empty + kRawStages);
+    uint64_t* raw_empty = raw_full + kRaw;
+    uint32_t* tmem_base_p = reinterpret_cast<uint32_t*>(raw_empty + kRaw);
     int* cta_err = reinterpret_cast<int*>(tmem_base_p + 1);
+    int* last_flag = cta_err + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -341,7 +444,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);
         }
-        for (int r = 0; r < kRawStages; ++r) {
+        for (int r = 0; r < kRaw; ++r) {
             mbar_init(&raw_full[r], 1);
             mbar_init(&raw_empty[r], kDqWarps);
         }
@@ -357,31 +460,45 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem = *tmem_base_p;
     griddep_launch_dependents();
-    griddep_wait();  // X16, the scales and (grouped) the tile table come from earlier kernels
-    const int tiles = tile_count<BN>(p);
+    griddep_wait();  // X16, the scales, the counters and (grouped) the tile table come from earlier kernels
+    const int units = unit_count<BN>(p);
+    const int S = p.groups ? 1 : p.ksplit;
 
     if (warp == 0) {
-        // ---------------- TMA producer: X16 tiles and raw weight stages ----------------
+        // ---------------- TMA producers ----------------
+        // Lane 0 streams the raw weight stages, lane 1 the X tiles: separate
+        // threads, so the raw ring runs as far ahead as its own depth allows
+        // instead of waiting on the (shallower) operand ring.
         if (lane == 0) {
             const int qdiv = TYPE == Q3XK_Q4_0 ? 2 : 1;  // quant bytes per column
             const uint32_t raw_tx = (uint32_t)(BM * (RAWK / qdiv) + kRawScaleBytes);
-            int it = 0, rit = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x) {
-                const TileCoord tc = tile_coord<BN>(p, tile);
+            int rit = 0;
+            for (int unit = blockIdx.x; unit < units && !*(volatile int*)cta_err; unit += gridDim.x) {
+                const TileCoord tc = tile_coord<BN>(p, unit / S);
+                int k0, k1;
+                unit_ksteps(p, unit, k0, k1);
                 bool ok = true;
-                for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
-                    if (ks % (RAWK / BK) == 0) {
-                        const int r = rit % kRawStages;
-                        if (rit >= kRawStages && !wait_or_flag(&raw_empty[r], ((rit / kRawStages) - 1) & 1, cta_err)) {
-                            ok = false;
-                            break;
-                        }
-                        uint8_t* dst = sraw + r * kRawBytes;
-                        mbar_arrive_expect_tx(&raw_full[r], raw_tx);
-                        tma_load_2d(dst, &qmap, ks * BK / qdiv, tc.w_row, &raw_full[r]);
-                        tma_load_2d(dst + kRawQuantBytes, &smap, ks * BK / 32, tc.w_row, &raw_full[r]);
-                        ++rit;
+                for (int ks = k0; ks < k1; ks += kKPerRaw, ++rit) {
+                    const int r = rit % kRaw;
+                    if (rit >= kRaw && !wait_or_flag(&raw_empty[r], ((rit / kRaw) - 1) & 1, cta_err)) {
+                        ok = false;
+                        break;
                     }
+                    uint8_t* dst = sraw + r * kRawBytes;
+                    mbar_arrive_expect_tx(&raw_full[r], raw_tx);
+                    tma_load_2d(dst, &qmap, ks * BK / qdiv, tc.w_row, &raw_full[r]);
+                    tma_load_2d(dst + kRawQuantBytes, &smap, ks * BK / 32, tc.w_row, &raw_full[r]);
+                }
+                if (!ok) break;
+            }
+        } else if (lane == 1) {
+            int it = 0;
+            for (int unit = blockIdx.x; unit < units && !*(volatile int*)cta_err; unit += gridDim.x) {
+                const TileCoord tc = tile_coord<BN>(p, unit / S);
+                int k0, k1;
+                unit_ksteps(p, unit, k0, k1);
+                bool ok = true;
+                for (int ks = k0; ks < k1; ++ks, ++it) {
                     const int s = it % kStages;
                     if (it >= kStages && !wait_or_flag(&empty[s], ((it / kStages) - 1) & 1, cta_err)) {
                         ok = false;
@@ -398,13 +515,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             int it = 0, lt = 0;
-            for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x, ++lt) {
+            for (int unit = blockIdx.x; unit < units && !*(volatile int*)cta_err; unit += gridDim.x, ++lt) {
+                int k0, k1;
+                unit_ksteps(p, unit, k0, k1);
                 const int b = lt % kAcc;
                 if (lt >= kAcc && !wait_or_flag(&acc_empty[b], ((lt / kAcc) - 1) & 1, cta_err)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + b * BN;
+                const uint32_t d_tmem = tmem + b * kAccCols;
                 bool ok = true;
-                for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
+                for (int ks = k0; ks < k1; ++ks, ++it) {
                     const int s = it % kStages;
                     const uint32_t ph = (it / kStages) & 1;
                     if (!wait_or_flag(&full[s], ph, cta_err)) {
@@ -416,11 +535,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t ah = sw128_desc(a0 + kk * 32), bh = sw128_desc(b0 + kk * 32);
-                        umma_f16(d_tmem, ah, bh, kIdesc, (ks | kk) ? 1u : 0u);
-                        if (SPLIT) {  // + w_hi x_lo + w_lo x_hi
-                            umma_f16(d_tmem, ah, sw128_desc(b0 + kTileBytesX + kk * 32), kIdesc, 1u);
+                        // SPLIT: B = [x_hi; x_lo] (2 BN rows) -> both halves of the accumulator
+                        umma_f16(d_tmem, ah, bh, kIdescWide, (ks > k0 || kk) ? 1u : 0u);
+                        if (SPLIT)  // + w_lo x_hi into the first half
                             umma_f16(d_tmem, sw128_desc(a0 + kTileBytesW + kk * 32), bh, kIdesc, 1u);
-                        }
                     }
                     umma_commit(&empty[s]);  // stage s free once these MMAs finish
                 }
@@ -432,14 +550,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         // ---------------- dequantisers ----------------
         const int d = threadIdx.x - 64;
         int it = 0, rit = 0;
-        for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x) {
+        for (int unit = blockIdx.x; unit < units && !*(volatile int*)cta_err; unit += gridDim.x) {
+            int k0, k1;
+            unit_ksteps(p, unit, k0, k1);
             bool ok = true;
-            for (int ks = 0; ks < p.ksteps; ++ks, ++it) {
-                const int kk = ks % (RAWK / BK);
-                const int r = rit % kRawStages;
+            for (int ks = k0; ks < k1; ++ks, ++it) {
+                const int kk = (ks - k0) % kKPerRaw;
+                const int r = rit % kRaw;
                 if (kk == 0) {
                     int good = 1;
-                    if (lane == 0) good = wait_or_flag(&raw_full[r], (rit / kRawStages) & 1, cta_err);
+                    if (lane == 0) good = wait_or_flag(&raw_full[r], (rit / kRaw) & 1, cta_err);
                     good = __shfl_sync(0xffffffffu, good, 0);
                     if (!good) {
                         ok = false;
@@ -460,7 +580,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                 fence_proxy_async_smem();  // generic-proxy writes -> tensor core reads
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
-                if (kk == RAWK / BK - 1 || ks == p.ksteps - 1) {
+                if (kk == kKPerRaw - 1 || ks == k1 - 1) {
                     if (lane == 0) mbar_arrive(&raw_empty[r]);
                     ++rit;
                 }
@@ -468,35 +588,94 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             if (!ok) break;
         }
     } else {
-        // ---------------- epilogue (TMEM -> Y) ----------------
+        // ---------------- epilogue (TMEM -> Y, or -> split-K partial) ----------------
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int m = 32 * q + lane;  // row of the tile
         int lt = 0;
-        for (int tile = blockIdx.x; tile < tiles && !*(volatile int*)cta_err; tile += gridDim.x, ++lt) {
+        for (int unit = blockIdx.x; unit < units; unit += gridDim.x, ++lt) {
+            const int tile = unit / S;
             const TileCoord tc = tile_coord<BN>(p, tile);
             const int b = lt % kAcc;
             int good = 1;
             if (lane == 0) good = wait_or_flag(&acc_full[b], (lt / kAcc) & 1, cta_err);
             good = __shfl_sync(0xffffffffu, good, 0);
-            if (!good) break;
+            if (!epi_all(good)) break;  // all 4 warps leave together
             tc_fence_after();
-            const int n = tc.n0 + 32 * q + lane;
+            const int n = tc.n0 + m;
+            if (S == 1) {
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + b * BN + c0, r);
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float r[32];
+                    tmem_cols<BN, SPLIT>(tmem + ((uint32_t)(32 * q) << 16) + b * kAccCols + c0, r);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (c0 + j < tc.t_valid && n < p.N) {
-                        const int t = tc.x_row + c0 + j;
-                        const float v = __uint_as_float(r[j]) * __ldg(&p.tok_scale[t]);
-                        float* yp = p.y + (int64_t)t * p.N + n;
-                        *yp = p.accumulate ? *yp + v : v;
+                    for (int j = 0; j < (BN < 32 ? BN : 32); ++j) {
+                        if (c0 + j < tc.t_valid && n < p.N) {
+                            const int t = tc.x_row + c0 + j;
+                            const float v = r[j] * __ldg(&p.tok_scale[t]);
+                            float* yp = p.y + (int64_t)t * p.N + n;
+                            *yp = p.accumulate ? *yp + v : v;
+                        }
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                continue;
+            }
+            // split-K: this segment's raw accumulators -> part[unit][m][c]
+            float* mine = p.part + (size_t)unit * BM * BN + (size_t)m * BN;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                float r[32];
+                tmem_cols<BN, SPLIT>(tmem + ((uint32_t)(32 * q) << 16) + b * kAccCols + c0, r);
+#pragma unroll
+                for (int j = 0; j < (BN < 32 ? BN : 32); j += 4)
+                    __stcg(reinterpret_cast<float4*>(mine + c0 + j), make_float4(r[j], r[j + 1], r[j + 2], r[j + 3]));
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[b]);
+            if (lane == 0) mbar_arrive(&acc_empty[b]);  // TMEM reusable; the partial is in memory
+            __threadfence();
+            epi_sync();
+            if (warp == kEpiWarp0 && lane == 0) *last_flag = atomicAdd(&p.counters[tile], 1) == S - 1;
+            epi_sync();
+            if (*(volatile int*)last_flag) {
+                // every segment of this tile has landed: add them in segment order,
+                // 8 columns at a time with every segment's loads in flight at once
+                __threadfence();
+                const float* base = p.part + (size_t)tile * S * BM * BN + (size_t)m * BN;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN && c0 < tc.t_valid; c0 += 8) {
+                    float4 a[kMaxSplit][2];
+#pragma unroll
+                    for (int sg = 0; sg < kMaxSplit; ++sg)
+                        if (sg < S) {
+                            const float4* src = reinterpret_cast<const float4*>(base + (size_t)sg * BM * BN + c0);
+                            a[sg][0] = __ldcg(src);
+                            a[sg][1] = __ldcg(src + 1);
+                        }
+                    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int sg = 0; sg < kMaxSplit; ++sg)
+                        if (sg < S) {
+                            v[0] += a[sg][0].x; v[1] += a[sg][0].y; v[2] += a[sg][0].z; v[3] += a[sg][0].w;
+                            v[4] += a[sg][1].x; v[5] += a[sg][1].y; v[6] += a[sg][1].z; v[7] += a[sg][1].w;
+                        }
+                    if (n < p.N) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            if (c0 + j < tc.t_valid) {
+                                const int t = tc.x_row + c0 + j;
+                                const float r = v[j] * __ldg(&p.tok_scale[t]);
+                                float* yp = p.y + (int64_t)t * p.N + n;
+                                *yp = p.accumulate ? *yp + r : r;
+                            }
+                        }
+                    }
+                }
+                epi_sync();
+                if (warp == kEpiWarp0 && lane == 0) p.counters[tile] = 0;  // ready for the next call
+            }
         }
     }
     tc_fence_before();
@@ -537,9 +716,10 @@ int sm_count() {
 
 }  // namespace
 
-int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s) {
+int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s,
+                    int* counters) {
     if (K % 8) return Q3XK_EINVAL;  // TMA row stride of X16 must be a multiple of 16 bytes
-    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, x16lo, tok_scale, K) != cudaSuccess)
+    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, x16lo, tok_scale, K, counters) != cudaSuccess)
         return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;
@@ -560,12 +740,17 @@ constexpr KernSlot slot_of() {
     return KernSlot{gemm_kernel<TYPE, BN, SPLIT>, TileN<BN, SPLIT>::kSmem, false};
 }
 
-// [type: Q8_0, Q4_0][BN: 64, 128, 256][FP16, SPLIT]; split has no 256-token tile.
-KernSlot g_kernels[2][3][2] = {
-    {{slot_of<Q3XK_Q8_0, 64, false>(), slot_of<Q3XK_Q8_0, 64, true>()},
+constexpr int kBNs[4] = {16, 64, 128, 256};
+int bn_index(int bn) { return bn == 16 ? 0 : bn == 64 ? 1 : bn == 128 ? 2 : 3; }
+
+// [type: Q8_0, Q4_0][BN: 16, 64, 128, 256][FP16, SPLIT]; split has no 256-token tile.
+KernSlot g_kernels[2][4][2] = {
+    {{slot_of<Q3XK_Q8_0, 16, false>(), slot_of<Q3XK_Q8_0, 16, true>()},
+     {slot_of<Q3XK_Q8_0, 64, false>(), slot_of<Q3XK_Q8_0, 64, true>()},
      {slot_of<Q3XK_Q8_0, 128, false>(), slot_of<Q3XK_Q8_0, 128, true>()},
      {slot_of<Q3XK_Q8_0, 256, false>(), KernSlot{nullptr, 0, false}}},
-    {{slot_of<Q3XK_Q4_0, 64, false>(), slot_of<Q3XK_Q4_0, 64, true>()},
+    {{slot_of<Q3XK_Q4_0, 16, false>(), slot_of<Q3XK_Q4_0, 16, true>()},
+     {slot_of<Q3XK_Q4_0, 64, false>(), slot_of<Q3XK_Q4_0, 64, true>()},
      {slot_of<Q3XK_Q4_0, 128, false>(), slot_of<Q3XK_Q4_0, 128, true>()},
      {slot_of<Q3XK_Q4_0, 256, false>(), KernSlot{nullptr, 0, false}}},
 };
@@ -580,17 +765,37 @@ bool encode_x_map(EncodeTiled enc, CUtensorMap* map, const __half* x16, int T, i
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// K segments per tile when the tiles alone leave SMs idle: the count that
+// minimises (waves of units) x (raw stages per segment), with a small charge
+// for the partials' round trip; bounded by kMaxSplit, by the raw stages of a
+// row and by the workspace's kMaxSplitUnits.
+int choose_ksplit(int tiles, int nraw, int sms) {
+    if (tiles >= sms) return 1;
+    int best = 1;
+    double best_cost = 1e30;
+    for (int S = 1; S <= kMaxSplit && S <= nraw && tiles * S <= kMaxSplitUnits; ++S) {
+        const int waves = (tiles * S + sms - 1) / sms;
+        const double cost = (double)waves * ((nraw + S - 1) / S) + (S > 1 ? 0.5 : 0.0);
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = S;
+        }
+    }
+    return best;
+}
+
 }  // namespace
 
 int gemm_f16(const q3xk_matrix* w, const __half* x16, const __half* x16lo, const float* tok_scale, int T, float* y,
-             int accumulate, const GemmGroups* groups, int bn_hint, cudaStream_t s) {
+             int accumulate, const GemmGroups* groups, int bn_hint, cudaStream_t s, const GemmSplitWs* splitws) {
     const int K = w->cols;
     const bool split = x16lo != nullptr;
     if (K % 8 || ((uintptr_t)x16 & 15) || ((uintptr_t)x16lo & 15) || ((uintptr_t)w->data & 15)) return Q3XK_EALIGN;
-    // Token tile = MMA N: the smallest of 64/128/256 that covers T, else 256
-    // (split: at most 128; grouped: 64).
-    int bn = groups ? 64 : bn_hint ? bn_hint : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+    // Token tile = MMA N: the smallest of 16/64/128/256 that covers T, else
+    // 256 (split precision: at most 128; grouped: 64).
+    int bn = groups ? 64 : bn_hint ? bn_hint : T <= 16 ? 16 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
     if (split && bn > 128) bn = 128;
+    if (bn != 16 && bn != 64 && bn != 128 && bn != 256) return Q3XK_EINVAL;
     EncodeTiled enc = encode_fn();
     if (!enc) return Q3XK_ECUDA;
     CUtensorMap map, lomap;
@@ -633,12 +838,21 @@ int gemm_f16(const q3xk_matrix* w, const __half* x16, const __half* x16lo, const
     p.tiles_w = (w->rows + BM - 1) / BM;
     p.tiles_t = (T + bn - 1) / bn;
     p.ksteps = (K + BK - 1) / BK;
+    p.nraw = (p.ksteps + kKPerRaw - 1) / kKPerRaw;
+    p.ksplit = 1;
     if (groups) {
         p.groups = groups->groups;
         p.xoff = groups->xoff;
         p.tile_off = groups->tile_off;
+    } else if (splitws && bn <= kSplitMaxBN) {
+        p.ksplit = choose_ksplit(p.tiles_w * p.tiles_t, p.nraw, sm_count());
+        if (p.ksplit > 1) {
+            if (p.tiles_w * p.tiles_t > kCounterInts) return Q3XK_EUNSUPPORTED;  // cannot happen: tiles < SMs
+            p.part = splitws->part;
+            p.counters = splitws->counters;
+        }
     }
-    KernSlot& ks = g_kernels[w->type == Q3XK_Q8_0 ? 0 : 1][bn == 64 ? 0 : bn == 128 ? 1 : 2][split ? 1 : 0];
+    KernSlot& ks = g_kernels[w->type == Q3XK_Q8_0 ? 0 : 1][bn_index(bn)][split ? 1 : 0];
     if (!ks.fn) return Q3XK_EUNSUPPORTED;
     if (!ks.configured) {
         if (cudaFuncSetAttribute(ks.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks.smem) != cudaSuccess)
@@ -646,8 +860,8 @@ int gemm_f16(const q3xk_matrix* w, const __half* x16, const __half* x16lo, const
         ks.configured = true;
     }
     // grouped: the tile count is only known on the device -> one CTA per SM
-    const int tiles = groups ? sm_count() : p.tiles_w * p.tiles_t;
-    const int grid = tiles < sm_count() ? tiles : sm_count();
+    const int units = groups ? sm_count() : p.tiles_w * p.tiles_t * p.ksplit;
+    const int grid = units < sm_count() ? units : sm_count();
     const cudaError_t e1 = launch_pdl(ks.fn, dim3(grid), dim3(kThreads), ks.smem, s, map, lomap, qmap, smap, p);
     if (e1 != cudaSuccess) return Q3XK_ECUDA;
     count_launch();
@@ -661,6 +875,25 @@ int gemm_clear_error() {
     return cuda_status(cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof zero));
 }
 
+namespace {
+
+// Workspace of one call: two FP16 planes of X (hi, lo), each 256-byte
+// aligned, the token scales, the split-K counters, then the split-K partials.
+struct WsLayout {
+    size_t plane, scale_off, counter_off, part_off, total;
+};
+WsLayout ws_layout(int T, int K) {
+    WsLayout l;
+    l.plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
+    l.scale_off = 2 * l.plane;
+    l.counter_off = l.scale_off + (((size_t)T * 4 + 255) & ~(size_t)255);
+    l.part_off = l.counter_off + (size_t)kCounterInts * 4;
+    l.total = l.part_off + kPartBytes;
+    return l;
+}
+
+}  // namespace
+
 }  // namespace q3xk
 
 using namespace q3xk;
@@ -669,9 +902,7 @@ extern "C" {
 
 int q3xk_gemm_workspace_bytes(int T, int K, size_t* bytes) {
     if (!bytes || T <= 0 || K <= 0) return Q3XK_EINVAL;
-    // two FP16 planes of X (hi, lo), each 256-byte aligned, then the token scales
-    const size_t plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
-    *bytes = 2 * plane + (size_t)T * 4;
+    *bytes = ws_layout(T, K).total;
     return Q3XK_OK;
 }
 
@@ -681,22 +912,20 @@ int q3xk_gemm_ex(const q3xk_matrix* w, const float* x, int T, float* y, int accu
     if (precision != Q3XK_GEMM_SPLIT && precision != Q3XK_GEMM_FP16) return Q3XK_EINVAL;
     if (w->type != Q3XK_Q8_0 && w->type != Q3XK_Q4_0) return Q3XK_EUNSUPPORTED;
     if (w->cols % kBlock || w->row_stride != row_record_bytes(w->type, w->cols)) return Q3XK_EINVAL;
-    size_t need = 0;
-    q3xk_gemm_workspace_bytes(T, w->cols, &need);
-    if (!workspace || workspace_bytes < need) return Q3XK_EWORKSPACE;
+    const WsLayout l = ws_layout(T, w->cols);
+    if (!workspace || workspace_bytes < l.total) return Q3XK_EWORKSPACE;
     if (((uintptr_t)workspace & 255) || ((uintptr_t)x & 15) || ((uintptr_t)w->data & 15) || ((uintptr_t)y & 3))
         return Q3XK_EALIGN;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int K = w->cols;
-    const size_t plane = ((size_t)T * K * 2 + 255) & ~(size_t)255;
-    __half* x16 = static_cast<__half*>(workspace);
-    __half* x16lo = precision == Q3XK_GEMM_SPLIT
-                        ? reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + plane)
-                        : nullptr;
-    float* tok_scale = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 2 * plane);
-    const int st = launch_x_to_f16(x, T, K, x16, x16lo, tok_scale, s);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    __half* x16 = reinterpret_cast<__half*>(ws);
+    __half* x16lo = precision == Q3XK_GEMM_SPLIT ? reinterpret_cast<__half*>(ws + l.plane) : nullptr;
+    float* tok_scale = reinterpret_cast<float*>(ws + l.scale_off);
+    const GemmSplitWs sw{reinterpret_cast<float*>(ws + l.part_off), reinterpret_cast<int*>(ws + l.counter_off)};
+    const int st = launch_x_to_f16(x, T, K, x16, x16lo, tok_scale, s, sw.counters);
     if (st != Q3XK_OK) return st;
-    return gemm_f16(w, x16, x16lo, tok_scale, T, y, accumulate, nullptr, 0, s);
+    return gemm_f16(w, x16, x16lo, tok_scale, T, y, accumulate, nullptr, 0, s, &sw);
 }
 
 int q3xk_gemm(const q3xk_matrix* w, const float* x, int T, float* y, int accumulate, void* workspace,

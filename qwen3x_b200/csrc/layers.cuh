@@ -38,13 +38,23 @@ struct GemmGroups {
     const int* tile_off;
 };
 // X (FP32 [T][K]) -> FP16 with a per-row power-of-two scale (tok_scale = 2^-s);
-// x16lo != nullptr also gets the residual plane fp16(x 2^s - x16).
-int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s);
+// x16lo != nullptr also gets the residual plane fp16(x 2^s - x16);
+// counters != nullptr: zeroes the GEMM's split-K counters too.
+int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s,
+                    int* counters = nullptr);
+// Split-K scratch of a plain (non-grouped) GEMM call: partials and per-tile
+// arrival counters (zero before the call, left zero after it).
+struct GemmSplitWs {
+    float* part;
+    int* counters;
+};
 // Y[T][N] (+)= X16 W^T * tok_scale on tcgen05; `groups` selects the expert-grouped tiles
 // (then W is a pool of groups experts and T the packed row count).  x16lo !=
 // nullptr selects the split precision (X = x16 + x16lo, three MMAs per K-step).
+// splitws != nullptr allows split-K for few-token calls.
 int gemm_f16(const q3xk_matrix* w, const __half* x16, const __half* x16lo, const float* tok_scale, int T, float* y,
-             int accumulate, const GemmGroups* groups, int bn_hint, cudaStream_t s);
+             int accumulate, const GemmGroups* groups, int bn_hint, cudaStream_t s,
+             const GemmSplitWs* splitws = nullptr);
 size_t gemm_grouped_tile_width();
 // Resets the GEMM's device error word (bounded mbarrier waits that gave up).
 int gemm_clear_error();

@@ -87,6 +87,34 @@ def test_gemm_activation_range(cuda, precision):
     assert check(Y, packed, Q8_0, rows, cols, X) <= TOL[precision]
 
 
+@pytest.mark.parametrize("precision", PRECISIONS)
+@pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
+@pytest.mark.parametrize("T,rows,cols,add", [(2, 4096, 4096, False), (8, 4096, 4096, True), (16, 4096, 12288, False),
+                                             (17, 4096, 4096, False), (64, 4096, 4096, True),
+                                             (8, 12288, 4096, False), (5, 2048, 5120, True)])
+def test_gemm_few_tokens_split_k(cuda, mtype, T, rows, cols, add, precision):
+    """Few tokens: 16- and 64-token tiles with K split over CTAs (tiles < SMs;
+    the last segment to finish adds the partials in segment order).  Two calls
+    give bit-identical results (deterministic reduction, counters reset)."""
+    import torch
+
+    packed = quant.quantize(quant.gaussian((rows, cols), 40 + T, 0.02), mtype)
+    X = quant.gaussian((T, cols), 41 + T)
+    Y0 = quant.gaussian((T, rows), 42) if add else None
+    Y = run_gemm(cuda, packed, mtype, rows, cols, X, Y0, precision=precision)
+    assert np.all(np.isfinite(Y))
+    assert check(Y, packed, mtype, rows, cols, X, Y0=Y0) <= TOL[precision]
+    lin = Linear.from_packed(packed, mtype, rows, cols, device=cuda)
+    Xd = torch.from_numpy(X).to(cuda)
+    outs = []
+    for _ in range(2):
+        Yd = torch.zeros(T, rows, device=cuda)
+        batch_mv(lin, Xd, Yd, precision=precision)
+        outs.append(Yd)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("mtype", [Q8_0, Q4_0])
 def test_gemm_split_weight_residual_exact(cuda, mtype):
     """Split precision holds d*q exactly (w_hi + w_lo): with X = one-hot rows
