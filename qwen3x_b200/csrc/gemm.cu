@@ -138,19 +138,20 @@ __device__ __forceinline__ int seg_begin(const GemmParams& p, int s) {
     return s >= p.ksplit ? p.ksteps : min(p.ksteps, (s * p.nraw / p.ksplit) * kKPerRaw);
 }
 
-// Per token-tile-width geometry: BN tokens per tile = MMA N (64, 128, 256).
-// SPLIT stages hold two planes of each operand (hi, lo), so they get fewer
-// stages and at most 128 tokens: 2 x 64 KB (BN 128) or 3 x 48 KB (BN 64),
-// plus the raw weight ring, within the 227 KB of shared memory.
-// Operand stages (kStages) and raw-weight stages (kRaw) per shape, within the
-// 227 KB of shared memory:
-//            FP16                       SPLIT
-//   BN 256   3 x 48 KB + 2 x 34 KB      -
-//   BN 128   3 x 32 KB + 3 x 34 KB      2 x 64 KB + 2 x 34 KB
-//   BN  64   3 x 24 KB + 4 x 34 KB      3 x 48 KB + 2 x 34 KB
-//   BN  16   3 x 18 KB + 4 x 34 KB      2 x 36 KB + 4 x 34 KB
-// Narrow token tiles are weight-streaming bound, so they get the deeper raw
-// ring (more bytes in flight per SM).
+// Per token-tile-width geometry: BN tokens per tile = MMA N (16, 64, 128,
+// 256).  SPLIT stages hold two planes of each operand (hi, lo), so they get
+// fewer stages and at most 128 tokens.
+// Three rings per shape, within the 227 KB of shared memory: dequantised
+// weights (kStages x planes x 16 KB), X tiles (kXStages x planes x BN x 128 B,
+// loaded by their own producer thread, so an X tile's TMA round trip is not
+// in the weight ring's recycle loop) and raw weights (kRaw x 34 KB):
+//            FP16                          SPLIT
+//   BN 256   A 3, X 3, raw 2  (212 KB)     -
+//   BN 128   A 3, X 3, raw 3  (198 KB)     A 2, X 2, raw 2  (196 KB)
+//   BN  64   A 3, X 4, raw 4  (216 KB)     A 2, X 3, raw 3  (214 KB)
+//   BN  16   A 3, X 8, raw 4  (200 KB)     A 2, X 8, raw 3  (198 KB)
+// Narrow token tiles are weight-streaming bound: they get the deeper raw and
+// X rings.
 template <int BN, bool SPLIT>
 struct TileN {
     static_assert(!SPLIT || BN <= 128, "split stages hold at most 128 tokens");
@@ -158,11 +159,11 @@ struct TileN {
     static constexpr int kPlanes = SPLIT ? 2 : 1;
     static constexpr int kStageX = kPlanes * kTileBytesX;
     static constexpr int kStageW = kPlanes * kTileBytesW;
-    static constexpr int kStages = SPLIT ? (BN == 64 ? 3 : 2) : Q3XK_GEMM_STAGES;
+    static constexpr int kStages = SPLIT ? 2 : Q3XK_GEMM_STAGES;
+    static constexpr int kXStages = BN == 16 ? 8 : BN == 64 ? (SPLIT ? 3 : 4) : SPLIT ? 2 : Q3XK_GEMM_STAGES;
     static constexpr int kRaw = BN == 256 ? Q3XK_GEMM_RAW_STAGES
                                 : BN == 128 ? (SPLIT ? 2 : 3)
-                                : BN == 64 ? (SPLIT ? 2 : 4)
-                                           : 4;
+                                : SPLIT ? 3 : 4;
     // SPLIT: an accumulator is 2 BN columns wide, [w_hi x_hi + w_lo x_hi | w_hi x_lo]:
     // the hi and lo X planes sit back to back in shared memory, so one MMA
     // with N = 2 BN reads w_hi once for both, and a second (N = BN) adds
@@ -171,9 +172,9 @@ struct TileN {
     static constexpr uint32_t kTmemCols = kAcc * kAccCols < 32 ? 32 : kAcc * kAccCols;  // power of 2 >= 32
     static constexpr uint32_t kIdesc = f16_idesc(BM, BN, 0);
     static constexpr uint32_t kIdescWide = f16_idesc(BM, kAccCols, 0);
-    static constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * (kStageX + kStageW) +
-                                    (size_t)kRaw * kRawBytes + (size_t)(3 * kStages + 2 * kAcc + 2 * kRaw) * 8 +
-                                    16;
+    static constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kXStages * kStageX +
+                                    (size_t)kStages * kStageW + (size_t)kRaw * kRawBytes +
+                                    (size_t)(2 * kStages + 2 * kXStages + 2 * kAcc + 2 * kRaw) * 8 + 16;
     static_assert(kSmem <= 232448, "shared memory per CTA");
     static_assert(BN % 16 == 0 && BN >= 16 && kAccCols <= 256, "MMA N for M = 128");
     static_assert(kTmemCols <= 512, "tensor memory columns");
@@ -417,16 +418,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     using G = TileN<BN, SPLIT>;
     constexpr int kTileBytesX = G::kTileBytesX;
     constexpr int kStageX = G::kStageX, kStageW = G::kStageW, kStages = G::kStages, kRaw = G::kRaw;
+    constexpr int kXStages = G::kXStages;
     constexpr uint32_t kTmemCols = G::kTmemCols;
     constexpr uint32_t kIdesc = G::kIdesc, kIdescWide = G::kIdescWide;
     constexpr int kAccCols = G::kAccCols;
-    uint8_t* sx = smem;                                // kStages x planes x BN x 128 B (hi, then lo)
-    uint8_t* sw = smem + kStages * kStageX;            // kStages x planes x 16 KB (hi, then lo)
+    uint8_t* sx = smem;                                // kXStages x planes x BN x 128 B (hi, then lo)
+    uint8_t* sw = smem + kXStages * kStageX;           // kStages x planes x 16 KB (hi, then lo)
     uint8_t* sraw = sw + kStages * kStageW;            // kRaw x (32 + 2) KB
     uint64_t* bars = reinterpret_cast<uint64_t*>(sraw + kRaw * kRawBytes);
-    uint64_t* full = bars;   // X bytes landed and every dequant warp arrived
-    uint64_t* empty = bars + 2 * kStages;
-    uint64_t* acc_full = bars + 3 * kStages;
+    uint64_t* full = bars;                 // weight stage: every dequant warp arrived
+    uint64_t* empty = full + kStages;      // weight stage: its MMAs are done
+    uint64_t* xfull = empty + kStages;     // X stage: bytes landed
+    uint64_t* xempty = xfull + kXStages;   // X stage: its MMAs are done
+    uint64_t* acc_full = xempty + kXStages;
     uint64_t* acc_empty = acc_full + kAcc;
     uint64_t* raw_full = acc_empty + kAcc;
     uint64_t* raw_empty = raw_full + kRaw;
@@ -437,8 +441,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1 + kDqWarps);
+            mbar_init(&full[s], kDqWarps);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kXStages; ++s) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&xempty[s], 1);
         }
         for (int b = 0; b < kAcc; ++b) {
             mbar_init(&acc_full[b], 1);
@@ -460,7 +468,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem = *tmem_base_p;
     griddep_launch_dependents();
-    griddep_wait();  // X16, the scales, the counters and (grouped) the tile table come from earlier kernels
+    // X16, the scales, the counters, Y and (grouped) the tile table come from
+    // earlier kernels.  The raw-weight producer of a plain GEMM reads none of
+    // them (weights are immutable, its tiles are arithmetic on the
+    // parameters), so it starts streaming while the previous kernel -- the X
+    // conversion -- is still running.
+    if (!(warp == 0 && lane == 0 && !p.groups)) griddep_wait();
     const int units = unit_count<BN>(p);
     const int S = p.groups ? 1 : p.ksplit;
 
@@ -499,14 +512,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                 unit_ksteps(p, unit, k0, k1);
                 bool ok = true;
                 for (int ks = k0; ks < k1; ++ks, ++it) {
-                    const int s = it % kStages;
-                    if (it >= kStages && !wait_or_flag(&empty[s], ((it / kStages) - 1) & 1, cta_err)) {
+                    const int s = it % kXStages;
+                    if (it >= kXStages && !wait_or_flag(&xempty[s], ((it / kXStages) - 1) & 1, cta_err)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], kStageX);
-                    tma_load_2d(sx + s * kStageX, &xmap, ks * BK, tc.x_row, &full[s]);
-                    if (SPLIT) tma_load_2d(sx + s * kStageX + kTileBytesX, &xlomap, ks * BK, tc.x_row, &full[s]);
+                    mbar_arrive_expect_tx(&xfull[s], kStageX);
+                    tma_load_2d(sx + s * kStageX, &xmap, ks * BK, tc.x_row, &xfull[s]);
+                    if (SPLIT) tma_load_2d(sx + s * kStageX + kTileBytesX, &xlomap, ks * BK, tc.x_row, &xfull[s]);
                 }
                 if (!ok) break;
             }
@@ -524,14 +537,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                 const uint32_t d_tmem = tmem + b * kAccCols;
                 bool ok = true;
                 for (int ks = k0; ks < k1; ++ks, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1;
-                    if (!wait_or_flag(&full[s], ph, cta_err)) {
+                    const int s = it % kStages, sxi = it % kXStages;
+                    if (!wait_or_flag(&xfull[sxi], (it / kXStages) & 1, cta_err) ||
+                        !wait_or_flag(&full[s], (it / kStages) & 1, cta_err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sw + s * kStageW), b0 = smem_u32(sx + s * kStageX);
+                    const uint32_t a0 = smem_u32(sw + s * kStageW), b0 = smem_u32(sx + sxi * kStageX);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk) {
                         const uint64_t ah = sw128_desc(a0 + kk * 32), bh = sw128_desc(b0 + kk * 32);
@@ -540,7 +553,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                         if (SPLIT)  // + w_lo x_hi into the first half
                             umma_f16(d_tmem, sw128_desc(a0 + kTileBytesW + kk * 32), bh, kIdesc, 1u);
                     }
-                    umma_commit(&empty[s]);  // stage s free once these MMAs finish
+                    umma_commit(&empty[s]);     // weight stage s free once these MMAs finish
+                    umma_commit(&xempty[sxi]);  // and X stage sxi
                 }
                 if (!ok) break;
                 umma_commit(&acc_full[b]);
