@@ -454,6 +454,14 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
             st.forward(prompt)
             e1.record(stream)
             torch.cuda.nvtx.range_pop()
+            # untimed: the prompt's logits at fixed vocabulary entries (the
+            # multi-GPU legs' parity check against the single-GPU run)
+            full = st.logits()
+            sample_idx = np.random.default_rng(5).choice(c.V, 256, replace=False)
+            out["prompt_logit_sample"] = [round(float(v), 6) for v in full[sample_idx]]
+            out["prompt_logit_absmax"] = round(float(np.abs(full).max()), 6)
+            e1b = torch.cuda.Event(enable_timing=True)
+            e1b.record(stream)
             tokens = []
             for _ in range(decode_steps):
                 tokens.append(st.argmax())
@@ -470,7 +478,7 @@ def time_engine(cfg_id: int, prompt_len: int, decode_steps: int, device, cpu_sam
             e4.synchronize()
             torch.cuda.nvtx.range_pop()
         prefill_s = e0.elapsed_time(e1) / 1e3
-        decode_s = e1.elapsed_time(e2) / 1e3
+        decode_s = e1b.elapsed_time(e2) / 1e3
         dev_step_s = e3.elapsed_time(e4) / 1e3 / len(tokens[:64])
         if dist:  # max over ranks
             t = torch.tensor([prefill_s, decode_s, dev_step_s], dtype=torch.float64, device=device)
@@ -590,14 +598,37 @@ def time_engine_batch(cfg_id: int, prompt_len: int, decode_steps: int, batch: in
     return out
 
 
-def recorded_first_tokens():
-    """Greedy tokens of the single-GPU engine legs (tests/golden/bench_first_tokens.json),
-    the parity check of the tensor- and expert-parallel legs."""
-    p = ROOT / "tests" / "golden" / "bench_first_tokens.json"
+def recorded_single_gpu():
+    """The single-GPU engine legs' prompt logits (at 256 fixed vocabulary
+    entries) and first greedy tokens, recorded from bench.py on one B200
+    (tests/golden/bench_single_gpu.json): the parity check of the tensor- and
+    expert-parallel legs."""
+    p = ROOT / "tests" / "golden" / "bench_single_gpu.json"
     try:
         return json.loads(p.read_text())
     except Exception:
         return {}
+
+
+def sharded_parity(res: dict, ref: dict) -> dict:
+    """Prompt logits of an N-GPU run against the single-GPU run (bar 5e-4 of
+    max(1, max|logit|), the reference's cross-backend bar) and where the greedy
+    tokens first differ (random-init logits have near-ties that FP32-grade
+    rounding differences can flip, so tokens are reported, not required)."""
+    a = res.get("prompt_logit_sample")
+    b = ref.get("prompt_logit_sample")
+    out = {"bar": 5e-4}
+    if a and b and len(a) == len(b):
+        scale = max(1.0, float(ref.get("prompt_logit_absmax", 1.0)))
+        err = max(abs(x - y) for x, y in zip(a, b)) / scale
+        out["prompt_logits_max_err"] = round(err, 8)
+        out["prompt_logits_within_bar"] = err <= 5e-4
+    ta, tb = res.get("first_tokens", []), ref.get("first_tokens", [])
+    n = min(len(ta), len(tb))
+    first = next((i for i in range(n) if ta[i] != tb[i]), None)
+    out["first_tokens_equal"] = first is None
+    out["first_token_divergence_step"] = first
+    return out
 
 
 def cpu_engine_tok_s(path, c, prompt=2, steps=2):
@@ -773,14 +804,18 @@ def main(argv=None):
     # greedy tokens checked against the recorded single-GPU run
     sharded = {}
     if args.only is None and world > 1 and not args.no_sharded:
-        golden = recorded_first_tokens()
+        golden = recorded_single_gpu()
         for cfg_id, key in ((27008, "engine_tp27b"), (36035, "engine_ep35b")):
             res = time_engine(cfg_id, prompts[cfg_id], 256, device, False, rank, world)
             ref = golden.get(str(cfg_id))
             if ref is not None:
-                res["first_tokens_match_single_gpu"] = res.get("first_tokens") == ref[:len(res.get("first_tokens", []))]
+                res["parity_vs_single_gpu"] = sharded_parity(res, ref)
+                res["single_gpu"] = {k: ref[k] for k in ("prefill_tok_s", "decode_tok_s") if k in ref}
+            res.pop("prompt_logit_sample", None)
             sharded[key] = res
 
+    if engine:
+        engine.pop("prompt_logit_sample", None)
     ref_programs = recorded_reference_programs()
     if ref_programs and engine and args.engine_config == 9000:
         rc = ref_programs.get("reference_cuda_9000", {})
