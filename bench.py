@@ -560,12 +560,14 @@ def time_engine_batch(cfg_id: int, prompt_len: int, decode_steps: int, batch: in
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(device.index) as clk:
             toks = [s.argmax() for s in states]
+            torch.cuda.nvtx.range_push("batch")  # ncu --nvtx-include "batch/" selects these launches
             e0.record(stream)
             for _ in range(decode_steps):
                 forward_batch(model, states, toks)
                 toks = [s.argmax() for s in states]
             e1.record(stream)
             e1.synchronize()
+            torch.cuda.nvtx.range_pop()
         batch_s = e0.elapsed_time(e1) / 1e3
         # the same decode with one sequence through state_forward
         for s in states:

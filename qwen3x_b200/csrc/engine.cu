@@ -22,6 +22,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -273,6 +274,10 @@ struct State {
     cudaGraphExec_t graph_exec = nullptr;
     cudaEvent_t batch_event = nullptr;  // orders this state's stream against a batched step it joins
     float* batch_logits = nullptr;      // [chunk][V] lm_head output of a batched step this state leads
+    uint64_t uid = 0;                   // unique per State of the process (never reused)
+    // the batched step this State leads, captured as a graph for one set of States
+    cudaGraphExec_t batch_exec = nullptr;
+    std::vector<uint64_t> batch_key;
     std::vector<void*> allocations;
 
     ~State() {
@@ -280,6 +285,7 @@ struct State {
         if (stream) cudaStreamSynchronize(stream);
         if (graph_exec) cudaGraphExecDestroy(graph_exec);
         if (graph) cudaGraphDestroy(graph);
+        if (batch_exec) cudaGraphExecDestroy(batch_exec);
         for (int r = 0; r < world && r < 8; ++r)
             if (peer_ready && r != rank && peer_bases[r]) cudaIpcCloseMemHandle(peer_bases[r]);
         for (void* p : allocations) cudaFree(p);
@@ -986,6 +992,8 @@ State* create_state(Model* model, int context, const char* nccl_id, char* err, s
     }
     std::unique_ptr<State> s(new (std::nothrow) State());
     if (!s) return nullptr;
+    static std::atomic<uint64_t> next_uid{1};
+    s->uid = next_uid.fetch_add(1);
     const Config& c = model->shard.lc;  // this rank's dims
     s->model = model;
     s->c = &c;
@@ -1174,7 +1182,37 @@ int state_forward_batch_impl(Model* m, State** states, const int* tokens, int n)
     }
     if (cudaMemcpyAsync(L.tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, L.stream) != cudaSuccess)
         return Q3XK_ECUDA;
-    Q3XB_TRY(forward_batch(*m, states, n));
+    if (L.use_graphs) {
+        // replay the step captured for exactly this list of States (positions
+        // live on the device, so one capture serves every later step)
+        std::vector<uint64_t> key(n);
+        for (int b = 0; b < n; ++b) key[b] = states[b]->uid;
+        if (!L.batch_exec || L.batch_key != key) {
+            if (L.batch_exec) {
+                cudaGraphExecDestroy(L.batch_exec);
+                L.batch_exec = nullptr;
+            }
+            if (cudaStreamBeginCapture(L.stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return Q3XK_ECUDA;
+            const int st = forward_batch(*m, states, n);
+            cudaGraph_t g = nullptr;
+            const cudaError_t e = cudaStreamEndCapture(L.stream, &g);
+            if (st != Q3XK_OK || e != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                cudaGetLastError();
+                return st != Q3XK_OK ? st : Q3XK_ECUDA;
+            }
+            const cudaError_t ie = cudaGraphInstantiate(&L.batch_exec, g, 0);
+            cudaGraphDestroy(g);
+            if (ie != cudaSuccess) {
+                L.batch_exec = nullptr;
+                return Q3XK_ECUDA;
+            }
+            L.batch_key = key;
+        }
+        if (cudaGraphLaunch(L.batch_exec, L.stream) != cudaSuccess) return Q3XK_ECUDA;
+    } else {
+        Q3XB_TRY(forward_batch(*m, states, n));
+    }
     if (n > 1) {
         if (!L.batch_event && cudaEventCreateWithFlags(&L.batch_event, cudaEventDisableTiming) != cudaSuccess)
             return Q3XK_ECUDA;

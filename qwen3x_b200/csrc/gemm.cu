@@ -187,28 +187,43 @@ struct TileN {
 // counters != nullptr: block 0 also zeroes the split-K arrival counters that
 // the following GEMM uses (they are left at zero by every GEMM, but the
 // caller's workspace starts out undefined).
-__global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ x16,
-                                                       __half* __restrict__ x16lo, float* __restrict__ tok_scale,
-                                                       int K, int* __restrict__ counters) {
+// One token per CTA of kXThreads threads; the token's values stay in
+// registers between the exponent pass and the conversion (K <= kXThreads * 4 *
+// kXVecs = 20480; longer rows are read again for the conversion).
+constexpr int kXThreads = 1024, kXVecs = 5;
+__global__ void __launch_bounds__(kXThreads) x_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ x16,
+                                                             __half* __restrict__ x16lo, float* __restrict__ tok_scale,
+                                                             int K, int* __restrict__ counters) {
     griddep_wait();
     griddep_launch_dependents();
     const int t = blockIdx.x;
     if (counters && t == 0)
         for (int i = threadIdx.x; i < kCounterInts; i += blockDim.x) counters[i] = 0;
     const float* row = x + (int64_t)t * K;
+    const bool held = K <= kXThreads * 4 * kXVecs;
+    float4 v[kXVecs];
     uint32_t emax = 0;
-    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(row + k);
-        emax = max(emax, max(max((__float_as_uint(v.x) >> 23) & 0xFFu, (__float_as_uint(v.y) >> 23) & 0xFFu),
-                             max((__float_as_uint(v.z) >> 23) & 0xFFu, (__float_as_uint(v.w) >> 23) & 0xFFu)));
+    auto upd = [&](const float4& a) {
+        emax = max(emax, max(max((__float_as_uint(a.x) >> 23) & 0xFFu, (__float_as_uint(a.y) >> 23) & 0xFFu),
+                             max((__float_as_uint(a.z) >> 23) & 0xFFu, (__float_as_uint(a.w) >> 23) & 0xFFu)));
+    };
+    if (held) {
+#pragma unroll
+        for (int i = 0; i < kXVecs; ++i) {
+            const int k = (threadIdx.x + i * kXThreads) * 4;
+            v[i] = k < K ? *reinterpret_cast<const float4*>(row + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            upd(v[i]);
+        }
+    } else {
+        for (int k = threadIdx.x * 4; k < K; k += kXThreads * 4) upd(*reinterpret_cast<const float4*>(row + k));
     }
-    __shared__ uint32_t red[8];
+    __shared__ uint32_t red[kXThreads / 32];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = emax;
     __syncthreads();
     emax = 0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) emax = max(emax, red[i]);
+    for (int i = 0; i < kXThreads / 32; ++i) emax = max(emax, red[i]);
     // Largest |x| < 2^(E+1): scale by 2^(14-E) so it lands in [2^14, 2^15).
     const int E = emax == 0xFFu ? 0 : (int)emax - 127;  // inf/nan stay inf/nan
     const int s = min(100, max(-100, 14 - E));
@@ -216,9 +231,8 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
     if (threadIdx.x == 0) tok_scale[t] = __uint_as_float((uint32_t)(127 - s) << 23);
     __half2* out = reinterpret_cast<__half2*>(x16 + (int64_t)t * K);
     __half2* lo = x16lo ? reinterpret_cast<__half2*>(x16lo + (int64_t)t * K) : nullptr;
-    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(row + k);
-        const float a0 = v.x * up, a1 = v.y * up, a2 = v.z * up, a3 = v.w * up;
+    auto put = [&](int k, const float4& a) {
+        const float a0 = a.x * up, a1 = a.y * up, a2 = a.z * up, a3 = a.w * up;
         const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
         out[k / 2] = h01;
         out[k / 2 + 1] = h23;
@@ -227,6 +241,15 @@ __global__ void __launch_bounds__(256) x_to_f16_kernel(const float* __restrict__
             lo[k / 2] = __floats2half2_rn(a0 - f01.x, a1 - f01.y);
             lo[k / 2 + 1] = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
         }
+    };
+    if (held) {
+#pragma unroll
+        for (int i = 0; i < kXVecs; ++i) {
+            const int k = (threadIdx.x + i * kXThreads) * 4;
+            if (k < K) put(k, v[i]);
+        }
+    } else {
+        for (int k = threadIdx.x * 4; k < K; k += kXThreads * 4) put(k, *reinterpret_cast<const float4*>(row + k));
     }
 }
 
@@ -733,7 +756,8 @@ int sm_count() {
 int launch_x_to_f16(const float* x, int T, int K, __half* x16, __half* x16lo, float* tok_scale, cudaStream_t s,
                     int* counters) {
     if (K % 8) return Q3XK_EINVAL;  // TMA row stride of X16 must be a multiple of 16 bytes
-    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(256), 0, s, x, x16, x16lo, tok_scale, K, counters) != cudaSuccess)
+    if (launch_pdl(x_to_f16_kernel, dim3(T), dim3(kXThreads), 0, s, x, x16, x16lo, tok_scale, K, counters) !=
+        cudaSuccess)
         return Q3XK_ECUDA;
     count_launch();
     return Q3XK_OK;

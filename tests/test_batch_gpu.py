@@ -94,3 +94,32 @@ def test_batch_arguments_are_checked(cuda, model_files):
     for x in s:
         x.close()
     model.close()
+
+
+def test_batch_graph_replay_equals_eager(cuda, model_files):
+    """The batched step replays a CUDA graph captured for its list of States;
+    launched eagerly instead (set_graphs(False) on the lead State) it gives the
+    same logits bit for bit, and a different list of States is captured anew."""
+    from qwen3x_b200.backend import Model, State, forward_batch
+
+    mid = 35091
+    c = modelfile.CONFIGS[mid]
+    model = Model(model_files[mid])
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, c.V, 6 + b).astype(np.int32) for b in range(4)]
+    g = [State(model, 64) for _ in range(4)]
+    e = [State(model, 64) for _ in range(4)]
+    e[0].set_graphs(False)
+    for b in range(4):
+        g[b].forward(prompts[b])
+        e[b].forward(prompts[b])
+    for step in range(6):
+        sub = 4 if step < 3 else 2  # the list changes: a new capture
+        toks = [g[b].argmax() for b in range(sub)]
+        forward_batch(model, g[:sub], toks)
+        forward_batch(model, e[:sub], toks)
+        for b in range(sub):
+            np.testing.assert_array_equal(g[b].logits(), e[b].logits())
+    for s in g + e:
+        s.close()
+    model.close()
