@@ -29,6 +29,7 @@
 #include <cstring>
 #include <memory>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "layers.cuh"
@@ -349,6 +350,64 @@ struct Loader {
     int status = Q3XK_OK;
     std::vector<float> host;
     std::vector<uint8_t> gather;
+    // Host -> device copies of the file's bytes go through two pinned buffers:
+    // host threads copy chunk i into one while the DMA of chunk i - 1 runs from
+    // the other (pageable copies from the mmap are staged by the driver and do
+    // not overlap with anything).
+    static constexpr size_t kPinChunk = (size_t)64 << 20;
+    static constexpr int kCopyThreads = 8;
+    uint8_t* pinned[2] = {nullptr, nullptr};
+    cudaEvent_t pin_free[2] = {nullptr, nullptr};
+    int pin_next = 0;
+
+    bool open_pinned() {
+        for (int i = 0; i < 2; ++i) {
+            if (cudaHostAlloc(reinterpret_cast<void**>(&pinned[i]), kPinChunk, cudaHostAllocDefault) != cudaSuccess ||
+                cudaEventCreateWithFlags(&pin_free[i], cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                close_pinned();
+                return false;
+            }
+        }
+        return true;
+    }
+    void close_pinned() {
+        for (int i = 0; i < 2; ++i) {
+            if (pin_free[i]) cudaEventSynchronize(pin_free[i]), cudaEventDestroy(pin_free[i]);
+            if (pinned[i]) cudaFreeHost(pinned[i]);
+            pinned[i] = nullptr;
+            pin_free[i] = nullptr;
+        }
+    }
+    // dst (device) <- bytes of src (host) on `stream`.
+    bool h2d(void* dst, const uint8_t* src, size_t bytes) {
+        if (!pinned[0]) return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream) == cudaSuccess;
+        for (size_t off = 0; off < bytes; off += kPinChunk) {
+            const size_t len = bytes - off < kPinChunk ? bytes - off : kPinChunk;
+            const int b = pin_next;
+            pin_next ^= 1;
+            if (cudaEventSynchronize(pin_free[b]) != cudaSuccess) return false;  // its last DMA is done
+            uint8_t* buf = pinned[b];
+            const uint8_t* from = src + off;
+            if (len < ((size_t)4 << 20)) {
+                std::memcpy(buf, from, len);
+            } else {
+                std::thread workers[kCopyThreads];
+                const size_t part = (len + kCopyThreads - 1) / kCopyThreads;
+                for (int t = 0; t < kCopyThreads; ++t) {
+                    const size_t a = (size_t)t * part, e = a + part < len ? a + part : len;
+                    if (a < e) workers[t] = std::thread([=] { std::memcpy(buf + a, from + a, e - a); });
+                }
+                for (auto& w : workers)
+                    if (w.joinable()) w.join();
+            }
+            if (cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, buf, len, cudaMemcpyHostToDevice, stream) !=
+                    cudaSuccess ||
+                cudaEventRecord(pin_free[b], stream) != cudaSuccess)
+                return false;
+        }
+        return true;
+    }
 
     uint8_t* carve(size_t bytes) {
         const size_t at = used;
@@ -389,7 +448,7 @@ struct Loader {
         }
         q3xk_matrix d = dst;
         d.experts = experts;
-        if (cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        if (!h2d(staging, src, bytes)) {
             status = Q3XK_ECUDA;
             return;
         }
@@ -409,7 +468,7 @@ struct Loader {
             status = Q3XK_EINVAL;
             return;
         }
-        if (cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        if (!h2d(staging, src, bytes)) {
             status = Q3XK_ECUDA;
             return;
         }
@@ -454,7 +513,7 @@ struct Loader {
         }
         gather.resize((size_t)rows * rb);
         for (int r = 0; r < rows; ++r) std::memcpy(gather.data() + (size_t)r * rb, src + (size_t)r * full + off, rb);
-        if (cudaMemcpyAsync(staging, gather.data(), gather.size(), cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+        if (!h2d(staging, gather.data(), gather.size())) {
             status = Q3XK_ECUDA;
             return;
         }
@@ -619,10 +678,12 @@ bool Model::load(const char* path, int rank, int world, const char** error) {
         return fail("cannot allocate the upload staging buffer");
     cudaStreamCreateWithFlags(&ld.stream, cudaStreamNonBlocking);
     madvise(mapped, file_size, MADV_SEQUENTIAL);
+    ld.open_pinned();  // without pinned memory the copies stay pageable
     ld.pass = 1;
     ld.used = 0;
     const char* e = ld.walk();
     const cudaError_t se = cudaStreamSynchronize(ld.stream);
+    ld.close_pinned();
     cudaStreamDestroy(ld.stream);
     cudaFree(ld.staging);
     if (e) return fail(e);
