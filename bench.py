@@ -842,7 +842,7 @@ def main(argv=None):
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profile_traffic("gemv_q8_cfg1"),
                          "bytes_per_launch": bytes_q8,
-                         "kernel": "q3xk::gemv_kernel<Q8_0,KS=1>"},
+                         "kernel": "q3xk::gemv_ring_kernel<Q8_0, 24 warps, 2 stages>"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", **e2e_io,
                     "path": "q3xk_try_mv_host (pinned host x/y, synchronous)"},
             "gpu_launches": int(launches),

@@ -287,6 +287,21 @@ Q3XK_API int q3xk_peer_allreduce_add(void* const* bases, int rank, int world, in
                                      const float* partial, float* y, int n, int* err, double timeout_s,
                                      void* stream);
 
+/*
+ * Kernel family of the plain Q8_0 / Q4_0 GEMVs (q3xk_gemv, q3xk_gemv_ex
+ * without a transform, q3xk_expert_gemv, q3xk_try_mv_host*):
+ *   0  automatic (default): the shared-memory ring kernel where its staging
+ *      fits (x prescaled plus a ~140-210 KB ring per SM; 24 warps per CTA
+ *      for Q8_0 matrices of up to one 4-row group per warp, else 16), else
+ *      the register one
+ *   1  register batches (128-bit loads held in registers)
+ *   2  ring, 16 warps per CTA     3  ring, 24 warps per CTA (20 for Q4_0)
+ * Process-wide; meant for tests and measurements that compare the families
+ * on the same inputs.  Results of every family meet the same parity bar.
+ * No counterpart in the reference.
+ */
+Q3XK_API int q3xk_gemv_set_family(int family);
+
 /* Number of kernel launches the calls above made since the last reset
  * (host-side counter used by the benchmark's gpu_launches report). */
 Q3XK_API uint64_t q3xk_launch_count(void);

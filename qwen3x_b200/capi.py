@@ -110,6 +110,7 @@ _SIGNATURES = {
                                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_void_p, ctypes.c_double, ctypes.c_void_p]),
     "q3xk_clear_device_error": (ctypes.c_int, []),
+    "q3xk_gemv_set_family": (ctypes.c_int, [ctypes.c_int]),
     "q3xk_launch_count": (ctypes.c_uint64, []),
     "q3xk_reset_launch_count": (None, []),
     # q3x_backend.h, C part

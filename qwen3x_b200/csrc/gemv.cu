@@ -28,6 +28,7 @@
 //    requested before griddepcontrol.wait, i.e. while the previous kernel in
 //    the stream is still finishing; x and y are only touched after it.
 #include <mutex>
+#include <type_traits>
 
 #include <cuda.h>
 
@@ -619,6 +620,248 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
         gemv_passes<TYPE, true, KS, MODE, DB>(p, rec, A, xs4, gg, part, seg_off, gb, ge, passes, row0, live);
 }
 
+// ---- Ring-staged GEMV (plain row addressing, Q8_0 / Q4_0) ------------------
+//
+// The weight stream goes through a per-warp ring of shared-memory stages
+// filled with cp.async (16 bytes per copy, no registers held while in
+// flight), and each ring is filled before griddepcontrol.wait: while the
+// previous kernel finishes and x is prescaled, ~200 KB per SM are already on
+// their way.  Measured on B200, a 53.5 MB read staged this way takes 7.9 us
+// per launch in a chain (6.7 TB/s) against 9.2 us for register-held loads.
+//
+// One CTA per SM with RW warps (16-24: enough eligible warps to hide the
+// shared-memory and FMA latencies of the dequant).  The CTA owns a balanced
+// range of 4-row groups; warp w takes groups w, w + RW, ...  A group's K runs
+// through the ring in stages of 64 units (two 16-byte units per lane and
+// row, each copied by that lane itself from a coalesced 512-byte span), so a
+// warp's stages run back to back across its groups.  A stage holds the 4
+// rows' quants [row][half][lane] and then their scales (copied by the first
+// lanes, read after __syncwarp).  x is prescaled once per CTA into shared
+// memory, unit by unit, with the chunks of a unit permuted so that 8
+// consecutive units hit 8 different bank groups.  Arithmetic per unit is the
+// register kernel's (Codec::dot, one FMA of the unit's scale into the row
+// sum; the row sums meet in the same butterfly).  Deterministic.
+constexpr int kUPL = 2;  // 16-byte units per lane and row in a stage
+
+template <int TYPE>
+struct RingGeo {
+    using C = Codec<TYPE>;
+    static constexpr int kSB = 64 * kUPL / C::kUnitsPerBlock;  // scale bytes per row and stage
+    static constexpr int kSPieces = kSB / 16;                   // 16-byte scale copies per row
+    static constexpr int kQBytes = kRows * kUPL * 512;          // quants of a stage
+    static constexpr int kStage = kQBytes + kRows * kSB;
+    static_assert(kRows * kSPieces <= 32, "scale copies must fit one warp");
+    // float4 slot of chunk j of unit u in the x area (the permutation depends
+    // only on u mod 8, i.e. on the lane)
+    __device__ static int xslot(int u, int j) {
+        return C::kChunks == 4 ? u * 4 + (j ^ ((u >> 1) & 3)) : u * 8 + (j ^ (u & 7));
+    }
+};
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async16_s(uint32_t saddr, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gmem) : "memory");
+}
+
+// Issue side of a warp's ring: the next stage to copy (its group, its stage
+// within the group, its slot) and this lane's running source pointers into
+// the group's 4 row records.  FULL: K is a whole number of stages, so no
+// copy needs a bounds check.
+template <int TYPE, int RW, int S, bool FULL>
+struct RingIssue {
+    using G = RingGeo<TYPE>;
+    const uint8_t* q[kRows];  // this lane's first unit of the next stage, per row
+    const uint8_t* sc;        // this lane's scale piece of the next stage (lanes < 4 * kSPieces)
+    uint32_t dq, ds;          // shared addresses of the same in slot 0
+    int grp, c, slot, t;
+
+    __device__ __forceinline__ void set_rows(const GemvParams& p, int gb, int warp, int lane) {
+        const int row0 = (gb + warp + RW * grp) * kRows;
+#pragma unroll
+        for (int j = 0; j < kRows; ++j)
+            q[j] = p.w + (int64_t)min(row0 + j, p.rows - 1) * p.row_stride + lane * 16;
+        const int js = (lane / G::kSPieces) & (kRows - 1), pc = lane % G::kSPieces;
+        sc = p.w + (int64_t)min(row0 + js, p.rows - 1) * p.row_stride + p.qbytes + pc * 16;
+    }
+    __device__ __forceinline__ void init(const GemvParams& p, uint8_t* wring, int gb, int warp, int lane, int ng) {
+        grp = c = slot = t = 0;
+        const uint32_t base = (uint32_t)__cvta_generic_to_shared(wring);
+        dq = base + lane * 16;
+        ds = base + G::kQBytes + (lane / G::kSPieces) * G::kSB + (lane % G::kSPieces) * 16;
+        if (ng > 0) set_rows(p, gb, warp, lane);
+    }
+    // Copies the next stage (if any) into its slot and commits one group of copies.
+    __device__ __forceinline__ void issue(const GemvParams& p, int gb, int warp, int lane, int ng, int nst,
+                                          int total, int nblocks) {
+        if (t < total) {
+            const uint32_t off = (uint32_t)slot * G::kStage;
+#pragma unroll
+            for (int h = 0; h < kUPL; ++h) {
+                if (FULL || c * 32 * kUPL + h * 32 + lane < p.units) {
+#pragma unroll
+                    for (int j = 0; j < kRows; ++j) cp_async16_s(dq + off + (j * kUPL + h) * 512, q[j] + h * 512);
+                }
+            }
+            if (lane < kRows * G::kSPieces && (FULL || (c * G::kSB + (lane % G::kSPieces) * 16) / 2 < nblocks))
+                cp_async16_s(ds + off, sc);
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) q[j] += 512 * kUPL;
+            sc += G::kSB;
+            ++t;
+            slot = slot + 1 == S ? 0 : slot + 1;
+            if (++c == nst) {
+                c = 0;
+                if (++grp < ng) set_rows(p, gb, warp, lane);
+            }
+        }
+        cp_async_commit();
+    }
+};
+
+template <int TYPE, int RW, int S, bool FULL, bool FAST>
+__device__ __forceinline__ void ring_main(const GemvParams& p, RingIssue<TYPE, RW, S, FULL>& is, const float4* xs4,
+                                          const float2* gg, uint8_t* wring, int gb, int warp, int lane, int ng,
+                                          int nst, int total, int nblocks) {
+    using C = Codec<TYPE>;
+    using G = RingGeo<TYPE>;
+    float acc[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) acc[j] = 0.f;
+    // x chunk offsets of this lane's units (the permutation repeats every 8 units)
+    int xo[C::kChunks];
+#pragma unroll
+    for (int k = 0; k < C::kChunks; ++k) xo[k] = G::xslot(lane, k);
+    int c = 0, grp = 0, slot = 0;
+#pragma unroll 1
+    for (int t = 0; t < total; ++t) {
+        cp_async_wait<S - 1>();
+        __syncwarp();
+        const uint8_t* st = wring + slot * G::kStage;
+#pragma unroll
+        for (int h = 0; h < kUPL; ++h) {
+            const int u = c * 32 * kUPL + h * 32;  // this lane's unit is u + lane
+            if (FULL || u + lane < p.units) {
+                const float4* xu = xs4 + u * C::kChunks;
+                float4 xr[C::kChunks];
+#pragma unroll
+                for (int k = 0; k < C::kChunks; ++k) xr[k] = xu[xo[k]];
+                const float2 gu = gg[u + lane];
+                const int sidx = (h * 32 + lane) / C::kUnitsPerBlock;  // the unit's scale within the stage
+#pragma unroll
+                for (int j = 0; j < kRows; ++j) {
+                    const uint4 qv = *reinterpret_cast<const uint4*>(st + (j * kUPL + h) * 512 + lane * 16);
+                    const float d = f16_bits_to_float(
+                        *reinterpret_cast<const uint16_t*>(st + G::kQBytes + j * G::kSB + sidx * 2));
+                    acc[j] = fmaf(d, C::template dot<FAST>(&qv, xr, gu), acc[j]);
+                }
+            }
+        }
+        __syncwarp();  // every lane has read this slot (scales included) before it is refilled
+        is.issue(p, gb, warp, lane, ng, nst, total, nblocks);
+        slot = slot + 1 == S ? 0 : slot + 1;
+        if (++c == nst) {  // group done: 4 row sums meet in the transposed butterfly
+            c = 0;
+            const int row0 = (gb + warp + RW * grp) * kRows;
+            ++grp;
+            const bool b4 = lane & 16, b3 = lane & 8;
+            float k0 = b4 ? acc[2] : acc[0], k1 = b4 ? acc[3] : acc[1];
+            const float s0 = b4 ? acc[0] : acc[2], s1 = b4 ? acc[1] : acc[3];
+            k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+            k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+            float k = b3 ? k1 : k0;
+            k += __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+            k += __shfl_xor_sync(0xffffffffu, k, 4);
+            k += __shfl_xor_sync(0xffffffffu, k, 2);
+            k += __shfl_xor_sync(0xffffffffu, k, 1);
+            if (p.epi) {
+                const float uu = __shfl_down_sync(0xffffffffu, k, 16);  // lanes 0, 8 <- rows 2, 3
+                if ((lane == 0 || lane == 8) && row0 < p.rows) p.y[row0 / 2 + (lane >> 3)] = k * sigmoid_ref(k) * uu;
+            } else {
+                const int r = (lane & 16 ? 2 : 0) + (lane & 8 ? 1 : 0);
+                if ((lane & 7) == 0 && row0 + r < p.rows) {
+                    float* yp = p.y + row0 + r;
+                    *yp = p.accumulate ? *yp + k : k;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) acc[j] = 0.f;
+        }
+    }
+}
+
+template <int TYPE, int RW, int S, int MINB, bool FULL>
+__global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvParams p) {
+    using C = Codec<TYPE>;
+    using G = RingGeo<TYPE>;
+    extern __shared__ __align__(128) uint8_t rsm[];
+    const int nblocks = p.cols / kBlock;
+    float4* xs4 = reinterpret_cast<float4*>(rsm);                                      // units * kChunks
+    float2* gg = reinterpret_cast<float2*>(rsm + (size_t)p.units * C::kCols * 4);      // units
+    uint8_t* ring = rsm + (size_t)p.units * C::kCols * 4 + (((size_t)p.units * 8 + 127) & ~(size_t)127);
+
+    griddep_launch_dependents();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t gt = (p.rows + kRows - 1) / kRows;
+    const int gb = (int)(blockIdx.x * gt / gridDim.x), ge = (int)((blockIdx.x + 1) * gt / gridDim.x);
+    const int ng = ge - gb > warp ? (ge - gb - warp + RW - 1) / RW : 0;  // this warp's groups
+    const int nst = (p.units + 32 * kUPL - 1) / (32 * kUPL);              // stages per group
+    const int total = ng * nst;
+    uint8_t* const wring = ring + (size_t)warp * S * G::kStage;
+
+    RingIssue<TYPE, RW, S, FULL> is;
+    is.init(p, wring, gb, warp, lane, ng);
+#pragma unroll 1
+    for (int t = 0; t < S; ++t) is.issue(p, gb, warp, lane, ng, nst, total, nblocks);
+    griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
+
+    // Prescale x per unit (as the register kernel does).
+    int slow = 0;
+    for (int u = tid; u < p.units; u += RW * 32) {
+        float v[C::kCols];
+        unit_x<C::kCols, false>(p, u, v, nullptr);
+        uint32_t emax = 0;
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < C::kCols; ++k) {
+            emax = max(emax, (__float_as_uint(v[k]) >> 23) & 0xFFu);
+            sum += v[k];
+        }
+        slow |= (emax == 0xFFu || (int)emax - 127 > 103) ? 1 : 0;
+        const int P = min(127, max(23, 126 - ((int)emax - 127)));
+#pragma unroll
+        for (int j = 0; j < C::kChunks; ++j) {
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[e] = v[C::element(4 * j + e)] * pow2f(P - C::shift(4 * j + e));
+            xs4[G::xslot(u, j)] = make_float4(o[0], o[1], o[2], o[3]);
+        }
+        gg[u] = f2(pow2f(149 - P), -C::kOffset * sum);
+    }
+    const int any_slow = __syncthreads_or(slow);
+    if (any_slow) {  // exact decode for the whole CTA: unscaled x in the same slots
+        for (int u = tid; u < p.units; u += RW * 32) {
+            float v[C::kCols];
+            unit_x<C::kCols, false>(p, u, v, nullptr);
+#pragma unroll
+            for (int j = 0; j < C::kChunks; ++j)
+                xs4[G::xslot(u, j)] = make_float4(v[C::element(4 * j)], v[C::element(4 * j + 1)],
+                                                  v[C::element(4 * j + 2)], v[C::element(4 * j + 3)]);
+        }
+        __syncthreads();
+        ring_main<TYPE, RW, S, FULL, false>(p, is, xs4, gg, wring, gb, warp, lane, ng, nst, total, nblocks);
+    } else {
+        ring_main<TYPE, RW, S, FULL, true>(p, is, xs4, gg, wring, gb, warp, lane, ng, nst, total, nblocks);
+    }
+    cp_async_wait<0>();
+}
+
+// Kernel family for plain Q8_0 / Q4_0 GEMVs: 0 = automatic, 1 = register
+// batches, 2 = ring (q3xk_gemv_set_family; tests run both on the same inputs).
+int g_gemv_family = 0;
+constexpr size_t kRingSmemMax = 227 * 1024;
+
 int sm_count_cached() {
     static int count = 0;
     if (!count) {
@@ -689,8 +932,78 @@ int launch_xf(const GemvParams& p, size_t smem, cudaStream_t s) {
 // flight) stream faster; with enough rows the single-buffered ones at 3 CTAs
 // per SM avoid a second wave.  Measured on B200 (Q8_0, us): 4096x4096 6.9 vs
 // 5.6 double-buffered, 4096x12288 19.2 vs 15.3; 12352x4096 12.0 vs 16.1.
+// Ring-kernel launch: one CTA per SM (fewer for small matrices); returns
+// Q3XK_EUNSUPPORTED when the shape's shared memory does not fit.
+template <int TYPE>
+size_t ring_smem(const GemvParams& p, int rw, int stages) {
+    return (size_t)p.units * Codec<TYPE>::kCols * 4 + (((size_t)p.units * 8 + 127) & ~(size_t)127) +
+           (size_t)rw * stages * RingGeo<TYPE>::kStage;
+}
+
+// Ring-kernel launch: one CTA per SM (fewer for small matrices).  MINB = 2:
+// the CTA takes at most half an SM, so the next GEMV's CTA can be resident
+// beside it and fill its own ring while this one runs.
+template <int TYPE, int RW, int S, int MINB>
+int launch_ring(const GemvParams& p, cudaStream_t s) {
+    const size_t smem = ring_smem<TYPE>(p, RW, S);
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(gemv_ring_kernel<TYPE, RW, S, MINB, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemMax) != cudaSuccess ||
+            cudaFuncSetAttribute(gemv_ring_kernel<TYPE, RW, S, MINB, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemMax) != cudaSuccess)
+            return Q3XK_ECUDA;
+        configured = true;
+    }
+    const int64_t groups = (p.rows + kRows - 1) / kRows;
+    const int64_t sms = sm_count_cached();
+    const int64_t grid = groups < sms ? groups : sms;
+    const cudaError_t e =
+        p.units % (32 * kUPL) == 0
+            ? launch_pdl(gemv_ring_kernel<TYPE, RW, S, MINB, true>, dim3((unsigned)grid), dim3(RW * 32), smem, s, p)
+            : launch_pdl(gemv_ring_kernel<TYPE, RW, S, MINB, false>, dim3((unsigned)grid), dim3(RW * 32), smem, s, p);
+    return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
+}
+
+// The deepest ring (stages per warp, up to SMAX) whose shared memory fits in
+// `cap` next to x; Q3XK_EUNSUPPORTED when even two stages do not fit.
+template <int TYPE, int RW, int SMAX, int MINB>
+int launch_ring_depth(const GemvParams& p, cudaStream_t s, size_t cap) {
+    if (SMAX >= 4 && ring_smem<TYPE>(p, RW, 4) <= cap) return launch_ring<TYPE, RW, 4, MINB>(p, s);
+    if (SMAX >= 3 && ring_smem<TYPE>(p, RW, 3) <= cap) return launch_ring<TYPE, RW, 3, MINB>(p, s);
+    if (ring_smem<TYPE>(p, RW, 2) <= cap) return launch_ring<TYPE, RW, 2, MINB>(p, s);
+    return Q3XK_EUNSUPPORTED;
+}
+
+template <int TYPE>
+int launch_ring_family(const GemvParams& p, cudaStream_t s) {
+    switch (g_gemv_family) {
+    case 3: {
+        const int st = launch_ring_depth<TYPE, 24, 2, 1>(p, s, kRingSmemMax);
+        if (st != Q3XK_EUNSUPPORTED) return st;
+        return launch_ring_depth<TYPE, 20, 2, 1>(p, s, kRingSmemMax);
+    }
+    case 2: return launch_ring_depth<TYPE, 16, 3, 1>(p, s, kRingSmemMax);
+    default: {
+        // Measured on B200 (us): Q8_0 12288x4096 10.1 with 24 warps vs 10.9
+        // with 16 (one 4-row group per warp), 248320x4096 169 vs 165; Q4_0
+        // 12288x4096 10.3 vs 9.5, 248320x2048 60.4 vs 54.3.
+        const int64_t groups = (p.rows + kRows - 1) / kRows;
+        if (TYPE == Q3XK_Q8_0 && groups <= 24 * (int64_t)sm_count_cached()) {
+            const int st = launch_ring_depth<TYPE, 24, 2, 1>(p, s, kRingSmemMax);
+            if (st != Q3XK_EUNSUPPORTED) return st;
+        }
+        return launch_ring_depth<TYPE, 16, 3, 1>(p, s, kRingSmemMax);
+    }
+    }
+}
+
 template <int TYPE, int MODE>
 int launch(GemvParams p, cudaStream_t s) {
+    if (TYPE != Q3XK_BF16 && MODE == kPlain && !p.xform && g_gemv_family != 1) {
+        const int st = launch_ring_family<TYPE == Q3XK_BF16 ? Q3XK_Q8_0 : TYPE>(p, s);
+        if (st != Q3XK_EUNSUPPORTED) return st;
+    }
     const size_t smem = smem_bytes<TYPE>(p);
     if (smem > 200 * 1024) return Q3XK_EUNSUPPORTED;
     if (p.xform) return launch_xf<TYPE, MODE, true, false>(p, smem, s);
@@ -993,5 +1306,11 @@ int q3xk_device_error(int* flags) {
 }
 
 int q3xk_clear_device_error(void) { return gemm_clear_error(); }
+
+int q3xk_gemv_set_family(int family) {
+    if (family < 0 || family > 3) return Q3XK_EINVAL;
+    g_gemv_family = family;
+    return Q3XK_OK;
+}
 
 }  // extern "C"

@@ -17,6 +17,18 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-5
 
 
+@pytest.fixture(params=[0, 1, 2, 3], ids=["auto", "register", "ring16", "ring24"], autouse=True)
+def gemv_family(request):
+    """Every case runs on each plain-GEMV kernel family (q3xk_gemv_set_family):
+    the automatic choice, register batches, and the shared-memory ring with
+    16 and 24 warps."""
+    from qwen3x_b200.capi import lib
+
+    assert lib().q3xk_gemv_set_family(request.param) == 0
+    yield request.param
+    lib().q3xk_gemv_set_family(0)
+
+
 def run_mv(cuda, packed, mtype, rows, cols, x, accumulate_into=None):
     import torch
 
