@@ -203,16 +203,29 @@ def time_gemv(mtype: int, steps: int, warmup: int, device, world: int, sample_cl
     for _ in range(max(warmup, 3)):
         step()
     torch.cuda.synchronize()
-    g_steps = min(GRAPH_STEPS, steps)
+    # K <= GRAPH_STEPS (the usual case): one graph holds exactly the K timed
+    # steps between two event-record nodes, so the events time the device
+    # execution of those steps and not the host's submission of the graph
+    # (~70 us for 120 kernel nodes, which would otherwise sit inside the
+    # timed region).  Larger K: graphs of GRAPH_STEPS steps replayed back to
+    # back between host-recorded events (the submission then overlaps them).
+    inner = steps <= GRAPH_STEPS
+    g_steps = steps if inner else GRAPH_STEPS
     graph = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     lib = capi.lib()
+    start = torch.cuda.Event(enable_timing=True, external=inner)
+    end = torch.cuda.Event(enable_timing=True, external=inner)
     with torch.cuda.stream(s):
         lib.q3xk_reset_launch_count()
         with torch.cuda.graph(graph, stream=s):
+            if inner:
+                start.record(s)
             for _ in range(g_steps):
                 step()
+            if inner:
+                end.record(s)
         per_graph = lib.q3xk_launch_count()
     torch.cuda.current_stream().wait_stream(s)
     replays, rem = divmod(steps, g_steps)
@@ -221,17 +234,18 @@ def time_gemv(mtype: int, steps: int, warmup: int, device, world: int, sample_cl
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(torch.cuda.current_device()) if sample_clocks else None
     if sampler:
         sampler.__enter__()
     lib.q3xk_reset_launch_count()
-    start.record()
+    if not inner:
+        start.record()
     for _ in range(replays):
         graph.replay()
     for _ in range(rem):
         step()
-    end.record()
+    if not inner:
+        end.record()
     torch.cuda.synchronize()
     eager_launches = lib.q3xk_launch_count()
     if sampler:
@@ -308,19 +322,21 @@ def time_gemm(mtype: int, T: int, reps: int, device, world: int, precision=None)
         for lin in lins:  # warm-up (configures the kernels before capture)
             batch_mv(lin, X, Y, workspace=ws, stream=stream, precision=precision)
         stream.synchronize()
+        # events as the graph's first and last nodes: device time of the calls
+        start = torch.cuda.Event(enable_timing=True, external=True)
+        end = torch.cuda.Event(enable_timing=True, external=True)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
+            start.record(stream)
             for i in range(per_graph):
                 batch_mv(lins[i % copies], X, Y, workspace=ws, stream=stream, precision=precision)
+            end.record(stream)
         g.replay()
         stream.synchronize()
     if world > 1:
         dist.barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):  # the graph replays on the current stream: time it there
-        start.record(stream)
+    with torch.cuda.stream(stream):  # the graph replays on the current stream
         g.replay()
-        end.record(stream)
     end.synchronize()
     secs = start.elapsed_time(end) / 1e3 / per_graph
     del g
@@ -699,6 +715,8 @@ def workload_config():
             "rows": ROWS, "cols": COLS, "weight_copies": COPIES,
             "l2": f"inputs larger than L2: {COPIES} resident weight copies x 53.5 MB rotated per step",
             "step": f"{COPIES} GEMV calls (one per weight copy), CUDA-graph replay",
+            "timing": "CUDA events recorded as the first and last nodes of the replayed graph "
+                      "(device time of the K steps; host graph submission excluded) when K <= 50",
             "parallelism": "weak: every rank runs the full workload on its own GPU"}
 
 
