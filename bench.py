@@ -826,7 +826,12 @@ def main(argv=None):
     if args.only is None and world > 1 and not args.no_sharded:
         golden = recorded_single_gpu()
         for cfg_id, key in ((27008, "engine_tp27b"), (36035, "engine_ep35b")):
-            res = time_engine(cfg_id, prompts[cfg_id], 256, device, False, rank, world)
+            try:
+                res = time_engine(cfg_id, prompts[cfg_id], 256, device, False, rank, world)
+            except Exception as exc:  # report the failed leg; the line itself still prints
+                sharded[key] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+                print(f"bench: sharded leg {key} failed on rank {rank}: {exc}", file=sys.stderr, flush=True)
+                continue
             ref = golden.get(str(cfg_id))
             if ref is not None:
                 res["parity_vs_single_gpu"] = sharded_parity(res, ref)

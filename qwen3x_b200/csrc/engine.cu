@@ -728,21 +728,24 @@ q3xk_xform rms_xf(const float* w1) {
     return xf;
 }
 
-// Measured on B200 (9B-shaped decode, 512-token context): RMSNorm and the
-// DeltaNet gated RMS as separate kernels 2.88 ms/token; fused into the
-// consuming GEMVs' staging of x (every CTA recomputes the statistics) 3.20 ms.
+// RMSNorm feeding a Q8_0 / Q4_0 decode GEMV runs in the GEMV's staging of x
+// (the ring GEMV's one CTA per SM computes the statistics in its prologue):
+// 9B-shaped decode measured 2.30 ms/token with the norms as their own
+// kernels.  The register GEMV family (BF16 router, MoE row gathers) keeps
+// the separate kernel: there every one of ~450 CTAs recomputed the
+// statistics (2.88 -> 3.20 ms/token when fused).
 #ifndef Q3XB_FUSE_RMS
-#define Q3XB_FUSE_RMS 0
+#define Q3XB_FUSE_RMS 1
 #endif
 #ifndef Q3XB_FUSE_GATED
 #define Q3XB_FUSE_GATED 0
 #endif
 
 // Input of a decode GEMV that reads RMSNorm(x) (engine.cpp:231-236): with
-// Q3XB_FUSE_RMS the GEMV normalises x while staging it (*xf is set), else
-// the norm runs as its own kernel into `normed` (returned).
-int rms_input(State& s, const float* x, const float* w1, int n, q3xk_xform* xf, const float** in) {
-    if (Q3XB_FUSE_RMS) {
+// `fuse` (and Q3XB_FUSE_RMS) the GEMV normalises x while staging it (*xf is
+// set), else the norm runs as its own kernel into `normed` (returned).
+int rms_input(State& s, const float* x, const float* w1, int n, q3xk_xform* xf, const float** in, bool fuse) {
+    if (Q3XB_FUSE_RMS && fuse) {
         *xf = rms_xf(w1);
         *in = x;
         return Q3XK_OK;
@@ -778,7 +781,7 @@ int moe_token(State& s, const Config& c, const Layer& l, int t, int layer) {
     float* h = s.hidden + (size_t)t * c.H;
     q3xk_xform xr;
     const float* in = nullptr;
-    Q3XB_TRY(rms_input(s, h, l.post_norm, c.H, &xr, &in));
+    Q3XB_TRY(rms_input(s, h, l.post_norm, c.H, &xr, &in, false));
     Q3XB_TRY(q3xk_gemv_ex(&l.router, in, s.rlogits, 0, &xr, st));
     Q3XB_TRY(router_topk(s.rlogits, c.experts, c.top_k, 1, sh.e0, sh.el, shared_slot(sh, layer), s.rids, s.rweights,
                          st));
@@ -810,7 +813,7 @@ int forward_token(Model& m, State& s, bool logits) {
         const int P = l.in_proj.rows;
         q3xk_xform xin;
         const float* in = nullptr;
-        Q3XB_TRY(rms_input(s, s.hidden, l.in_norm, c.H, &xin, &in));
+        Q3XB_TRY(rms_input(s, s.hidden, l.in_norm, c.H, &xin, &in, l.in_proj.type != Q3XK_BF16));
         Q3XB_TRY(q3xk_gemv_ex(&l.in_proj, in, s.proj, 0, &xin, st));
         if (l.delta) {
             const DeltaDims dd{c.KH, c.VH, c.KD, c.VD, DQKV, DQKV + DO, DQKV + DO + c.VH};
@@ -845,7 +848,7 @@ int forward_token(Model& m, State& s, bool logits) {
         } else {
             q3xk_xform xpost;
             const float* pin = nullptr;
-            Q3XB_TRY(rms_input(s, s.hidden, l.post_norm, c.H, &xpost, &pin));
+            Q3XB_TRY(rms_input(s, s.hidden, l.post_norm, c.H, &xpost, &pin, l.gate_up.type != Q3XK_BF16));
             Q3XB_TRY(gemv_swiglu(&l.gate_up, pin, s.mix, nullptr, 0, nullptr, &xpost, st));
             Q3XB_TRY(row_parallel(s, l.down, s.mix, 1, s.hidden));
         }
@@ -853,7 +856,7 @@ int forward_token(Model& m, State& s, bool logits) {
     if (logits) {
         q3xk_xform xf;
         const float* fin = nullptr;
-        Q3XB_TRY(rms_input(s, s.hidden, m.final_norm, c.H, &xf, &fin));
+        Q3XB_TRY(rms_input(s, s.hidden, m.final_norm, c.H, &xf, &fin, m.lm_head.type != Q3XK_BF16));
         Q3XB_TRY(q3xk_gemv_ex(&m.lm_head, fin, s.logits, 0, &xf, st));
     }
     return launch_advance(s.pos, 1, st);

@@ -816,11 +816,45 @@ __global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvPara
     for (int t = 0; t < S; ++t) is.issue(p, gb, warp, lane, ng, nst, total, nblocks);
     griddep_wait();  // x and (when accumulating) y may be written by the previous kernel
 
+    // RMSNorm of x applied while staging it (p.xform == RMS): x * scale * w1,
+    // scale = 1 / sqrt(mean(x^2) + eps) (engine.cpp:231-236), the statistics
+    // from one pass over x by the whole CTA.
+    float rscale = 1.f;
+    if (p.xform == Q3XK_XFORM_RMS) {
+        __shared__ float red[RW];
+        float ss = 0.f;
+        for (int k = tid * 4; k < p.cols; k += RW * 32 * 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(p.x + k));
+            ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < RW; ++w) tot += red[w];
+        rscale = 1.0f / sqrtf(tot / (float)p.cols + kXEps);
+    }
+    auto load_unit = [&](int u, float (&v)[C::kCols]) {
+        unit_x<C::kCols, false>(p, u, v, nullptr);
+        if (p.xform == Q3XK_XFORM_RMS) {
+            const float4* w4 = reinterpret_cast<const float4*>(p.xw + (int64_t)u * C::kCols);
+#pragma unroll
+            for (int i = 0; i < C::kCols / 4; ++i) {
+                const float4 w = __ldg(w4 + i);
+                v[4 * i] = v[4 * i] * rscale * w.x;
+                v[4 * i + 1] = v[4 * i + 1] * rscale * w.y;
+                v[4 * i + 2] = v[4 * i + 2] * rscale * w.z;
+                v[4 * i + 3] = v[4 * i + 3] * rscale * w.w;
+            }
+        }
+    };
+
     // Prescale x per unit (as the register kernel does).
     int slow = 0;
     for (int u = tid; u < p.units; u += RW * 32) {
         float v[C::kCols];
-        unit_x<C::kCols, false>(p, u, v, nullptr);
+        load_unit(u, v);
         uint32_t emax = 0;
         float sum = 0.f;
 #pragma unroll
@@ -843,7 +877,7 @@ __global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvPara
     if (any_slow) {  // exact decode for the whole CTA: unscaled x in the same slots
         for (int u = tid; u < p.units; u += RW * 32) {
             float v[C::kCols];
-            unit_x<C::kCols, false>(p, u, v, nullptr);
+            load_unit(u, v);
 #pragma unroll
             for (int j = 0; j < C::kChunks; ++j)
                 xs4[G::xslot(u, j)] = make_float4(v[C::element(4 * j)], v[C::element(4 * j + 1)],
@@ -860,7 +894,7 @@ __global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvPara
 // Kernel family for plain Q8_0 / Q4_0 GEMVs: 0 = automatic, 1 = register
 // batches, 2 = ring (q3xk_gemv_set_family; tests run both on the same inputs).
 int g_gemv_family = 0;
-constexpr size_t kRingSmemMax = 227 * 1024;
+constexpr size_t kRingSmemMax = 227 * 1024 - 256;  // dynamic; the kernel's static arrays take the rest
 
 int sm_count_cached() {
     static int count = 0;
@@ -1000,7 +1034,7 @@ int launch_ring_family(const GemvParams& p, cudaStream_t s) {
 
 template <int TYPE, int MODE>
 int launch(GemvParams p, cudaStream_t s) {
-    if (TYPE != Q3XK_BF16 && MODE == kPlain && !p.xform && g_gemv_family != 1) {
+    if (TYPE != Q3XK_BF16 && MODE == kPlain && (!p.xform || p.xform == Q3XK_XFORM_RMS) && g_gemv_family != 1) {
         const int st = launch_ring_family<TYPE == Q3XK_BF16 ? Q3XK_Q8_0 : TYPE>(p, s);
         if (st != Q3XK_EUNSUPPORTED) return st;
     }

@@ -57,10 +57,16 @@ def packed_matrix(mtype, rows, cols, seed):
     return quantize(w, mtype)
 
 
+@pytest.mark.parametrize("family", [0, 1], ids=["auto", "register"])
 @pytest.mark.parametrize("mtype", [Q8_0, Q4_0, BF16])
-@pytest.mark.parametrize("rows,cols", [(4096, 4096), (333, 512)])
-def test_rms_xform(cuda, mtype, rows, cols):
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (333, 512), (2048, 5120)])
+def test_rms_xform(cuda, mtype, rows, cols, family):
+    """RMSNorm applied while staging x, on the default kernel family (the ring
+    GEMV for Q8_0 / Q4_0, statistics computed in its prologue) and on the
+    register GEMV."""
     import torch
+
+    assert lib().q3xk_gemv_set_family(family) == 0
 
     packed = packed_matrix(mtype, rows, cols, 3)
     lin = Linear.from_packed(packed, mtype, rows, cols, device=cuda)
@@ -69,9 +75,12 @@ def test_rms_xform(cuda, mtype, rows, cols):
     xd, wd = dev(x, cuda), dev(w1, cuda)
     yd = torch.full((rows,), float("nan"), device=cuda)
     xf = XForm(kind=capi.XFORM_RMS, group=0, w=wd.data_ptr())
-    capi.check(lib().q3xk_gemv_ex(ctypes.byref(lin.m), xd.data_ptr(), yd.data_ptr(), 0, ctypes.byref(xf),
-                                  capi.stream_ptr()), "gemv_ex")
-    torch.cuda.synchronize()
+    try:
+        capi.check(lib().q3xk_gemv_ex(ctypes.byref(lin.m), xd.data_ptr(), yd.data_ptr(), 0, ctypes.byref(xf),
+                                      capi.stream_ptr()), "gemv_ex")
+        torch.cuda.synchronize()
+    finally:
+        lib().q3xk_gemv_set_family(0)
     check(yd.cpu().numpy(), packed, mtype, rows, cols, rms_ref(x, w1))
 
 
