@@ -17,8 +17,8 @@ cpu_baseline the reference's own arch/cpu.cpp mv (oracle/_ref), 1 thread as
             the reference runs on Linux, a bounded sample of the same workload
 --impl reference   the reference CPU implementation with all host threads.
 
-N > 1: every rank runs its own full copy of the workload (rows shard with no
-data-path collective), so scaling is "weak".
+N > 1: rank r streams row block r of a (12288 N) x 4096 matrix (x replicated,
+y sharded, no data-path collective), so scaling is "weak".
 """
 from __future__ import annotations
 
@@ -176,10 +176,17 @@ def dist_setup(n_gpus: int):
 
 
 def make_matrix(mtype: int, device):
+    """This rank's row block of the GEMV matrix: with N ranks the workload is
+    one (12288 N) x 4096 matrix split by rows, block r drawn from seed
+    1 + 1000 r (block 0 is BASELINE config 1's matrix), x the same on every
+    rank; no step needs a collective (y stays sharded)."""
+    import os
+
     from qwen3x_b200 import quant
     from qwen3x_b200.linear import Linear
 
-    w = quant.gaussian((ROWS, COLS), 1, 0.02)
+    rank = int(os.environ.get("RANK", "0"))
+    w = quant.gaussian((ROWS, COLS), 1 + 1000 * rank, 0.02)
     packed = quant.quantize(w, mtype)
     return [Linear.from_packed(packed, mtype, ROWS, COLS, device=device) for _ in range(COPIES)], packed
 
@@ -717,7 +724,8 @@ def workload_config():
             "step": f"{COPIES} GEMV calls (one per weight copy), CUDA-graph replay",
             "timing": "CUDA events recorded as the first and last nodes of the replayed graph "
                       "(device time of the K steps; host graph submission excluded) when K <= 50",
-            "parallelism": "weak: every rank runs the full workload on its own GPU"}
+            "parallelism": "weak, row split: rank r streams row block r of a (12288 N) x 4096 matrix "
+                           "(x replicated, y sharded, no collective per step)"}
 
 
 def main(argv=None):
@@ -867,7 +875,11 @@ def main(argv=None):
                          "bytes_per_launch": bytes_q8,
                          "kernel": "q3xk::gemv_ring_kernel<Q8_0, 24 warps, 2 stages>"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", **e2e_io,
-                    "path": "q3xk_try_mv_host (pinned host x/y, synchronous)"},
+                    "path": "q3xk_try_mv_host (pinned host x/y, synchronous)",
+                    "note": "host-latency-bound by the synchronous try_mv contract (one H2D copy, the "
+                            "GEMV, one D2H copy and a stream sync per call, ~49 us per 53.5 MB call); "
+                            "the end-to-end figure of the model path is extra.engine_9b.decode_tok_s "
+                            "(host argmax round trip per token) beside decode_device_ms_per_token"},
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
