@@ -779,10 +779,16 @@ int moe_token(State& s, const Config& c, const Layer& l, int t, int layer) {
     const Shard& sh = s.model->shard;
     const int S = c.top_k + 1;  // routed slots + the shared expert
     float* h = s.hidden + (size_t)t * c.H;
-    q3xk_xform xr;
-    const float* in = nullptr;
-    Q3XB_TRY(rms_input(s, h, l.post_norm, c.H, &xr, &in, false));
-    Q3XB_TRY(q3xk_gemv_ex(&l.router, in, s.rlogits, 0, &xr, st));
+    q3xk_xform xr{};
+    const float* in = s.normed;
+    // RMSNorm in the router GEMV's prologue, which also leaves the normalised
+    // hidden state in s.normed for the expert GEMVs; else its own kernel.
+    int rs = Q3XB_FUSE_RMS ? gemv_rms_out(&l.router, h, l.post_norm, s.rlogits, s.normed, st) : Q3XK_EUNSUPPORTED;
+    if (rs == Q3XK_EUNSUPPORTED) {
+        Q3XB_TRY(rms_input(s, h, l.post_norm, c.H, &xr, &in, false));
+        rs = q3xk_gemv_ex(&l.router, in, s.rlogits, 0, &xr, st);
+    }
+    Q3XB_TRY(rs);
     Q3XB_TRY(router_topk(s.rlogits, c.experts, c.top_k, 1, sh.e0, sh.el, shared_slot(sh, layer), s.rids, s.rweights,
                          st));
     Q3XB_TRY(gemv_swiglu(&l.gate_up, in, s.hbuf, s.rids, S, s.rweights, &xr, st));

@@ -97,6 +97,9 @@ struct GemvParams {
     // y[row / 2 + {0,1}] = (ew[slot] *) silu(g) * u.
     int epi;
     const float* ew;
+    // Ring kernel: when set, CTA 0 also writes the transformed x here (the
+    // RMSNorm output that later kernels of a decode step read).
+    float* xout;
 };
 
 constexpr int kMaxXGroups = 64;
@@ -646,7 +649,8 @@ constexpr int kUPL = 2;  // 16-byte units per lane and row in a stage
 template <int TYPE>
 struct RingGeo {
     using C = Codec<TYPE>;
-    static constexpr int kSB = 64 * kUPL / C::kUnitsPerBlock;  // scale bytes per row and stage
+    // scale bytes per row and stage (BF16 rows carry none)
+    static constexpr int kSB = TYPE == Q3XK_BF16 ? 0 : 64 * kUPL / C::kUnitsPerBlock;
     static constexpr int kSPieces = kSB / 16;                   // 16-byte scale copies per row
     static constexpr int kQBytes = kRows * kUPL * 512;          // quants of a stage
     static constexpr int kStage = kQBytes + kRows * kSB;
@@ -654,7 +658,8 @@ struct RingGeo {
     // float4 slot of chunk j of unit u in the x area (the permutation depends
     // only on u mod 8, i.e. on the lane)
     __device__ static int xslot(int u, int j) {
-        return C::kChunks == 4 ? u * 4 + (j ^ ((u >> 1) & 3)) : u * 8 + (j ^ (u & 7));
+        return C::kChunks == 2 ? u * 2 + (j ^ ((u >> 2) & 1))
+             : C::kChunks == 4 ? u * 4 + (j ^ ((u >> 1) & 3)) : u * 8 + (j ^ (u & 7));
     }
 };
 
@@ -752,9 +757,13 @@ __device__ __forceinline__ void ring_main(const GemvParams& p, RingIssue<TYPE, R
 #pragma unroll
                 for (int j = 0; j < kRows; ++j) {
                     const uint4 qv = *reinterpret_cast<const uint4*>(st + (j * kUPL + h) * 512 + lane * 16);
-                    const float d = f16_bits_to_float(
-                        *reinterpret_cast<const uint16_t*>(st + G::kQBytes + j * G::kSB + sidx * 2));
-                    acc[j] = fmaf(d, C::template dot<FAST>(&qv, xr, gu), acc[j]);
+                    if (TYPE == Q3XK_BF16) {
+                        acc[j] += C::template dot<FAST>(&qv, xr, gu);
+                    } else {
+                        const float d = f16_bits_to_float(
+                            *reinterpret_cast<const uint16_t*>(st + G::kQBytes + j * G::kSB + sidx * 2));
+                        acc[j] = fmaf(d, C::template dot<FAST>(&qv, xr, gu), acc[j]);
+                    }
                 }
             }
         }
@@ -850,11 +859,24 @@ __global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvPara
         }
     };
 
-    // Prescale x per unit (as the register kernel does).
+    // Prescale x per unit (as the register kernel does); BF16 rows use x as it
+    // is.  CTA 0 also hands the transformed x to later kernels (p.xout).
     int slow = 0;
     for (int u = tid; u < p.units; u += RW * 32) {
         float v[C::kCols];
         load_unit(u, v);
+        if (p.xout && blockIdx.x == 0) {
+#pragma unroll
+            for (int i = 0; i < C::kCols / 4; ++i)
+                reinterpret_cast<float4*>(p.xout + (int64_t)u * C::kCols)[i] =
+                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+        if (TYPE == Q3XK_BF16) {
+#pragma unroll
+            for (int j = 0; j < C::kChunks; ++j)
+                xs4[G::xslot(u, j)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            continue;
+        }
         uint32_t emax = 0;
         float sum = 0.f;
 #pragma unroll
@@ -1034,10 +1056,11 @@ int launch_ring_family(const GemvParams& p, cudaStream_t s) {
 
 template <int TYPE, int MODE>
 int launch(GemvParams p, cudaStream_t s) {
-    if (TYPE != Q3XK_BF16 && MODE == kPlain && (!p.xform || p.xform == Q3XK_XFORM_RMS) && g_gemv_family != 1) {
-        const int st = launch_ring_family<TYPE == Q3XK_BF16 ? Q3XK_Q8_0 : TYPE>(p, s);
+    if (MODE == kPlain && (!p.xform || p.xform == Q3XK_XFORM_RMS) && g_gemv_family != 1) {
+        const int st = launch_ring_family<TYPE>(p, s);
         if (st != Q3XK_EUNSUPPORTED) return st;
     }
+    if (p.xout) return Q3XK_EUNSUPPORTED;  // the normalised-x output is the ring kernel's
     const size_t smem = smem_bytes<TYPE>(p);
     if (smem > 200 * 1024) return Q3XK_EUNSUPPORTED;
     if (p.xform) return launch_xf<TYPE, MODE, true, false>(p, smem, s);
@@ -1126,6 +1149,26 @@ int gemv_impl(const q3xk_matrix* m, const uint8_t* base, const float* x, float* 
 }
 
 }  // namespace
+
+int gemv_rms_out(const q3xk_matrix* m, const float* x, const float* w1, float* y, float* xout, cudaStream_t s) {
+    int st = check_matrix(m);
+    if (st != Q3XK_OK || !x || !w1 || !y || !xout) return Q3XK_EINVAL;
+    if (((uintptr_t)m->data & 15) || ((uintptr_t)x & 15) || ((uintptr_t)w1 & 15) || ((uintptr_t)xout & 15) ||
+        ((uintptr_t)y & 3))
+        return Q3XK_EALIGN;
+    GemvParams p = base_params(m, static_cast<const uint8_t*>(m->data), x, y, 0);
+    q3xk_xform xf{};
+    xf.kind = Q3XK_XFORM_RMS;
+    xf.w = w1;
+    st = set_xform(p, &xf, m->cols, kPlain);
+    if (st != Q3XK_OK) return st;
+    p.xout = xout;
+    p.ksplit = 1;
+    st = launch_type<kPlain>(m->type, p, s);
+    if (st != Q3XK_OK) return st;
+    count_launch();
+    return last_launch_status();
+}
 
 int gemv_swiglu(const q3xk_matrix* m, const float* x, float* y, const int* ids, int slots, const float* slot_w,
                 const q3xk_xform* xf, cudaStream_t s) {

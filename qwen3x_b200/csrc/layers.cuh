@@ -27,6 +27,11 @@ int repack_swiglu(const q3xk_matrix* m, const void* packed, int64_t src_rows, in
 // ids != nullptr (MoE gate|up of the selected experts; w per slot).
 int gemv_swiglu(const q3xk_matrix* w, const float* x, float* y, const int* ids, int slots, const float* slot_w,
                 const q3xk_xform* xf, cudaStream_t s);
+// y = W RMSNorm(x) (weights w1 = 1 + w') on the ring GEMV, which also writes
+// RMSNorm(x) to xout for the kernels after it (MoE decode: router logits, then
+// the experts read xout).  Q3XK_EUNSUPPORTED when the ring kernel cannot take
+// the shape (the caller then runs the norm as its own kernel).
+int gemv_rms_out(const q3xk_matrix* w, const float* x, const float* w1, float* y, float* xout, cudaStream_t s);
 
 // ---- dequant-GEMM internals (gemm.cu) --------------------------------------------
 // Expert-grouped tiles: X rows [xoff[e], xoff[e+1]) multiply expert e of a
