@@ -711,9 +711,15 @@ namespace {
         if (q3xb_st != Q3XK_OK) return q3xb_st; \
     } while (0)
 
+// Up to this many tokens a matrix is applied as one ring GEMV per token: the
+// GEMV streams 53.5 MB in 10.2 us, the few-token dequant-GEMM takes ~39 us at
+// any T <= 16 (its TMA weight stream and split-K reduction set the floor).
+constexpr int kGemvTokens = 3;
+
 int mm(State& s, const q3xk_matrix& w, const float* X, int T, float* Y, int accumulate) {
     if (T == 1) return q3xk_gemv(&w, X, Y, accumulate, s.stream);
-    if (w.type == Q3XK_BF16 || s.exact_prefill) {  // no BF16 GEMM / FP32-exact mode: one GEMV per token
+    // no BF16 GEMM / FP32-exact mode / few tokens: one GEMV per token
+    if (w.type == Q3XK_BF16 || s.exact_prefill || T <= kGemvTokens) {
         for (int t = 0; t < T; ++t)
             Q3XB_TRY(q3xk_gemv(&w, X + (size_t)t * w.cols, Y + (size_t)t * w.rows, accumulate, s.stream));
         return Q3XK_OK;
