@@ -140,3 +140,16 @@ def test_launchers_validate_before_launch():
     assert L.q3xk_gemv(ctypes.byref(bad), 0x2000, 0x3000, 0, None) == capi.EINVAL
     assert L.q3xk_repack(ctypes.byref(bad), 0x4000, None) == capi.EINVAL
     assert L.q3xk_launch_count() == before
+
+
+def test_gemv_family_switch_validates():
+    """q3xk_gemv_set_family takes 0 (automatic), 1 (register kernel), 2 and 3
+    (ring kernel, 16 / 24 warps) and rejects anything else; host-side only."""
+    handle = lib()
+    try:
+        for fam in (0, 1, 2, 3):
+            assert handle.q3xk_gemv_set_family(fam) == capi.OK
+        for bad in (-1, 4, 99):
+            assert handle.q3xk_gemv_set_family(bad) == capi.EINVAL
+    finally:
+        handle.q3xk_gemv_set_family(0)
