@@ -2,7 +2,12 @@
 //
 // Replaces the reference's one-CTA-per-row kernels with 1-byte loads and a
 // per-element FP16 decode (engine.cu:546-612).  Decode GEMV is HBM-bound
-// (~1.9 flop/B for Q8_0); the kernel is built around bytes in flight:
+// (~1.9 flop/B for Q8_0).  Two kernel families share the dequant arithmetic
+// below: the ring kernel (gemv_ring_kernel, further down), which stages the
+// weight stream through shared-memory rings filled by cp.async and is the
+// default for plain Q8_0 / Q4_0 / BF16 GEMVs, and the register kernel
+// (gemv_kernel), used for expert gathers and input transforms other than
+// RMSNorm.  The register kernel is built around bytes in flight:
 //
 //  * Every CTA owns a contiguous, balanced range of rows (+-1 row), so all
 //    SMs stream the same number of bytes.  Inside a CTA, thread t owns one
@@ -913,8 +918,9 @@ __global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvPara
     cp_async_wait<0>();
 }
 
-// Kernel family for plain Q8_0 / Q4_0 GEMVs: 0 = automatic, 1 = register
-// batches, 2 = ring (q3xk_gemv_set_family; tests run both on the same inputs).
+// Kernel family for plain GEMVs: 0 = automatic, 1 = register batches, 2 / 3 =
+// ring with 16 / 24 warps (q3xk_gemv_set_family; tests run every family on
+// the same inputs).
 int g_gemv_family = 0;
 constexpr size_t kRingSmemMax = 227 * 1024 - 256;  // dynamic; the kernel's static arrays take the rest
 
