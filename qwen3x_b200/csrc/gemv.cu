@@ -805,8 +805,8 @@ __device__ __forceinline__ void ring_main(const GemvParams& p, RingIssue<TYPE, R
     }
 }
 
-template <int TYPE, int RW, int S, int MINB, bool FULL>
-__global__ void __launch_bounds__(RW * 32, MINB) gemv_ring_kernel(const GemvParams p) {
+template <int TYPE, int RW, int S, bool FULL>
+__global__ void __launch_bounds__(RW * 32, 1) gemv_ring_kernel(const GemvParams p) {
     using C = Codec<TYPE>;
     using G = RingGeo<TYPE>;
     extern __shared__ __align__(128) uint8_t rsm[];
@@ -1002,17 +1002,15 @@ size_t ring_smem(const GemvParams& p, int rw, int stages) {
            (size_t)rw * stages * RingGeo<TYPE>::kStage;
 }
 
-// Ring-kernel launch: one CTA per SM (fewer for small matrices).  MINB = 2:
-// the CTA takes at most half an SM, so the next GEMV's CTA can be resident
-// beside it and fill its own ring while this one runs.
-template <int TYPE, int RW, int S, int MINB>
+// Ring-kernel launch: one CTA per SM (fewer for small matrices).
+template <int TYPE, int RW, int S>
 int launch_ring(const GemvParams& p, cudaStream_t s) {
     const size_t smem = ring_smem<TYPE>(p, RW, S);
     static bool configured = false;
     if (!configured) {
-        if (cudaFuncSetAttribute(gemv_ring_kernel<TYPE, RW, S, MINB, true>,
+        if (cudaFuncSetAttribute(gemv_ring_kernel<TYPE, RW, S, true>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemMax) != cudaSuccess ||
-            cudaFuncSetAttribute(gemv_ring_kernel<TYPE, RW, S, MINB, false>,
+            cudaFuncSetAttribute(gemv_ring_kernel<TYPE, RW, S, false>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemMax) != cudaSuccess)
             return Q3XK_ECUDA;
         configured = true;
@@ -1022,18 +1020,18 @@ int launch_ring(const GemvParams& p, cudaStream_t s) {
     const int64_t grid = groups < sms ? groups : sms;
     const cudaError_t e =
         p.units % (32 * kUPL) == 0
-            ? launch_pdl(gemv_ring_kernel<TYPE, RW, S, MINB, true>, dim3((unsigned)grid), dim3(RW * 32), smem, s, p)
-            : launch_pdl(gemv_ring_kernel<TYPE, RW, S, MINB, false>, dim3((unsigned)grid), dim3(RW * 32), smem, s, p);
+            ? launch_pdl(gemv_ring_kernel<TYPE, RW, S, true>, dim3((unsigned)grid), dim3(RW * 32), smem, s, p)
+            : launch_pdl(gemv_ring_kernel<TYPE, RW, S, false>, dim3((unsigned)grid), dim3(RW * 32), smem, s, p);
     return e == cudaSuccess ? Q3XK_OK : Q3XK_ECUDA;
 }
 
 // The deepest ring (stages per warp, up to SMAX) whose shared memory fits in
 // `cap` next to x; Q3XK_EUNSUPPORTED when even two stages do not fit.
-template <int TYPE, int RW, int SMAX, int MINB>
-int launch_ring_depth(const GemvParams& p, cudaStream_t s, size_t cap) {
-    if (SMAX >= 4 && ring_smem<TYPE>(p, RW, 4) <= cap) return launch_ring<TYPE, RW, 4, MINB>(p, s);
-    if (SMAX >= 3 && ring_smem<TYPE>(p, RW, 3) <= cap) return launch_ring<TYPE, RW, 3, MINB>(p, s);
-    if (ring_smem<TYPE>(p, RW, 2) <= cap) return launch_ring<TYPE, RW, 2, MINB>(p, s);
+template <int TYPE, int RW, int SMAX>
+int launch_ring_depth(const GemvParams& p, cudaStream_t s) {
+    if (SMAX >= 4 && ring_smem<TYPE>(p, RW, 4) <= kRingSmemMax) return launch_ring<TYPE, RW, 4>(p, s);
+    if (SMAX >= 3 && ring_smem<TYPE>(p, RW, 3) <= kRingSmemMax) return launch_ring<TYPE, RW, 3>(p, s);
+    if (ring_smem<TYPE>(p, RW, 2) <= kRingSmemMax) return launch_ring<TYPE, RW, 2>(p, s);
     return Q3XK_EUNSUPPORTED;
 }
 
@@ -1041,21 +1039,21 @@ template <int TYPE>
 int launch_ring_family(const GemvParams& p, cudaStream_t s) {
     switch (g_gemv_family) {
     case 3: {
-        const int st = launch_ring_depth<TYPE, 24, 2, 1>(p, s, kRingSmemMax);
+        const int st = launch_ring_depth<TYPE, 24, 2>(p, s);
         if (st != Q3XK_EUNSUPPORTED) return st;
-        return launch_ring_depth<TYPE, 20, 2, 1>(p, s, kRingSmemMax);
+        return launch_ring_depth<TYPE, 20, 2>(p, s);
     }
-    case 2: return launch_ring_depth<TYPE, 16, 3, 1>(p, s, kRingSmemMax);
+    case 2: return launch_ring_depth<TYPE, 16, 3>(p, s);
     default: {
         // Measured on B200 (us): Q8_0 12288x4096 10.1 with 24 warps vs 10.9
         // with 16 (one 4-row group per warp), 248320x4096 169 vs 165; Q4_0
         // 12288x4096 10.3 vs 9.5, 248320x2048 60.4 vs 54.3.
         const int64_t groups = (p.rows + kRows - 1) / kRows;
         if (TYPE == Q3XK_Q8_0 && groups <= 24 * (int64_t)sm_count_cached()) {
-            const int st = launch_ring_depth<TYPE, 24, 2, 1>(p, s, kRingSmemMax);
+            const int st = launch_ring_depth<TYPE, 24, 2>(p, s);
             if (st != Q3XK_EUNSUPPORTED) return st;
         }
-        return launch_ring_depth<TYPE, 16, 3, 1>(p, s, kRingSmemMax);
+        return launch_ring_depth<TYPE, 16, 3>(p, s);
     }
     }
 }
