@@ -34,7 +34,9 @@ struct State;
 Q3XK_API Model* model_create(const char* path, char* err, size_t errlen);
 Q3XK_API void model_destroy(Model* model);
 
-/* internal.h:19-30. */
+/* internal.h:19-30.  state_forward (and state_forward_batch) return once the
+ * step's device work has finished, as the reference's CUDA backend does
+ * (arch/cuda/engine.cu:2307); the C mirror below is stream-ordered instead. */
 Q3XK_API State* state_create(Model* model, int context_size);
 Q3XK_API void state_destroy(State* state);
 Q3XK_API void state_reset(State* state);

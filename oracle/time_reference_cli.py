@@ -2,10 +2,13 @@
 oracle/_ref/qwen3x, built by `make -C oracle cli` from the unmodified qwen3x
 sources) with their `--bench PREFILL DECODE` mode (main.cpp:1310-1377 of
 qwen3x) on the same seeded synthetic model.bin that bench.py's engine legs
-use (modelfile.write_model, seed 7).  Comparison measurement only: nothing of
-this backend runs here, and the product never calls it.
+use (modelfile.write_model, seed 7).  `--program b200` runs the same program
+objects linked against this repository's libq3xk.so (`make -C oracle
+b200cli`): the reference's CLI and Session runtime, unchanged, on this
+backend.  Comparison measurement only; the product never calls it.
 
     python oracle/time_reference_cli.py --config 9000 --program cuda --bench 4096 256
+    python oracle/time_reference_cli.py --config 9000 --program b200 --bench 4096 256
     python oracle/time_reference_cli.py --config 9000 --program cpu --bench 4 4
 
 Prints one JSON line with the program's own prefill and decode rates (wall
@@ -27,7 +30,8 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 sys.path.insert(0, str(ROOT))
 
-PROGRAMS = {"cuda": HERE / "_ref" / "qwen3x-cuda", "cpu": HERE / "_ref" / "qwen3x"}
+PROGRAMS = {"cuda": HERE / "_ref" / "qwen3x-cuda", "cpu": HERE / "_ref" / "qwen3x",
+            "b200": HERE / "_ref" / "qwen3x-b200"}
 LINE = re.compile(r"^(prefill|decode)\s+(\d+) tokens\s+([0-9.]+) s\s+([0-9.]+) tok/s")
 
 

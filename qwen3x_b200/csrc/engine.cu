@@ -1376,6 +1376,13 @@ int copy_logits_impl(const State* s, float* out) {
     return peer_status(s);
 }
 
+// Waits until the state's stream has drained; then the peer-wait status.
+int drain(const State* s) {
+    if (cudaSetDevice(s->device) != cudaSuccess) return Q3XK_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess) return Q3XK_ECUDA;
+    return peer_status(s);
+}
+
 // The reference's Q3X_ASSERT: report, then abort (internal.h:70-80).
 [[noreturn]] void fatal(const char* what, int status) {
     std::fprintf(stderr, "q3x_backend: %s failed: %s\n", what, q3xk_status_string(status));
@@ -1416,8 +1423,14 @@ void state_reset(State* state) {
     const int st = reset_impl(state);
     if (st != Q3XK_OK) fatal("state_reset", st);
 }
+// state_forward returns once the step's work is done, as the reference's CUDA
+// backend does (arch/cuda/engine.cu:2307, a stream synchronize at the end), so
+// callers that sequence or time calls by the wall clock (the runtime's
+// --bench, its logs) see the same behaviour.  The C mirror (q3xb_*) stays
+// stream-ordered; q3xb_state_synchronize waits there.
 void state_forward(Model* model, State* state, const int* tokens, int count, bool compute_logits) {
-    const int st = state_forward_impl(model, state, tokens, count, compute_logits);
+    int st = state_forward_impl(model, state, tokens, count, compute_logits);
+    if (st == Q3XK_OK) st = drain(state);
     if (st != Q3XK_OK) fatal("state_forward", st);
 }
 void state_checkpoint_save(State* state) {
@@ -1440,7 +1453,8 @@ void state_copy_logits(const State* state, float* output) {
     if (st != Q3XK_OK) fatal("state_copy_logits", st);
 }
 void state_forward_batch(Model* model, State* const* states, const int* tokens, int count) {
-    const int st = state_forward_batch_impl(model, const_cast<State**>(states), tokens, count);
+    int st = state_forward_batch_impl(model, const_cast<State**>(states), tokens, count);
+    for (int i = 0; st == Q3XK_OK && i < count; ++i) st = drain(states[i]);
     if (st != Q3XK_OK) fatal("state_forward_batch", st);
 }
 uint32_t model_id(const Model* model) { return model->config->id; }
