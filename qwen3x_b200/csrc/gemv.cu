@@ -628,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
         gemv_passes<TYPE, true, KS, MODE, DB>(p, rec, A, xs4, gg, part, seg_off, gb, ge, passes, row0, live);
 }
 
-// ---- Ring-staged GEMV (plain row addressing, Q8_0 / Q4_0) ------------------
+// ---- Ring-staged GEMV (plain row addressing, Q8_0 / Q4_0 / BF16) -----------
 //
 // The weight stream goes through a per-warp ring of shared-memory stages
 // filled with cp.async (16 bytes per copy, no registers held while in
@@ -646,9 +646,11 @@ __global__ void __launch_bounds__(kThreads, DB ? kDbBlocks : Q3XK_GEMV_MIN_BLOCK
 // rows' quants [row][half][lane] and then their scales (copied by the first
 // lanes, read after __syncwarp).  x is prescaled once per CTA into shared
 // memory, unit by unit, with the chunks of a unit permuted so that 8
-// consecutive units hit 8 different bank groups.  Arithmetic per unit is the
-// register kernel's (Codec::dot, one FMA of the unit's scale into the row
-// sum; the row sums meet in the same butterfly).  Deterministic.
+// consecutive units hit 8 different bank groups; an RMSNorm of x (the
+// decode norms) is applied while staging it, its statistics computed once
+// per CTA.  Arithmetic per unit is the register kernel's (Codec::dot, one FMA
+// of the unit's scale into the row sum -- BF16 rows have no scales; the row
+// sums meet in the same butterfly).  Deterministic.
 constexpr int kUPL = 2;  // 16-byte units per lane and row in a stage
 
 template <int TYPE>
