@@ -73,6 +73,17 @@ class Linear:
               "q3xk_repack")
 
 
+GEMV_AUTO, GEMV_REGISTER, GEMV_RING16, GEMV_RING24 = range(4)
+
+
+def set_gemv_family(family: int) -> None:
+    """Kernel family of the plain GEMVs, process-wide (q3xk_gemv_set_family):
+    GEMV_AUTO (default: the shared-memory ring kernel where it fits),
+    GEMV_REGISTER, GEMV_RING16 or GEMV_RING24.  For comparisons and tests;
+    every family meets the same parity bar."""
+    check(lib().q3xk_gemv_set_family(int(family)), "q3xk_gemv_set_family")
+
+
 def _gemv(linear: Linear, x, y, accumulate: int, stream) -> None:
     check(lib().q3xk_gemv(ctypes.byref(linear.m), ptr(x), ptr(y), accumulate, stream_ptr(stream)),
           "q3xk_gemv")

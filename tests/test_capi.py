@@ -153,3 +153,15 @@ def test_gemv_family_switch_validates():
             assert handle.q3xk_gemv_set_family(bad) == capi.EINVAL
     finally:
         handle.q3xk_gemv_set_family(0)
+
+
+def test_linear_set_gemv_family_wrapper():
+    from qwen3x_b200 import linear
+
+    try:
+        for fam in (linear.GEMV_AUTO, linear.GEMV_REGISTER, linear.GEMV_RING16, linear.GEMV_RING24):
+            linear.set_gemv_family(fam)
+        with pytest.raises(capi.Q3xkError):
+            linear.set_gemv_family(7)
+    finally:
+        linear.set_gemv_family(linear.GEMV_AUTO)
